@@ -1,0 +1,447 @@
+"""Benchmark of tilec_b200.ext.matrix_mul on B200 (one JSON line on rank 0).
+
+Workload (the config the headline metric is quoted on at 1/2/4/8
+GPUs): C = x1 @ x2 with M = 65536, K = 8192, N = 8192, fp32.  x1 ~ N(0,1) is split into
+M/world row blocks (rank r owns its block), x2 ~ N(0, 1/K) lives on rank 0 and is
+NCCL-broadcast each step; C stays row-sharded.  One step = broadcast of x2 (world > 1)
++ the local GEMM of every rank.  Total work is fixed as the GPU count grows (strong
+scaling).  Inputs (4.56 GB per step) are far larger than L2, so no flush is needed.
+
+  value    whole-job TFLOP/s = 2*M*N*K*steps / (max over ranks of the device time of
+           the timed steps), inputs resident in HBM.
+  e2e      same metric through the public API with host buffers: every step copies x1's
+           block and (rank 0) x2 from pinned host memory, runs the step, and copies C's
+           block back to pinned host memory.
+  roofline dominant kernel (the GEMM), CUDA-event time per launch vs the measured peak.
+  cpu_baseline  the reference test's oracle x1 @ x2 (torch fp32, CPU) on a bounded
+           sample of rows of the same workload, all host threads (rank 0, N = 1 only).
+
+--impl reference times that CPU oracle alone (the reference itself runs only on Apple
+GPUs through Metal, which this box does not have).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M5, K5, N5 = 65536, 8192, 8192
+METRIC = "matrix_mul fp32 TFLOP/s and % of roofline at 1/2/4/8 B200 vs CPU oracle"
+UNIT = "TFLOP/s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--variant", default="auto")
+    p.add_argument("--panels", type=int, default=2)
+    p.add_argument("--no-extra", action="store_true", help="skip the configs 1-3 single-GPU figures")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (debug only)")
+    p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end measurement (debug only)")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"], "bf16_sus": d["bf16_tflops_sustained"],
+                "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sus": 1400.0, "src": "fallback"}
+
+
+def variant_peak(variant, pk, sustained):
+    """(peak TFLOP/s of the pipe the variant uses, note)."""
+    bf16 = pk["bf16_sus"] if sustained else pk["bf16"]
+    tag = f"{pk['src']} bf16 {'sustained' if sustained else 'burst'} {bf16:.0f}"
+    if variant in ("3xtf32", "3xtf32_rawhi"):
+        return bf16 / 2 / 3, f"{tag} / 2 (tf32 rate) / 3 (MMAs per useful FLOP)"
+    if variant == "tf32":
+        return bf16 / 2, f"{tag} / 2 (tf32 rate)"
+    # SIMT FP32: 148 SMs x 128 FFMA lanes x 2 FLOP x max SM clock (nominal; no measured figure)
+    return 148 * 128 * 2 * 1965e6 / 1e12, "nominal FP32 SIMT peak at 1965 MHz (148 SMs x 128 lanes x 2)"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, indices):
+        self.indices = indices
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", ",".join(map(str, self.indices))],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def setup_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def cpu_baseline(target_s=8.0, seed=0):
+    """torch fp32 x1_sample @ x2 on all host threads; rows sized for ~target_s of work."""
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(seed)
+    x2 = torch.randn(K5, N5, generator=g) / K5 ** 0.5
+    rows = 64
+    x1 = torch.randn(rows, K5, generator=g)
+    oracle.mm_torch(x1, x2)  # warm-up
+    t0 = time.perf_counter()
+    oracle.mm_torch(x1, x2)
+    dt = time.perf_counter() - t0
+    rows = int(min(M5, max(64, rows * target_s / max(dt, 1e-6) / 2)))
+    x1 = torch.randn(rows, K5, generator=g)
+    times = []
+    deadline = time.perf_counter() + target_s
+    while True:
+        t0 = time.perf_counter()
+        oracle.mm_torch(x1, x2)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > deadline or len(times) >= 5:
+            break
+    t = statistics.median(times)
+    tflops = 2.0 * rows * N5 * K5 / t / 1e12
+    return {"value": round(tflops, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{rows} of {M5} rows of x1 ({rows}x{K5} @ {K5}x{N5}), median of {len(times)} runs, "
+                      f"torch {torch.__version__} CPU fp32 x1 @ x2 (tests/test_matmul.py:40 oracle)"}
+
+
+def reference_arm(args, world, rank):
+    """--impl reference: the CPU oracle, rank 0 only, each step a bounded row sample."""
+    if rank != 0:
+        return
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(1)
+    x2 = torch.randn(K5, N5, generator=g) / K5 ** 0.5
+    rows = 128
+    x1 = torch.randn(rows, K5, generator=g)
+    oracle.mm_torch(x1, x2)
+    t0 = time.perf_counter()
+    oracle.mm_torch(x1, x2)
+    dt = time.perf_counter() - t0
+    rows = int(min(M5, max(64, rows * 1.5 / max(dt, 1e-6))))  # ~1.5 s per step
+    x1 = torch.randn(rows, K5, generator=g)
+    for _ in range(args.warmup):
+        oracle.mm_torch(x1, x2)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.mm_torch(x1, x2)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = 2.0 * rows * N5 * K5 / dt / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config5 row sample: [{rows},{K5}] @ [{K5},{N5}] of [{M5},{K5}] @ [{K5},{N5}]",
+                   "M": M5, "K": K5, "N": N5, "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{rows} rows of x1 per step; torch {torch.__version__} CPU fp32 x1 @ x2 "
+                                   "(the reference test's oracle; the reference's Metal path is unavailable "
+                                   "on this box)"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def time_launches(fn, reps, warm=10):
+    """Mean CUDA-event time (ms) of fn() over reps back-to-back calls on the current stream."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def extra_configs(pk):
+    """Single-GPU figures for BASELINE configs 1-3 (inputs rotated over a pool larger than L2)."""
+    from tilec_b200 import ext
+    out = {}
+    l2_bytes = 126 * 2 ** 20
+    for name, (m, k, n, dist_) in (("config1_512x4096x64", (512, 4096, 64, "n")),
+                                   ("config2_2048^3", (2048, 2048, 2048, "n")),
+                                   ("config3_1000x3001x777", (1000, 3001, 777, "u"))):
+        per = 4 * (m * k + k * n + m * n)
+        copies = max(2, -(-3 * l2_bytes // per))
+        g = torch.Generator(device="cuda").manual_seed(3)
+        xs = []
+        for _ in range(copies):
+            if dist_ == "u":
+                a = torch.rand(m, k, device="cuda", generator=g) * 2 - 1
+                b = torch.rand(k, n, device="cuda", generator=g) * 2 - 1
+            else:
+                a = torch.randn(m, k, device="cuda", generator=g)
+                b = torch.randn(k, n, device="cuda", generator=g)
+            xs.append((a, b, torch.empty(m, n, device="cuda")))
+        variant, split = ext.plan(xs[0][0], xs[0][1])
+        i = [0]
+
+        def step():
+            a, b, c = xs[i[0] % copies]
+            i[0] += 1
+            ext._matrix_mul(a, b, out=c)
+        reps = max(20, min(400, int(2e11 / (2 * m * n * k))))
+        ms = time_launches(step, reps)
+        flops = 2.0 * m * n * k
+        tfl = flops / (ms * 1e-3) / 1e12
+        peak, note = variant_peak(variant, pk, sustained=False)
+        bw_bound = (flops / per) * pk["hbm_gbs"] / 1e3  # AI x HBM, TFLOP/s
+        roof = min(peak, bw_bound)
+        out[name] = {"variant": variant, "split_k": split, "ms": round(ms, 5), "tflops": round(tfl, 3),
+                     "gbs": round(per / (ms * 1e-3) / 1e9, 1), "roofline_tflops": round(roof, 2),
+                     "roofline_frac": round(tfl / roof, 4),
+                     "bound": "hbm" if bw_bound < peak else ("tensor" if "tf32" in variant else "fp32"),
+                     "peak_note": note, "l2": f"rotating {copies} input sets ({copies * per / 2**20:.0f} MiB > L2)",
+                     "timing": f"mean of {reps} back-to-back launches, CUDA events, incl. host launch path"}
+        del xs
+        torch.cuda.empty_cache()
+    return out
+
+
+def main():
+    args = parse()
+    world, rank, local = setup_dist()
+    if args.impl == "reference":
+        reference_arm(args, world, rank)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    from tilec_b200 import ext
+    from tilec_b200.dist import RowShardedMatmul, shard_rows
+
+    dev = torch.device("cuda", local if world > 1 else 0)
+    r0, r1 = shard_rows(M5, world, rank)
+    rows = r1 - r0
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x1 = torch.randn(rows, K5, device=dev, generator=g)
+    x2 = None
+    if rank == 0:
+        g0 = torch.Generator(device=dev).manual_seed(7)
+        x2 = torch.randn(K5, N5, device=dev, generator=g0) / K5 ** 0.5
+    out = torch.empty(rows, N5, device=dev)
+    if args.variant != "auto":
+        os.environ["TILEC_MM_VARIANT"] = args.variant
+    op = RowShardedMatmul(K5, N5, panels=args.panels, device=dev)
+    panel_w = op.bounds[0][1] - op.bounds[0][0]
+    variant, split = ext.plan(x1, x2 if world == 1 else torch.empty(K5, panel_w, device=dev))
+
+    gemm_events = []
+
+    def timed_gemm(p, fn):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        gemm_events.append((s, e))
+
+    def step(hook=None):
+        op(x1, x2, out=out, on_gemm=hook)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    clocks = ClockSampler(list(range(world)) if world > 1 else [dev.index]) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for _ in range(args.steps):
+        step(timed_gemm)
+    t_end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+
+    ms_total = t_start.elapsed_time(t_end)
+    gemm_ms = [s.elapsed_time(e) for s, e in gemm_events]
+    t = torch.tensor([ms_total, statistics.mean(gemm_ms)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total, gemm_ms_max = t.tolist()
+    ms_step = ms_total / args.steps
+    flops_step = 2.0 * M5 * N5 * K5
+    value = flops_step * args.steps / (ms_total * 1e-3) / 1e12
+
+    pk = peaks()
+    peak, peak_note = variant_peak(variant, pk, sustained=True)
+    flops_launch = 2.0 * rows * panel_w * K5
+    bytes_launch = 4.0 * (rows * K5 + K5 * panel_w + rows * panel_w)
+    achieved = flops_launch / (gemm_ms_max * 1e-3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            tr = json.load(f)
+        key = f"{variant}:{rows}x{K5}x{panel_w}"
+        if key in tr:
+            traffic = tr[key]
+
+    # ---------------------------------------------------------------- end to end
+    e2e = None
+    if not args.no_e2e:
+        h_x1 = torch.empty(rows, K5, dtype=torch.float32, pin_memory=True)
+        h_x1.copy_(x1)
+        h_out = torch.empty(rows, N5, dtype=torch.float32, pin_memory=True)
+        h_x2 = None
+        if rank == 0:
+            h_x2 = torch.empty(K5, N5, dtype=torch.float32, pin_memory=True)
+            h_x2.copy_(x2)
+        d_x1 = torch.empty_like(x1)
+        d_x2 = torch.empty(K5, N5, device=dev) if rank == 0 else None
+        del x1
+        torch.cuda.empty_cache()
+
+        def e2e_step():
+            d_x1.copy_(h_x1, non_blocking=True)
+            if rank == 0:
+                d_x2.copy_(h_x2, non_blocking=True)
+            op(d_x1, d_x2, out=out)
+            h_out.copy_(out, non_blocking=True)
+
+        for _ in range(max(1, min(args.warmup, 2))):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(2, min(args.steps, 5))
+        s.record()
+        for _ in range(n_e2e):
+            e2e_step()
+        e.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([s.elapsed_time(e)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = te.item() / n_e2e
+        h2d = 4 * rows * K5 + (4 * K5 * N5 if rank == 0 else 0)
+        e2e = {"value": round(flops_step / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT,
+               "h2d_bytes_per_step": int(4 * M5 * K5 + 4 * K5 * N5), "d2h_bytes_per_step": int(4 * M5 * N5),
+               "ms_per_step": round(e2e_ms, 3), "steps": n_e2e,
+               "path": "pinned host x1 block (+x2 on rank 0) -> device, RowShardedMatmul (tilec_b200.ext), "
+                       "C block -> pinned host; rank-local h2d this rank: %d bytes" % h2d}
+
+    extra = None
+    cpu = None
+    if rank == 0 and world == 1:
+        if not args.no_extra:
+            extra = extra_configs(pk)
+        if not args.no_cpu:
+            cpu = cpu_baseline()
+
+    if rank == 0:
+        launches_per_step = op.gemm_launches_per_call * (1 + (1 if split > 1 else 0))
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 (3xTF32 split on tcgen05: fp32-class accuracy, relFrob <= 1e-5)"
+            if variant.startswith("3xtf32") else ("tf32" if variant == "tf32" else "f32"),
+            "data": "synthetic",
+            "config": {"workload": f"config5 row-sharded GEMM [{M5},{K5}] @ [{K5},{N5}] fp32, x2 broadcast "
+                                   f"from rank 0 in {len(op.bounds)} column panel(s)",
+                       "M": M5, "K": K5, "N": N5, "rows_per_rank": rows, "variant": variant, "split_k": split,
+                       "parallelism": f"row-shard x{world}" + (" + NCCL broadcast of x2" if world > 1 else ""),
+                       "l2": "inputs larger than L2 (4.56 GB per step)"},
+            "roofline": {"bound": "tensor" if "tf32" in variant else "fp32", "achieved": round(achieved, 2),
+                         "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "algorithmic_bytes": int(bytes_launch),
+                         "kernel": f"tc_gemm ({variant}) on [{rows},{K5}] @ [{K5},{panel_w}]",
+                         "launch_ms": round(gemm_ms_max, 4), "peak_note": peak_note + " (of measured)"
+                         if pk["src"] == "measured" else peak_note},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(launches_per_step * args.steps),
+            "clocks": clk,
+        }
+        if extra:
+            line["configs_1_3"] = extra
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,123 @@
+/*
+ * tilec_mm.h -- C ABI of the B200 (sm_100a) fp32 GEMM library behind
+ * tilec_b200.ext.matrix_mul.
+ *
+ * Replaces, for the one op the reference ships, the path
+ *   tilec/ext.py:54-63  _matrix_mul_tiled(x1, x2)  (host: shape check, contiguous, new_empty, launch)
+ *   tilec/ext.py:13-24  _matmul_tiled[grid](...)   (device: masked 64x64x16 tiled C = A.B)
+ *   tilec/jit.py:88-105 _launch(...)               (kernel launch through torch.mps.compile_shader)
+ * with plain pointers, sizes and a stream.  No torch type appears here; any FFI
+ * (ctypes, cgo, JNI, N-API) can bind these symbols.
+ *
+ * Semantics (all entry points):
+ *   C[m, n] = sum_k A[m, k] * B[k, n] for 0 <= m < M, 0 <= n < N, fp32 in, fp32 out,
+ *   A row-major with row stride lda, B row-major with row stride ldb, C row-major
+ *   with row stride ldc (strides in elements).  Elements of A/B outside [M,K]/[K,N]
+ *   are never read (the reference reads them as 0.0, tilec/ext.py:21-22); elements
+ *   of C outside [M,N] are never written (tilec/ext.py:24).  K == 0 writes zeros.
+ *   M == 0 or N == 0 is a no-op.
+ *
+ * Calls are asynchronous and stream-ordered on `stream` (a cudaStream_t, NULL = the
+ * legacy default stream).  They allocate no memory, never synchronise the device and
+ * never throw; errors come back as a tilec_status code.  Kernels never trap: a fault
+ * detected on the device is recorded in a device status word that
+ * tilec_mm_device_status() reads.
+ */
+#ifndef TILEC_MM_H
+#define TILEC_MM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TILEC_MM_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TILEC_API __attribute__((visibility("default")))
+#else
+#define TILEC_API
+#endif
+
+/* Return codes.  0 is success; tilec_strerror() names every code. */
+typedef enum tilec_status {
+  TILEC_OK = 0,
+  TILEC_ERR_BAD_ARG = 1,      /* negative size, null pointer with non-empty operand, ld < row length */
+  TILEC_ERR_MISALIGNED = 2,   /* a variant that needs 16-byte aligned rows was forced on unaligned operands */
+  TILEC_ERR_NO_DEVICE = 3,    /* no CUDA device, or the device is not sm_100 */
+  TILEC_ERR_LAUNCH = 4,       /* a kernel launch failed (cudaGetLastError after the launch) */
+  TILEC_ERR_DEVICE = 5,       /* a device-side check failed (see tilec_mm_device_status) */
+  TILEC_ERR_WORKSPACE = 6,    /* workspace is NULL or smaller than tilec_mm_workspace_bytes() */
+  TILEC_ERR_UNSUPPORTED = 7,  /* variant/size combination not built (e.g. K > 2^31 on the TMA path) */
+  TILEC_ERR_TOO_LARGE = 8     /* request exceeds a fixed limit of the entry point */
+} tilec_status;
+
+/* Kernel variants.  AUTO lets the library choose (tilec_mm_plan shows the choice). */
+typedef enum tilec_mm_variant {
+  TILEC_MM_AUTO = 0,
+  TILEC_MM_SIMT = 1,      /* fp32 FFMA, exact fp32 products; any strides / alignment */
+  TILEC_MM_SPLITK = 2,    /* SIMT with K split over CTAs + ordered reduction (skinny / small-M shapes) */
+  TILEC_MM_TF32 = 3,      /* tcgen05 kind::tf32, TMEM accumulators; rows must be 16-byte aligned */
+  TILEC_MM_3XTF32 = 4,    /* tcgen05 kind::tf32 with hi/lo operand split (3 MMAs): fp32-class accuracy */
+  TILEC_MM_3XTF32_RAWHI = 5 /* as 3XTF32, but hi(x) is the tensor core's own tf32 reading of x (its low 13
+                               mantissa bits ignored) instead of an explicitly masked copy */
+} tilec_mm_variant;
+
+/* Per-call configuration.  Zero-initialise, then set what you need. */
+typedef struct tilec_mm_cfg {
+  int32_t variant;     /* tilec_mm_variant */
+  int32_t split_k;     /* SPLITK / tensor variants: number of K slices (0 = choose) */
+  int32_t reserved[6]; /* must be zero */
+} tilec_mm_cfg;
+
+/* C = A . B  (see the semantics block above).
+ * cfg may be NULL (= AUTO).  workspace/ws_bytes: scratch for split-K partial sums;
+ * may be NULL/0 when tilec_mm_workspace_bytes() returns 0 for the same arguments.
+ * Replaces tilec/ext.py:54-63 + tilec/jit.py:88-105 (one launch per call). */
+TILEC_API int tilec_mm_f32(const float* A, const float* B, float* C,
+                 int64_t M, int64_t N, int64_t K,
+                 int64_t lda, int64_t ldb, int64_t ldc,
+                 const tilec_mm_cfg* cfg,
+                 void* workspace, size_t ws_bytes,
+                 void* stream);
+
+/* Bytes of workspace tilec_mm_f32 needs for these arguments (0 when none).
+ * Pointer alignment affects the AUTO choice, so pass the same pointers (or NULL
+ * to assume 16-byte aligned operands). */
+TILEC_API size_t tilec_mm_workspace_bytes(const float* A, const float* B, const float* C,
+                                int64_t M, int64_t N, int64_t K,
+                                int64_t lda, int64_t ldb, int64_t ldc,
+                                const tilec_mm_cfg* cfg);
+
+/* Resolve AUTO (and split_k == 0) to the concrete variant/split tilec_mm_f32 would
+ * launch, without launching.  Writes the resolved config to *out.
+ * Counterpart of the reference's per-shape config pick (tilec/tune.py:143-151). */
+TILEC_API int tilec_mm_plan(const float* A, const float* B, const float* C,
+                  int64_t M, int64_t N, int64_t K,
+                  int64_t lda, int64_t ldb, int64_t ldc,
+                  const tilec_mm_cfg* cfg, tilec_mm_cfg* out);
+
+/* Install a per-shape selection table used by AUTO.  Each row is
+ * {log2M_lo, log2M_hi, log2N_lo, log2N_hi, log2K_lo, log2K_hi, variant, split_k}
+ * (int32, bounds inclusive-exclusive, first matching row wins).  rows == 0 clears
+ * the table (built-in rules apply).  Not thread-safe against concurrent calls. */
+TILEC_API int tilec_mm_set_table(const int32_t* rows, int32_t nrows);
+
+/* Read and clear the device status word of the current device (0 = clean).
+ * Synchronises `stream`. */
+TILEC_API int tilec_mm_device_status(void* stream, int32_t* status_out);
+
+/* Text for a tilec_status code (static storage). */
+TILEC_API const char* tilec_strerror(int code);
+
+/* ABI version (TILEC_MM_ABI_VERSION) and the sm arch the library was built for. */
+TILEC_API int tilec_mm_abi_version(void);
+TILEC_API int tilec_mm_built_arch(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TILEC_MM_H */

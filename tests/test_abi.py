@@ -1,0 +1,84 @@
+"""The C-ABI library: it builds for sm_100a, loads, and exports what include/tilec_mm.h declares.
+
+No compute call runs here (this host has no GPU): only symbol, string and error-path
+checks.
+"""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+import torch
+
+from tilec_b200 import _native, build
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "tilec_mm.h")
+
+
+def _header():
+    with open(HEADER) as f:
+        return f.read()
+
+
+def _declared_functions():
+    return re.findall(r"TILEC_API\s+[\w\s\*]+?\b(tilec_\w+)\s*\(", _header())
+
+
+def test_header_declares_the_binding_list():
+    assert sorted(_declared_functions()) == sorted(_native.EXPORTS)
+
+
+def test_library_builds_and_exports_every_declared_symbol():
+    path = build.build()
+    out = subprocess.run(["nm", "-D", "--defined-only", path], check=True, capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\bT (tilec_\w+)", out))
+    assert set(_declared_functions()) <= exported
+    # Nothing else leaks: only the ABI is visible.
+    assert exported == set(_declared_functions())
+    lib = _native.load()
+    for name in _declared_functions():
+        assert getattr(lib, name) is not None
+
+
+def test_abi_constants_match_header():
+    h = _header()
+    lib = _native.load()
+    ver = int(re.search(r"#define TILEC_MM_ABI_VERSION (\d+)", h).group(1))
+    assert lib.tilec_mm_abi_version() == ver
+    assert lib.tilec_mm_built_arch() == 100
+    for name, code in re.findall(r"(TILEC_(?:OK|ERR_\w+))\s*=\s*(\d+)", h):
+        assert _native.STATUS_NAMES[int(code)] == name
+    for name, code in re.findall(r"TILEC_MM_(AUTO|SIMT|SPLITK|TF32|3XTF32|3XTF32_RAWHI)\s*=\s*(\d+)", h):
+        assert _native.VARIANTS[name.lower()] == int(code)
+    assert ctypes.sizeof(_native.MMConfig) == 32
+
+
+def test_strerror_names_every_code():
+    for code in _native.STATUS_NAMES:
+        assert _native.strerror(code)
+    assert "unknown" in _native.strerror(99)
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device error path")
+def test_no_device_is_an_error_not_a_fallback():
+    lib = _native.load()
+    cfg = _native.make_cfg("auto")
+    res = _native.MMConfig()
+    rc = lib.tilec_mm_plan(16, 16, 16, 4, 4, 4, 4, 4, 4, ctypes.byref(cfg), ctypes.byref(res))
+    assert rc == 3  # TILEC_ERR_NO_DEVICE
+    rc = lib.tilec_mm_f32(16, 16, 16, 4, 4, 4, 4, 4, 4, None, None, 0, None)
+    assert rc == 3
+
+
+def test_bad_arguments_rejected_before_device():
+    lib = _native.load()
+    # negative size / too-small leading dimension / null output
+    assert lib.tilec_mm_f32(16, 16, 16, -1, 4, 4, 4, 4, 4, None, None, 0, None) == 1
+    assert lib.tilec_mm_f32(16, 16, 16, 4, 4, 4, 3, 4, 4, None, None, 0, None) == 1
+    assert lib.tilec_mm_f32(16, 16, None, 4, 4, 4, 4, 4, 4, None, None, 0, None) == 1
+    # empty problems are a no-op even without a device
+    assert lib.tilec_mm_f32(None, None, None, 0, 4, 4, 4, 4, 4, None, None, 0, None) == 0
+    rows = (ctypes.c_int32 * 8)(0, 1, 0, 1, 0, 1, 9, 0)
+    assert lib.tilec_mm_set_table(rows, 1) == 1  # unknown variant
+    assert lib.tilec_mm_set_table(None, 0) == 0

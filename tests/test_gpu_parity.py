@@ -1,0 +1,207 @@
+"""Parity of every kernel variant against the CPU oracle, on a B200 (run with -m gpu).
+
+Gates (relative Frobenius error against the oracle, fp32 in / fp32 out):
+  SIMT, SPLITK, 3XTF32 : <= 1e-5        TF32 : <= 5e-3
+plus the reference test's own check, np.testing.assert_allclose(rtol=1e-3, atol=1e-2)
+against ``x1 @ x2`` (tests/test_matmul.py:40), on the reference test's shapes
+(tests/test_matmul.py:33).  Exactly representable inputs must match bit for bit.
+Large configs are checked through sampled rows against an fp64 product and a
+row-checksum identity C.1 = x1.(x2.1) evaluated in fp64.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import gen
+import oracle
+from tilec_b200 import TilecError, _native, ext
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+TOL = {"simt": 1e-5, "splitk": 1e-5, "3xtf32": 1e-5, "3xtf32_rawhi": 1e-5, "tf32": 5e-3, "auto": 1e-5}
+TENSOR = ("tf32", "3xtf32", "3xtf32_rawhi")
+ALL = ("auto", "simt", "splitk", "tf32", "3xtf32", "3xtf32_rawhi")
+
+
+def _aligned(k, n):
+    return k % 4 == 0 and n % 4 == 0
+
+
+def _run(x1, x2, variant, split_k=0):
+    d1 = torch.as_tensor(x1).to(DEV)
+    d2 = torch.as_tensor(x2).to(DEV)
+    return ext._matrix_mul(d1, d2, variant=variant, split_k=split_k).cpu().numpy()
+
+
+def _status_clean():
+    st = ctypes.c_int32(-1)
+    _native.check(_native.load().tilec_mm_device_status(None, ctypes.byref(st)), "device_status")
+    return st.value == 0
+
+
+@pytest.mark.parametrize("variant", ALL)
+@pytest.mark.parametrize("shape", gen.REF_TEST_SHAPES)
+def test_reference_test_shapes(shape, variant):
+    m, k, n = shape
+    if variant in TENSOR and not _aligned(k, n):
+        pytest.skip("tensor-core variants need 16-byte aligned rows")
+    x1, x2 = gen.randn_inputs(m, k, n, 42)
+    got = _run(x1, x2, variant)
+    np.testing.assert_allclose(got, oracle.mm_torch(x1, x2), rtol=1e-3, atol=1e-2)
+    assert oracle.rel_frob(got, oracle.mm_tiled(x1, x2)) <= TOL[variant]
+
+
+GOLDEN = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "golden.npz"))
+GOLDEN_CASES = sorted(k[:-7] for k in GOLDEN.files if k.endswith("_digest"))
+
+
+@pytest.mark.parametrize("variant", ALL)
+@pytest.mark.parametrize("base", GOLDEN_CASES)
+def test_golden_vectors(base, variant):
+    tag, shape, s = base.split("_")
+    m, k, n = map(int, shape.split("x"))
+    if variant in TENSOR and not _aligned(k, n):
+        pytest.skip("tensor-core variants need 16-byte aligned rows")
+    x1, x2 = (gen.randn_inputs if tag == "randn" else gen.exact_inputs)(m, k, n, int(s[1:]))
+    assert gen.digest(x1, x2) == str(GOLDEN[base + "_digest"])
+    got = _run(x1, x2, variant)
+    if base + "_c" in GOLDEN.files:
+        ref = GOLDEN[base + "_c"]
+    else:
+        got, ref = got[GOLDEN[base + "_rows"]], GOLDEN[base + "_c_rows"]
+    if tag == "exact":
+        assert np.array_equal(got, ref), f"max diff {np.abs(got - ref).max()}"
+    else:
+        assert oracle.rel_frob(got, ref) <= TOL[variant]
+
+
+def _config_inputs(cfg, seed):
+    m, k, n, dist = cfg
+    g = torch.Generator().manual_seed(seed)
+    if dist == "uniform":
+        return torch.rand(m, k, generator=g) * 2 - 1, torch.rand(k, n, generator=g) * 2 - 1
+    return torch.randn(m, k, generator=g), torch.randn(k, n, generator=g)
+
+
+@pytest.mark.parametrize("variant", ALL)
+@pytest.mark.parametrize("cfg", [gen.CONFIG1, gen.CONFIG2, gen.CONFIG3], ids=["config1", "config2", "config3"])
+def test_baseline_configs(cfg, variant):
+    m, k, n, _ = cfg
+    if variant in TENSOR and not _aligned(k, n):
+        pytest.skip("config 3 rows are not 16-byte aligned")
+    x1, x2 = _config_inputs(cfg, 11)
+    ref = oracle.mm_tiled(x1.numpy(), x2.numpy()) if m * n * k <= 2 ** 31 else oracle.mm_torch(x1, x2)
+    got = _run(x1, x2, variant)
+    assert np.isfinite(got).all()
+    assert oracle.rel_frob(got, ref) <= TOL[variant]
+
+
+def _sampled_check(x1, x2, got, tol, nrows=8):
+    """Sampled rows vs fp64 and the row-checksum identity, both in fp64 on the CPU."""
+    m = x1.shape[0]
+    rows = torch.unique(torch.linspace(0, m - 1, min(nrows, m)).round().long())
+    ref_rows = x1[rows].double() @ x2.double()
+    err_rows = oracle.rel_frob(got[rows].numpy(), ref_rows.numpy())
+    ref_rs = x1.double() @ x2.double().sum(1)
+    err_rs = oracle.rel_frob(got.double().sum(1).numpy(), ref_rs.numpy())
+    assert err_rows <= tol, f"sampled rows relFrob {err_rows:.3e}"
+    assert err_rs <= max(tol, 1e-5), f"row checksum relFrob {err_rs:.3e}"
+
+
+@pytest.mark.parametrize("shape", gen.config4_shapes(), ids=lambda s: "x".join(map(str, s)))
+def test_config4_sweep(shape):
+    m, k, n = shape
+    g = torch.Generator().manual_seed(m * 7919 + k * 31 + n)
+    x1 = torch.randn(m, k, generator=g)
+    x2 = torch.randn(k, n, generator=g)
+    d1, d2 = x1.to(DEV), x2.to(DEV)
+    variants = ["auto", "simt", "splitk"] + (["3xtf32", "tf32"] if _aligned(k, n) else [])
+    for v in variants:
+        got = ext._matrix_mul(d1, d2, variant=v).cpu()
+        _sampled_check(x1, x2, got, TOL[v])
+
+
+def test_config5_single_gpu():
+    m, k, n = 65536, 8192, 8192
+    g = torch.Generator(device=DEV).manual_seed(5)
+    d1 = torch.randn(m, k, device=DEV, generator=g)
+    d2 = torch.randn(k, n, device=DEV, generator=g) / k ** 0.5
+    got = ext.matrix_mul(d1, d2)
+    rows = torch.unique(torch.linspace(0, m - 1, 16).round().long()).to(DEV)
+    ref_rows = (d1[rows].double() @ d2.double()).cpu()
+    assert oracle.rel_frob(got[rows].cpu().numpy(), ref_rows.numpy()) <= 1e-5
+    ref_rs = (d1.double() @ d2.double().sum(1)).cpu()
+    assert oracle.rel_frob(got.double().sum(1).cpu().numpy(), ref_rs.numpy()) <= 1e-5
+    assert _status_clean()
+
+
+@pytest.mark.parametrize("variant", ("splitk", "tf32", "3xtf32"))
+@pytest.mark.parametrize("split_k", (1, 2, 3, 7, 16, 64))
+def test_forced_split_k(variant, split_k):
+    x1, x2 = _config_inputs(gen.CONFIG1, 3)
+    got = _run(x1, x2, variant, split_k)
+    assert oracle.rel_frob(got, oracle.mm_tiled(x1.numpy(), x2.numpy())) <= TOL[variant]
+
+
+@pytest.mark.parametrize("variant", ALL)
+def test_edge_sizes(variant):
+    for (m, k, n) in [(1, 4, 4), (4, 0, 8), (0, 8, 4), (8, 8, 0), (129, 4, 260), (3, 4100, 5 * 4), (300, 8, 1000)]:
+        if variant in TENSOR and not _aligned(k, n):
+            continue
+        x1, x2 = gen.exact_inputs(m, k, n, 5)
+        got = _run(x1, x2, variant)
+        assert got.shape == (m, n)
+        assert np.array_equal(got, oracle.mm_f64(x1, x2).astype(np.float32))
+
+
+@pytest.mark.parametrize("variant", ALL)
+def test_strided_views_and_guard_band(variant):
+    g = torch.Generator().manual_seed(9)
+    big1 = torch.randn(300, 520, generator=g).to(DEV)
+    big2 = torch.randn(520, 700, generator=g).to(DEV)
+    x1 = big1[10:290, 8:520]     # row view: ld = 520, no copy
+    x2 = big2[:512, 4:644]       # row view: ld = 700
+    if variant in TENSOR:
+        assert x1.data_ptr() % 16 == 0 and x2.data_ptr() % 16 == 0
+    buf = torch.full((290, 700), float("nan"), device=DEV)
+    out = buf[5:285, 30:670]     # guard band around the output, ldc = 700
+    ext._matrix_mul(x1, x2, variant=variant, out=out)
+    ref = oracle.mm_tiled(x1.cpu().numpy(), x2.cpu().numpy())
+    assert oracle.rel_frob(out.cpu().numpy(), ref) <= TOL[variant]
+    b = buf.cpu()
+    inside = torch.zeros_like(b, dtype=torch.bool)
+    inside[5:285, 30:670] = True
+    assert torch.isnan(b[~inside]).all(), "a store landed outside [M, N]"
+    # transposed operand: copied like tilec/ext.py:59-60
+    t = ext._matrix_mul(big2[:512, :300].t(), big2[:512, :644], variant="simt").cpu().numpy()
+    assert oracle.rel_frob(t, oracle.mm_tiled(big2[:512, :300].t().contiguous().cpu().numpy(),
+                                              big2[:512, :644].cpu().numpy())) <= 1e-5
+
+
+@pytest.mark.parametrize("variant", ALL)
+def test_deterministic(variant):
+    x1, x2 = _config_inputs(gen.CONFIG1, 4)
+    d1, d2 = x1.to(DEV), x2.to(DEV)
+    a = ext._matrix_mul(d1, d2, variant=variant)
+    b = ext._matrix_mul(d1, d2, variant=variant)
+    assert torch.equal(a, b)
+
+
+def test_misaligned_tensor_variant_is_an_error():
+    x1 = torch.randn(64, 30, device=DEV)
+    x2 = torch.randn(30, 64, device=DEV)
+    with pytest.raises(TilecError, match="MISALIGNED"):
+        ext._matrix_mul(x1, x2, variant="3xtf32")
+    # AUTO picks a kernel that handles it
+    got = ext.matrix_mul(x1, x2).cpu().numpy()
+    assert oracle.rel_frob(got, oracle.mm_tiled(x1.cpu().numpy(), x2.cpu().numpy())) <= 1e-5
+
+
+def test_plan_and_status():
+    x1 = torch.randn(2048, 2048, device=DEV)
+    v, s = ext.plan(x1, x1)
+    assert v in ("simt", "splitk", "tf32", "3xtf32", "3xtf32_rawhi") and s >= 1
+    assert _status_clean()

@@ -1,0 +1,103 @@
+"""ctypes binding of the C ABI in include/tilec_mm.h (libtilec_mm.so, built in-tree).
+
+This is the binding a maintainer of the reference would add on the Python side; the
+same symbols bind from any other FFI.  There is no fallback: if the library is missing
+or cannot load, every call raises.
+"""
+import ctypes
+import os
+import threading
+
+from . import build as _build
+
+TILEC_OK = 0
+STATUS_NAMES = {
+    0: "TILEC_OK", 1: "TILEC_ERR_BAD_ARG", 2: "TILEC_ERR_MISALIGNED", 3: "TILEC_ERR_NO_DEVICE",
+    4: "TILEC_ERR_LAUNCH", 5: "TILEC_ERR_DEVICE", 6: "TILEC_ERR_WORKSPACE", 7: "TILEC_ERR_UNSUPPORTED",
+    8: "TILEC_ERR_TOO_LARGE",
+}
+
+VARIANTS = {"auto": 0, "simt": 1, "splitk": 2, "tf32": 3, "3xtf32": 4, "3xtf32_rawhi": 5}
+VARIANT_NAMES = {v: k for k, v in VARIANTS.items()}
+
+# Every function the header declares (tests check the library exports exactly these).
+EXPORTS = [
+    "tilec_mm_f32", "tilec_mm_workspace_bytes", "tilec_mm_plan", "tilec_mm_set_table",
+    "tilec_mm_device_status", "tilec_strerror", "tilec_mm_abi_version", "tilec_mm_built_arch",
+]
+
+
+class MMConfig(ctypes.Structure):
+    _fields_ = [("variant", ctypes.c_int32), ("split_k", ctypes.c_int32), ("reserved", ctypes.c_int32 * 6)]
+
+
+class TilecError(RuntimeError):
+    """A C-ABI call returned a non-zero tilec_status."""
+
+    def __init__(self, code, where):
+        self.code = code
+        super().__init__(f"{where}: {STATUS_NAMES.get(code, code)}: {strerror(code)}")
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib_path():
+    return _build.LIB
+
+
+def load():
+    """Load libtilec_mm.so (building it first if the sources are newer and nvcc exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not _build.up_to_date():
+            try:
+                _build.build()
+            except Exception as e:  # noqa: BLE001
+                if not os.path.exists(_build.LIB):
+                    raise RuntimeError(f"tilec_b200: kernel library {_build.LIB} is missing and could not "
+                                       f"be built ({e})") from e
+        lib = ctypes.CDLL(_build.LIB)
+        vp, i64, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_size_t
+        cfgp = ctypes.POINTER(MMConfig)
+        lib.tilec_mm_f32.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, cfgp, vp, sz, vp]
+        lib.tilec_mm_f32.restype = ctypes.c_int
+        lib.tilec_mm_workspace_bytes.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, cfgp]
+        lib.tilec_mm_workspace_bytes.restype = sz
+        lib.tilec_mm_plan.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, cfgp, cfgp]
+        lib.tilec_mm_plan.restype = ctypes.c_int
+        lib.tilec_mm_set_table.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int32]
+        lib.tilec_mm_set_table.restype = ctypes.c_int
+        lib.tilec_mm_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_int32)]
+        lib.tilec_mm_device_status.restype = ctypes.c_int
+        lib.tilec_strerror.argtypes = [ctypes.c_int]
+        lib.tilec_strerror.restype = ctypes.c_char_p
+        lib.tilec_mm_abi_version.restype = ctypes.c_int
+        lib.tilec_mm_built_arch.restype = ctypes.c_int
+        _lib = lib
+        return _lib
+
+
+def strerror(code):
+    return load().tilec_strerror(int(code)).decode()
+
+
+def check(code, where):
+    if code != TILEC_OK:
+        raise TilecError(code, where)
+
+
+def make_cfg(variant="auto", split_k=0):
+    if isinstance(variant, str):
+        try:
+            v = VARIANTS[variant.lower()]
+        except KeyError:
+            raise ValueError(f"unknown matrix_mul variant {variant!r}; expected one of {sorted(VARIANTS)}")
+    else:
+        v = int(variant)
+    return MMConfig(v, int(split_k))

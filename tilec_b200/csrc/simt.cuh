@@ -1,0 +1,235 @@
+// simt.cuh -- fp32 FFMA GEMM for sm_100a (variant SIMT, and SPLITK when gridDim.z > 1).
+//
+// Arithmetic of the reference kernel tilec/ext.py:13-24 (_matmul_tiled): one CTA owns
+// an output tile, walks K in BK-wide steps, reads out-of-range elements of A and B as
+// 0.0 (ext.py:21-22) and stores only in-range elements of C (ext.py:24).  Every
+// product is a single fp32 FFMA accumulated in k order, so results are fp32-exact
+// in the usual GEMM sense.
+//
+// B200 mapping:
+//   * CTA tile 128 x BN x 16 (BN = 128 or 64), 256 threads, each thread an 8 x (BN/16)
+//     register block (2-D register blocking, 64 or 32 FFMA per k).
+//   * 4-stage cp.async pipeline global -> shared.  16-byte copies when rows are 16-byte
+//     aligned (VEC), 4-byte copies otherwise; the tail of a ragged tile is zero-filled
+//     by cp.async's src-size operand, so no out-of-range address is ever read.
+//   * Shared tiles are unpadded: A as [128][16] (k fastest), B as [16][BN].  A thread
+//     owns rows tm + 16*i, so the two row indices a warp touches per A load are
+//     adjacent and land in different banks; B loads are contiguous float4 runs.
+//   * Split-K (gridDim.z = S > 1): CTA z covers K range [z*k_chunk, min(K,(z+1)*k_chunk))
+//     and writes its partial tile to slab z of the workspace; splitk_reduce_kernel
+//     sums the slabs in z order (deterministic).
+#pragma once
+
+#include "common.cuh"
+
+namespace tilec {
+
+constexpr int kSimtBM = 128;
+constexpr int kSimtBK = 16;
+constexpr int kSimtStages = 4;
+constexpr int kSimtThreads = 256;
+
+template <int BN>
+constexpr int simt_smem_bytes() {
+  return kSimtStages * (kSimtBM * kSimtBK + kSimtBK * BN) * 4;
+}
+
+template <int BN, bool VEC>
+__device__ __forceinline__ void simt_load_tile(float* as, float* bs, const float* __restrict__ A,
+                                               const float* __restrict__ B, int64_t M, int64_t N, int64_t lda,
+                                               int64_t ldb, int64_t m0, int64_t n0, int64_t k0, int64_t k_end,
+                                               int tid) {
+  if constexpr (VEC) {
+    // A: 128 rows x 16 k = 512 float4 chunks, 2 per thread.
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c = tid + i * kSimtThreads;
+      const int row = c >> 2;
+      const int kq = (c & 3) * 4;
+      const int64_t gm = m0 + row, gk = k0 + kq;
+      uint32_t bytes = 0;
+      const float* src = A;
+      if (gm < M && gk < k_end) {
+        const int64_t rem = k_end - gk;
+        bytes = static_cast<uint32_t>(rem >= 4 ? 16 : rem * 4);
+        src = A + gm * lda + gk;
+      }
+      cp_async_16(as + row * kSimtBK + kq, src, bytes);
+    }
+    // B: 16 rows x BN cols = 4*BN float4 chunks.
+    constexpr int kChunksPerRow = BN / 4;
+#pragma unroll
+    for (int i = 0; i < (kSimtBK * BN / 4) / kSimtThreads; ++i) {
+      const int c = tid + i * kSimtThreads;
+      const int row = c / kChunksPerRow;
+      const int nq = (c % kChunksPerRow) * 4;
+      const int64_t gk = k0 + row, gn = n0 + nq;
+      uint32_t bytes = 0;
+      const float* src = B;
+      if (gk < k_end && gn < N) {
+        const int64_t rem = N - gn;
+        bytes = static_cast<uint32_t>(rem >= 4 ? 16 : rem * 4);
+        src = B + gk * ldb + gn;
+      }
+      cp_async_16(bs + row * BN + nq, src, bytes);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < (kSimtBM * kSimtBK) / kSimtThreads; ++i) {
+      const int e = tid + i * kSimtThreads;
+      const int row = e >> 4;
+      const int kk = e & 15;
+      const int64_t gm = m0 + row, gk = k0 + kk;
+      const bool ok = gm < M && gk < k_end;
+      cp_async_4(as + row * kSimtBK + kk, ok ? A + gm * lda + gk : A, ok ? 4u : 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < (kSimtBK * BN) / kSimtThreads; ++i) {
+      const int e = tid + i * kSimtThreads;
+      const int row = e / BN;
+      const int nn = e % BN;
+      const int64_t gk = k0 + row, gn = n0 + nn;
+      const bool ok = gk < k_end && gn < N;
+      cp_async_4(bs + row * BN + nn, ok ? B + gk * ldb + gn : B, ok ? 4u : 0u);
+    }
+  }
+}
+
+// out/ldo: C (gridDim.z == 1) or the split-K workspace (slab z at out + z*out_slab).
+template <int BN, bool VEC>
+__global__ void __launch_bounds__(kSimtThreads, 1)
+    simt_gemm_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ out,
+                     int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldo, int64_t out_slab,
+                     int64_t k_chunk, int vec_out) {
+  constexpr int TN = BN / 16;  // columns per thread: 8 (two float4 groups 64 apart) or 4
+  extern __shared__ __align__(16) float smem[];
+  float* As = smem;
+  float* Bs = smem + kSimtStages * kSimtBM * kSimtBK;
+
+  if (blockDim.x != kSimtThreads) {
+    if (threadIdx.x == 0) record_status(TILEC_DEV_BAD_LAUNCH);
+    return;
+  }
+  const int tid = threadIdx.x;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kSimtBM;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * BN;
+  const int64_t k_begin = static_cast<int64_t>(blockIdx.z) * k_chunk;
+  const int64_t k_end = (k_begin + k_chunk < K) ? k_begin + k_chunk : K;
+  const int64_t nkt = (k_end > k_begin) ? (k_end - k_begin + kSimtBK - 1) / kSimtBK : 0;
+  out += static_cast<int64_t>(blockIdx.z) * out_slab;
+
+  const int tm = tid >> 4;
+  const int tn = tid & 15;
+
+  float acc[8][TN];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
+
+#pragma unroll
+  for (int s = 0; s < kSimtStages - 1; ++s) {
+    if (s < nkt)
+      simt_load_tile<BN, VEC>(As + s * kSimtBM * kSimtBK, Bs + s * kSimtBK * BN, A, B, M, N, lda, ldb, m0, n0,
+                              k_begin + s * kSimtBK, k_end, tid);
+    cp_async_commit();
+  }
+
+  for (int64_t kt = 0; kt < nkt; ++kt) {
+    cp_async_wait<kSimtStages - 2>();
+    __syncthreads();
+    const int64_t nt = kt + kSimtStages - 1;
+    if (nt < nkt) {
+      const int ns = static_cast<int>(nt % kSimtStages);
+      simt_load_tile<BN, VEC>(As + ns * kSimtBM * kSimtBK, Bs + ns * kSimtBK * BN, A, B, M, N, lda, ldb, m0,
+                              n0, k_begin + nt * kSimtBK, k_end, tid);
+    }
+    cp_async_commit();
+
+    const int cs = static_cast<int>(kt % kSimtStages);
+    const float* as = As + cs * kSimtBM * kSimtBK;
+    const float* bs = Bs + cs * kSimtBK * BN;
+#pragma unroll
+    for (int kq = 0; kq < kSimtBK / 4; ++kq) {
+      float4 a4[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        a4[i] = *reinterpret_cast<const float4*>(as + (tm + 16 * i) * kSimtBK + kq * 4);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float* brow = bs + (kq * 4 + kk) * BN;
+        float b[TN];
+        const float4 b0 = *reinterpret_cast<const float4*>(brow + tn * 4);
+        b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
+        if constexpr (TN == 8) {
+          const float4 b1 = *reinterpret_cast<const float4*>(brow + 64 + tn * 4);
+          b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float a = kk == 0 ? a4[i].x : kk == 1 ? a4[i].y : kk == 2 ? a4[i].z : a4[i].w;
+#pragma unroll
+          for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a, b[j], acc[i][j]);
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  // Epilogue: masked stores (ext.py:24).  Each warp writes two 256-byte row runs.
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t gm = m0 + tm + 16 * i;
+    if (gm >= M) continue;
+    float* crow = out + gm * ldo;
+#pragma unroll
+    for (int g = 0; g < TN / 4; ++g) {
+      const int64_t gn = n0 + g * 64 + tn * 4;
+      if (vec_out && gn + 3 < N) {
+        *reinterpret_cast<float4*>(crow + gn) =
+            make_float4(acc[i][g * 4 + 0], acc[i][g * 4 + 1], acc[i][g * 4 + 2], acc[i][g * 4 + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (gn + j < N) crow[gn + j] = acc[i][g * 4 + j];
+      }
+    }
+  }
+}
+
+// C[m, n] = sum_{z < S} W[z][m, n], summed in z order.  W slabs have row stride ldw
+// (a multiple of 4) and slab stride `slab`.  One thread per 4 columns of one row.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ W, float* __restrict__ C,
+                                                            int64_t M, int64_t N, int64_t ldw, int64_t ldc,
+                                                            int64_t slab, int S, int vec_out) {
+  const int64_t groups_per_row = (N + 3) / 4;
+  const int64_t total = M * groups_per_row;
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = g / groups_per_row;
+    const int64_t n = (g % groups_per_row) * 4;
+    const float* w = W + m * ldw + n;
+    float4 s = *reinterpret_cast<const float4*>(w);
+    for (int z = 1; z < S; ++z) {
+      const float4 v = *reinterpret_cast<const float4*>(w + z * slab);
+      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+    }
+    float* c = C + m * ldc + n;
+    if (vec_out && n + 3 < N) {
+      *reinterpret_cast<float4*>(c) = s;
+    } else {
+      const float v[4] = {s.x, s.y, s.z, s.w};
+      for (int j = 0; j < 4 && n + j < N; ++j) c[j] = v[j];
+    }
+  }
+}
+
+// K == 0: the reference's accumulator stays 0 and is stored (ext.py:18,24).
+__global__ void __launch_bounds__(256) fill_zero_kernel(float* __restrict__ C, int64_t M, int64_t N, int64_t ldc) {
+  const int64_t total = M * N;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    C[(e / N) * ldc + (e % N)] = 0.f;
+}
+
+}  // namespace tilec

@@ -1,0 +1,473 @@
+// tilec_mm.cu -- C ABI (include/tilec_mm.h) and host-side dispatch of the sm_100a GEMMs.
+//
+// Host logic of the reference op tilec/ext.py:54-63 (_matrix_mul_tiled) and its launcher
+// tilec/jit.py:88-105 (_launch), minus what the Python wrapper keeps (shape errors,
+// output allocation).  Differences from the reference launcher, by design:
+//   * M, N, K and strides are passed by value as int64 (the reference packs them into
+//     three 1-element int32 device tensors per call, jit.py:93-94, and its i32 indexing
+//     overflows past 2^31 elements);
+//   * the launch shape is chosen per call from the operands (variant, tile, split-K),
+//     where the reference always launches 64x64 tiles (ext.py:54,62).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/tilec_mm.h"
+#include "common.cuh"
+#include "simt.cuh"
+#include "tc_gemm.cuh"
+
+namespace tilec {
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxSplit = 64;
+
+struct DeviceInfo {
+  int sms = 0;
+  int cc_major = 0;
+  int cc_minor = 0;
+  int max_smem_optin = 0;
+  cudaError_t init_err = cudaSuccess;
+};
+
+DeviceInfo g_dev[kMaxDevices];
+std::once_flag g_dev_once[kMaxDevices];
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+std::mutex g_table_mu;
+std::vector<int32_t> g_table;  // rows of 8 int32
+
+template <int BN, int BK, int STAGES, bool SPLIT3, bool HI>
+cudaError_t set_tc_attr() {
+  using Cfg = TcCfg<BN, BK, STAGES, SPLIT3>;
+  return cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+}
+
+// Tensor-kernel instantiations: (BN, BK, STAGES) per mode.
+//   TF32   : BK = 32 (128B-swizzled A), 4 stages.
+//   3XTF32 : BK = 16 (64B-swizzled A), raw + lo buffers per stage.
+template <int BN>
+struct TcShape {
+  static constexpr int kTf32Stages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int k3xStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+};
+
+cudaError_t init_device_attrs() {
+  cudaError_t e = cudaSuccess;
+  auto acc = [&](cudaError_t x) {
+    if (e == cudaSuccess && x != cudaSuccess) e = x;
+  };
+  acc(cudaFuncSetAttribute(simt_gemm_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           simt_smem_bytes<128>()));
+  acc(cudaFuncSetAttribute(simt_gemm_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           simt_smem_bytes<128>()));
+  acc(cudaFuncSetAttribute(simt_gemm_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           simt_smem_bytes<64>()));
+  acc(cudaFuncSetAttribute(simt_gemm_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           simt_smem_bytes<64>()));
+  acc(set_tc_attr<256, 32, TcShape<256>::kTf32Stages, false, false>());
+  acc(set_tc_attr<128, 32, TcShape<128>::kTf32Stages, false, false>());
+  acc(set_tc_attr<64, 32, TcShape<64>::kTf32Stages, false, false>());
+  acc(set_tc_attr<256, 16, TcShape<256>::k3xStages, true, true>());
+  acc(set_tc_attr<128, 16, TcShape<128>::k3xStages, true, true>());
+  acc(set_tc_attr<64, 16, TcShape<64>::k3xStages, true, true>());
+  acc(set_tc_attr<256, 16, TcShape<256>::k3xStages, true, false>());
+  acc(set_tc_attr<128, 16, TcShape<128>::k3xStages, true, false>());
+  acc(set_tc_attr<64, 16, TcShape<64>::k3xStages, true, false>());
+  return e;
+}
+
+int current_device(DeviceInfo** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return TILEC_ERR_NO_DEVICE;
+  }
+  std::call_once(g_dev_once[dev], [dev]() {
+    DeviceInfo& d = g_dev[dev];
+    cudaError_t e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e == cudaSuccess)
+      e = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e == cudaSuccess && d.cc_major != 10) e = cudaErrorNoKernelImageForDevice;
+    if (e == cudaSuccess) e = init_device_attrs();
+    d.init_err = e;
+    cudaGetLastError();
+  });
+  if (g_dev[dev].init_err != cudaSuccess) return TILEC_ERR_NO_DEVICE;
+  *out = &g_dev[dev];
+  return TILEC_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  std::call_once(g_encode_once, []() {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    cudaGetLastError();
+  });
+  return g_encode;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
+
+struct Plan {
+  int variant = TILEC_MM_SIMT;
+  int split = 1;
+  int64_t k_chunk = 0;
+  int bn = 128;
+  size_t ws_bytes = 0;
+  int64_t ldw = 0;
+};
+
+bool tensor_path_ok(const float* A, const float* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb) {
+  const int64_t lim = (int64_t(1) << 31) - 256;
+  return aligned16(A) && aligned16(B) && (lda % 4 == 0) && (ldb % 4 == 0) && M < lim && N < lim && K < lim;
+}
+
+int ilog2_floor(int64_t v) {
+  int r = 0;
+  while (v > 1) { v >>= 1; ++r; }
+  return r;
+}
+
+// Built-in AUTO rules (a table installed with tilec_mm_set_table overrides them).
+void choose_auto(const DeviceInfo& d, const float* A, const float* B, int64_t M, int64_t N, int64_t K,
+                 int64_t lda, int64_t ldb, int* variant, int* split) {
+  {
+    std::lock_guard<std::mutex> lk(g_table_mu);
+    if (!g_table.empty()) {
+      const int lm = ilog2_floor(M), ln = ilog2_floor(N), lk2 = ilog2_floor(K);
+      for (size_t r = 0; r + 8 <= g_table.size(); r += 8) {
+        const int32_t* t = &g_table[r];
+        if (lm >= t[0] && lm < t[1] && ln >= t[2] && ln < t[3] && lk2 >= t[4] && lk2 < t[5]) {
+          int v = t[6];
+          if ((v == TILEC_MM_TF32 || v == TILEC_MM_3XTF32) && !tensor_path_ok(A, B, M, N, K, lda, ldb))
+            v = TILEC_MM_SIMT;
+          *variant = v;
+          *split = t[7];
+          return;
+        }
+      }
+    }
+  }
+  (void)d;
+  *split = 0;
+  const double flops = 2.0 * double(M) * double(N) * double(K);
+  if (tensor_path_ok(A, B, M, N, K, lda, ldb) && flops >= 1.0e8) {
+    *variant = TILEC_MM_3XTF32;
+    return;
+  }
+  const int64_t tiles = cdiv(M, kSimtBM) * cdiv(N, N <= 64 ? 64 : 128);
+  *variant = (tiles < d.sms && K >= 1024) ? TILEC_MM_SPLITK : TILEC_MM_SIMT;
+}
+
+int choose_split(int64_t tiles, int64_t K, int bk, int sms, int requested) {
+  if (requested > 0) return requested > kMaxSplit ? kMaxSplit : requested;
+  if (tiles >= sms) return 1;
+  int64_t s = cdiv(2 * int64_t(sms), tiles);
+  const int64_t max_by_k = K / (int64_t(bk) * 8);  // keep >= 8 K-steps per slice
+  if (s > max_by_k) s = max_by_k;
+  if (s > kMaxSplit) s = kMaxSplit;
+  if (s < 1) s = 1;
+  return static_cast<int>(s);
+}
+
+int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K,
+              int64_t lda, int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg, Plan* p) {
+  (void)C;
+  (void)ldc;
+  int variant = cfg ? cfg->variant : TILEC_MM_AUTO;
+  int requested_split = cfg ? cfg->split_k : 0;
+  if (cfg) {
+    for (int i = 0; i < 6; ++i)
+      if (cfg->reserved[i] != 0) return TILEC_ERR_BAD_ARG;
+  }
+  if (requested_split < 0) return TILEC_ERR_BAD_ARG;
+  if (variant == TILEC_MM_AUTO) choose_auto(d, A, B, M, N, K, lda, ldb, &variant, &requested_split);
+  if (variant < TILEC_MM_SIMT || variant > TILEC_MM_3XTF32_RAWHI) return TILEC_ERR_BAD_ARG;
+  const bool tensor = variant == TILEC_MM_TF32 || variant == TILEC_MM_3XTF32 || variant == TILEC_MM_3XTF32_RAWHI;
+  if (tensor && !tensor_path_ok(A, B, M, N, K, lda, ldb)) return TILEC_ERR_MISALIGNED;
+
+  p->variant = variant;
+  if (tensor) {
+    p->bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
+    const int bk = variant == TILEC_MM_TF32 ? 32 : 16;
+    const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
+    p->split = choose_split(tiles, K, bk, d.sms, requested_split);
+    p->k_chunk = round_up(cdiv(K, p->split), bk);
+    p->split = static_cast<int>(cdiv(K, p->k_chunk > 0 ? p->k_chunk : 1));
+    if (p->split < 1) p->split = 1;
+  } else {
+    p->bn = N <= 64 ? 64 : 128;
+    const int64_t tiles = cdiv(M, kSimtBM) * cdiv(N, p->bn);
+    int split = 1;
+    if (variant == TILEC_MM_SPLITK) split = choose_split(tiles, K, kSimtBK, d.sms, requested_split);
+    p->k_chunk = round_up(cdiv(K, split), kSimtBK);
+    split = static_cast<int>(cdiv(K, p->k_chunk > 0 ? p->k_chunk : 1));
+    p->split = split < 1 ? 1 : split;
+  }
+  if (p->k_chunk <= 0) p->k_chunk = 16;
+  p->ldw = round_up(N, 4);
+  p->ws_bytes = p->split > 1 ? size_t(p->split) * size_t(M) * size_t(p->ldw) * sizeof(float) : 0;
+  return TILEC_OK;
+}
+
+int check_args(const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+               int64_t ldb, int64_t ldc) {
+  if (M < 0 || N < 0 || K < 0) return TILEC_ERR_BAD_ARG;
+  if (M == 0 || N == 0) return TILEC_OK;
+  if (C == nullptr || ldc < N) return TILEC_ERR_BAD_ARG;
+  if (K > 0 && (A == nullptr || B == nullptr || lda < K || ldb < N)) return TILEC_ERR_BAD_ARG;
+  return TILEC_OK;
+}
+
+int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TILEC_OK : TILEC_ERR_LAUNCH;
+}
+
+int encode_maps(const float* A, const float* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                int bk, int a_swizzle_bytes, CUtensorMap* ma, CUtensorMap* mb) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode();
+  if (!enc) return TILEC_ERR_NO_DEVICE;
+  {
+    cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(M)};
+    cuuint64_t strides[1] = {cuuint64_t(lda) * 4};
+    cuuint32_t box[2] = {cuuint32_t(bk), cuuint32_t(kTcBM)};
+    cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapSwizzle sw =
+        a_swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    if (enc(ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(A), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return TILEC_ERR_BAD_ARG;
+  }
+  {
+    cuuint64_t dims[2] = {cuuint64_t(N), cuuint64_t(K)};
+    cuuint64_t strides[1] = {cuuint64_t(ldb) * 4};
+    cuuint32_t box[2] = {32, cuuint32_t(bk)};
+    cuuint32_t estr[2] = {1, 1};
+    if (enc(mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(B), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return TILEC_ERR_BAD_ARG;
+  }
+  return TILEC_OK;
+}
+
+template <int BN, int BK, int STAGES, bool SPLIT3, bool HI>
+int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N, int64_t ldo,
+              int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, cudaStream_t s) {
+  using Cfg = TcCfg<BN, BK, STAGES, SPLIT3>;
+  const int m_tiles = static_cast<int>(cdiv(M, kTcBM));
+  const int n_tiles = static_cast<int>(cdiv(N, BN));
+  const int group_m = 16;
+  dim3 grid(static_cast<unsigned>(int64_t(m_tiles) * n_tiles), 1, static_cast<unsigned>(split));
+  tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI><<<grid, kTcThreads, Cfg::kSmemBytes, s>>>(
+      ma, mb, out, static_cast<int>(M), static_cast<int>(N), ldo, slab, static_cast<int>(K),
+      static_cast<int>(k_chunk), m_tiles, n_tiles, group_m, vec_out);
+  return launch_status();
+}
+
+template <int BN, bool SPLIT3, bool HI>
+int launch_tc_mode(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N, int64_t ldo,
+                   int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, cudaStream_t s) {
+  if constexpr (SPLIT3)
+    return launch_tc<BN, 16, TcShape<BN>::k3xStages, true, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split,
+                                                               vec_out, s);
+  else
+    return launch_tc<BN, 32, TcShape<BN>::kTf32Stages, false, false>(ma, mb, out, M, N, ldo, slab, K, k_chunk,
+                                                                     split, vec_out, s);
+}
+
+template <bool SPLIT3, bool HI>
+int dispatch_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N,
+                   int64_t ldo, int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, cudaStream_t s) {
+  switch (bn) {
+    case 64: return launch_tc_mode<64, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, s);
+    case 128: return launch_tc_mode<128, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, s);
+    default: return launch_tc_mode<256, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, s);
+  }
+}
+
+int launch_reduce(const float* ws, float* C, int64_t M, int64_t N, int64_t ldw, int64_t ldc, int split,
+                  const DeviceInfo& d, cudaStream_t s) {
+  const int64_t groups = M * cdiv(N, 4);
+  int64_t blocks = cdiv(groups, 256);
+  const int64_t cap = int64_t(d.sms) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  const int vec_out = aligned16(C) && (ldc % 4 == 0);
+  splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(ws, C, M, N, ldw, ldc, M * ldw, split,
+                                                                     vec_out);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace tilec
+
+using namespace tilec;
+
+extern "C" {
+
+int tilec_mm_plan(const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                  int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg, tilec_mm_cfg* out) {
+  if (!out) return TILEC_ERR_BAD_ARG;
+  int rc = check_args(A, B, C, M, N, K, lda, ldb, ldc);
+  if (rc) return rc;
+  DeviceInfo* d = nullptr;
+  rc = current_device(&d);
+  if (rc) return rc;
+  Plan p;
+  rc = make_plan(*d, A, B, C, M, N, K, lda, ldb, ldc, cfg, &p);
+  if (rc) return rc;
+  std::memset(out, 0, sizeof(*out));
+  out->variant = p.variant;
+  out->split_k = p.split;
+  return TILEC_OK;
+}
+
+size_t tilec_mm_workspace_bytes(const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K,
+                                int64_t lda, int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  DeviceInfo* d = nullptr;
+  if (current_device(&d)) return 0;
+  // NULL operands: assume 16-byte aligned pointers (documented in the header).
+  const float* a = A ? A : reinterpret_cast<const float*>(uintptr_t(256));
+  const float* b = B ? B : reinterpret_cast<const float*>(uintptr_t(256));
+  Plan p;
+  if (make_plan(*d, a, b, C, M, N, K, lda, ldb, ldc, cfg, &p)) return 0;
+  return p.ws_bytes;
+}
+
+int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                 int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg, void* workspace, size_t ws_bytes,
+                 void* stream) {
+  int rc = check_args(A, B, C, M, N, K, lda, ldb, ldc);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return TILEC_OK;
+  DeviceInfo* d = nullptr;
+  rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  if (K == 0) {
+    int64_t blocks = cdiv(M * N, 256);
+    if (blocks > int64_t(d->sms) * 8) blocks = int64_t(d->sms) * 8;
+    fill_zero_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(C, M, N, ldc);
+    return launch_status();
+  }
+
+  Plan p;
+  rc = make_plan(*d, A, B, C, M, N, K, lda, ldb, ldc, cfg, &p);
+  if (rc) return rc;
+  if (p.split > 1) {
+    if (!workspace || ws_bytes < p.ws_bytes || !aligned16(workspace)) return TILEC_ERR_WORKSPACE;
+  }
+  float* out = p.split > 1 ? static_cast<float*>(workspace) : C;
+  const int64_t ldo = p.split > 1 ? p.ldw : ldc;
+  const int64_t slab = p.split > 1 ? M * p.ldw : 0;
+  const int vec_out = p.split > 1 ? 1 : (aligned16(C) && (ldc % 4 == 0) ? 1 : 0);
+
+  if (p.variant == TILEC_MM_SIMT || p.variant == TILEC_MM_SPLITK) {
+    const bool vec = aligned16(A) && aligned16(B) && (lda % 4 == 0) && (ldb % 4 == 0);
+    const int64_t mt = cdiv(M, kSimtBM), nt = cdiv(N, p.bn);
+    if (nt > 65535) return TILEC_ERR_UNSUPPORTED;
+    dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(p.split));
+    if (p.bn == 64) {
+      if (vec)
+        simt_gemm_kernel<64, true><<<grid, kSimtThreads, simt_smem_bytes<64>(), s>>>(
+            A, B, out, M, N, K, lda, ldb, ldo, slab, p.k_chunk, vec_out);
+      else
+        simt_gemm_kernel<64, false><<<grid, kSimtThreads, simt_smem_bytes<64>(), s>>>(
+            A, B, out, M, N, K, lda, ldb, ldo, slab, p.k_chunk, vec_out);
+    } else {
+      if (vec)
+        simt_gemm_kernel<128, true><<<grid, kSimtThreads, simt_smem_bytes<128>(), s>>>(
+            A, B, out, M, N, K, lda, ldb, ldo, slab, p.k_chunk, vec_out);
+      else
+        simt_gemm_kernel<128, false><<<grid, kSimtThreads, simt_smem_bytes<128>(), s>>>(
+            A, B, out, M, N, K, lda, ldb, ldo, slab, p.k_chunk, vec_out);
+    }
+    rc = launch_status();
+  } else {
+    CUtensorMap ma, mb;
+    const int bk = p.variant == TILEC_MM_TF32 ? 32 : 16;
+    rc = encode_maps(A, B, M, N, K, lda, ldb, bk, bk * 4, &ma, &mb);
+    if (rc) return rc;
+    if (p.variant == TILEC_MM_TF32)
+      rc = dispatch_tc_bn<false, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
+    else if (p.variant == TILEC_MM_3XTF32)
+      rc = dispatch_tc_bn<true, true>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
+    else
+      rc = dispatch_tc_bn<true, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
+  }
+  if (rc) return rc;
+  if (p.split > 1) rc = launch_reduce(static_cast<float*>(workspace), C, M, N, p.ldw, ldc, p.split, *d, s);
+  return rc;
+}
+
+int tilec_mm_set_table(const int32_t* rows, int32_t nrows) {
+  if (nrows < 0 || (nrows > 0 && rows == nullptr)) return TILEC_ERR_BAD_ARG;
+  for (int32_t r = 0; r < nrows; ++r) {
+    const int32_t v = rows[r * 8 + 6];
+    if (v < TILEC_MM_SIMT || v > TILEC_MM_3XTF32_RAWHI || rows[r * 8 + 7] < 0) return TILEC_ERR_BAD_ARG;
+  }
+  std::lock_guard<std::mutex> lk(g_table_mu);
+  g_table.assign(rows, rows + size_t(nrows) * 8);
+  return TILEC_OK;
+}
+
+int tilec_mm_device_status(void* stream, int32_t* status_out) {
+  if (!status_out) return TILEC_ERR_BAD_ARG;
+  DeviceInfo* d = nullptr;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  const int zero = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_status, sizeof(int), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaMemcpyToSymbolAsync(g_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess) {
+    cudaGetLastError();
+    return TILEC_ERR_DEVICE;
+  }
+  *status_out = v;
+  return TILEC_OK;
+}
+
+const char* tilec_strerror(int code) {
+  switch (code) {
+    case TILEC_OK: return "ok";
+    case TILEC_ERR_BAD_ARG: return "bad argument (negative size, null pointer, or leading dimension too small)";
+    case TILEC_ERR_MISALIGNED: return "tensor-core variant needs 16-byte aligned operands and row strides";
+    case TILEC_ERR_NO_DEVICE: return "no usable sm_100 CUDA device";
+    case TILEC_ERR_LAUNCH: return "kernel launch failed";
+    case TILEC_ERR_DEVICE: return "device-side check failed";
+    case TILEC_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case TILEC_ERR_UNSUPPORTED: return "unsupported size for this variant";
+    case TILEC_ERR_TOO_LARGE: return "request exceeds the entry point's fixed limit";
+    default: return "unknown tilec status";
+  }
+}
+
+int tilec_mm_abi_version(void) { return TILEC_MM_ABI_VERSION; }
+int tilec_mm_built_arch(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,132 @@
+"""Row-sharded matrix_mul across the GPUs of one box (one process per GPU).
+
+The reference has no multi-GPU path.  For large M, C = x1 @ x2 splits into independent
+row blocks C[r] = x1[r] @ x2 once every GPU holds x2, so the only exchange is
+replicating x2 from one rank:
+
+* rank r owns rows ``shard_rows(M, world, r)`` of x1 and of C;
+* x2 ([K, N], on rank ``src``) is cut into ``panels`` column panels; rank ``src`` packs
+  panel p into a contiguous [K, w_p] buffer and NCCL broadcasts it into every rank's
+  own buffer (kernels only ever read local memory);
+* every broadcast is enqueued up front on the NCCL stream; the GEMM of panel p waits
+  for broadcast p only (``Work.wait()`` orders the compute stream behind the NCCL
+  stream; no host blocking and no device spin-wait), so broadcast p+1 overlaps GEMM p;
+* panel p's GEMM writes C[:, n0:n1] in place (ldc = N): no reduction, no extra traffic;
+* the output stays sharded, or is all-gathered on request (``gather=True``).
+
+Process groups use the backend of the caller (NCCL on GPUs; the partition, broadcast
+and gather logic is also exercised with gloo on CPU ranks in the tests).
+"""
+import torch
+import torch.distributed as dist
+
+
+def shard_rows(M, world, rank):
+    """[start, stop) of the rows rank owns: near-equal blocks, the first M % world ranks get one extra."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} for world size {world}")
+    base, extra = divmod(M, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def panel_bounds(N, panels, align=256):
+    """Split [0, N) into <= panels contiguous column ranges, widths multiples of `align`
+    except the last (tile-aligned panels keep the GEMM's N tiles whole)."""
+    if N <= 0:
+        return []
+    panels = max(1, int(panels))
+    width = -(-N // panels)
+    width = -(-width // align) * align
+    out = []
+    n0 = 0
+    while n0 < N:
+        n1 = min(N, n0 + width)
+        out.append((n0, n1))
+        n0 = n1
+    return out
+
+
+def pack_panels(x2, bounds, bufs):
+    """Copy column panels of x2 into contiguous per-panel buffers (source rank only)."""
+    for (n0, n1), b in zip(bounds, bufs):
+        b.copy_(x2[:, n0:n1])
+
+
+def broadcast_panels(bufs, src=0, group=None):
+    """Enqueue one async broadcast per panel; returns the Work handles in panel order."""
+    return [dist.broadcast(b, src=src, group=group, async_op=True) for b in bufs]
+
+
+def gather_rows(c_shard, M, group=None):
+    """All-gather row shards (possibly of unequal length) into the full [M, N] result."""
+    world = dist.get_world_size(group)
+    sizes = [shard_rows(M, world, r) for r in range(world)]
+    longest = max(b - a for a, b in sizes)
+    N = c_shard.shape[1]
+    padded = c_shard
+    if c_shard.shape[0] != longest:
+        padded = c_shard.new_zeros(longest, N)
+        padded[: c_shard.shape[0]].copy_(c_shard)
+    full = c_shard.new_empty(world * longest, N)
+    dist.all_gather_into_tensor(full, padded.contiguous(), group=group)
+    parts = [full[r * longest: r * longest + (b - a)] for r, (a, b) in enumerate(sizes)]
+    return torch.cat(parts, 0)
+
+
+class RowShardedMatmul:
+    """C[rows of this rank] = x1_shard @ x2, with x2 broadcast from ``src`` in panels.
+
+    Buffers for x2's panels are allocated once and reused across calls.
+    """
+
+    def __init__(self, K, N, panels=2, group=None, src=0, device=None):
+        self.K, self.N = int(K), int(N)
+        self.group = group
+        self.src = src
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.bounds = panel_bounds(self.N, panels if self.world > 1 else 1)
+        self.bufs = [torch.empty(self.K, n1 - n0, dtype=torch.float32, device=self.device)
+                     for (n0, n1) in self.bounds] if self.world > 1 else []
+        self.gemm_launches_per_call = len(self.bounds)
+
+    def __call__(self, x1_shard, x2=None, out=None, gather=False, M=None, on_gemm=None):
+        """x2: [K, N] on rank src (ignored elsewhere).  out: optional [rows, N] result.
+        on_gemm(p, fn): optional hook wrapping each panel GEMM launch (used for timing)."""
+        from . import ext
+        rows = x1_shard.shape[0]
+        if out is None:
+            out = x1_shard.new_empty(rows, self.N)
+        if self.world == 1:
+            def run():
+                ext._matrix_mul(x1_shard, x2, out=out)
+            (on_gemm(0, run) if on_gemm else run())
+            return out
+        if self.rank == self.src:
+            if x2 is None or tuple(x2.shape) != (self.K, self.N):
+                raise ValueError(f"rank {self.rank} is the source: x2 must be [{self.K}, {self.N}]")
+            pack_panels(x2, self.bounds, self.bufs)
+        works = broadcast_panels(self.bufs, self.src, self.group)
+        for p, ((n0, n1), buf, w) in enumerate(zip(self.bounds, self.bufs, works)):
+            w.wait()
+
+            def run(buf=buf, n0=n0, n1=n1):
+                ext._matrix_mul(x1_shard, buf, out=out[:, n0:n1])
+            (on_gemm(p, run) if on_gemm else run())
+        if gather:
+            if M is None:
+                raise ValueError("gather=True needs the global row count M")
+            return gather_rows(out, M, self.group)
+        return out
+
+
+def matrix_mul_rowsharded(x1_shard, x2, group=None, src=0, gather=False, M=None, panels=2):
+    """One-shot row-sharded matrix_mul (allocates panel buffers per call)."""
+    K = x1_shard.shape[1]
+    N = x2.shape[1] if x2 is not None else None
+    if N is None:
+        raise ValueError("every rank needs N: pass x2 (any [K, N] tensor on non-source ranks)")
+    op = RowShardedMatmul(K, N, panels=panels, group=group, src=src, device=x1_shard.device)
+    return op(x1_shard, x2, gather=gather, M=M)

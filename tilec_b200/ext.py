@@ -1,0 +1,155 @@
+"""tilec_b200.ext -- drop-in for ``tilec.ext`` (tilec/ext.py) on NVIDIA B200.
+
+``matrix_mul(x1, x2)`` keeps the reference's call signature, argument meaning, result
+and error behaviour (tilec/ext.py:54-67):
+
+* ``x1`` [M, K] and ``x2`` [K, N] float32 tensors on one CUDA device;
+* ``K != K2`` raises ``ValueError("matrix_mul: shapes (..) and (..) don't match")``
+  (ext.py:57-58); tensors that are not 2-D fail when their shape is unpacked
+  (ext.py:55-56), also with ``ValueError``;
+* a non-float32 tensor raises ``TypeError`` (the reference's argument type check,
+  tilec/jit.py:34-39);
+* the result is a new [M, N] float32 tensor allocated like ``x1.new_empty(M, N)``
+  (ext.py:61) holding ``x1 @ x2``.
+
+Where the reference always copies its inputs with ``.contiguous()`` (ext.py:59-60), row
+views with unit column stride are passed through with their row stride (no copy);
+other layouts are still made contiguous.  There is no CPU path: CPU tensors raise, and
+a missing kernel library raises.
+"""
+import ctypes
+import os
+
+import torch
+
+from . import _native
+from .language import cdiv  # noqa: F401  (re-exported like tilec/ext.py:3)
+
+# Kernel tile shapes (for callers that size work around them; the library picks per call).
+SIMT_TILE = (128, 128, 16)     # BM, BN, BK of the SIMT kernel
+TENSOR_TILE = (128, 256, 16)   # BM, BN, BK of the tcgen05 3xTF32 kernel
+
+_ENV_VARIANT = "TILEC_MM_VARIANT"
+
+
+def _default_variant():
+    return os.environ.get(_ENV_VARIANT, "auto")
+
+
+def _check_operand(x):
+    if x.dtype != torch.float32:
+        raise TypeError(f"unsupported kernel argument of dtype {x.dtype} (use float32 tensors and ints)")
+
+
+def _rows(x):
+    """Return (tensor, row stride) with unit column stride; copies only when it must."""
+    r, c = x.shape
+    if (c <= 1 or x.stride(1) == 1) and (r <= 1 or x.stride(0) >= max(c, 1)):
+        return x, (x.stride(0) if r > 1 else max(c, 1))
+    x = x.contiguous()
+    return x, max(c, 1)
+
+
+def _check_out(out, M, N, device):
+    if out.dtype != torch.float32:
+        raise TypeError(f"matrix_mul: out must be float32, got {out.dtype}")
+    if out.device != device:
+        raise ValueError(f"matrix_mul: out is on {out.device}, inputs on {device}")
+    if tuple(out.shape) != (M, N):
+        raise ValueError(f"matrix_mul: out has shape {tuple(out.shape)}, expected {(M, N)}")
+    if not ((N <= 1 or out.stride(1) == 1) and (M <= 1 or out.stride(0) >= max(N, 1))):
+        raise ValueError("matrix_mul: out must have unit column stride and non-overlapping rows")
+    return out.stride(0) if M > 1 else max(N, 1)
+
+
+def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k):
+    lib = _native.load()
+    from . import select  # installs the B200 selection table on first use
+    select.ensure_installed()
+    cfg = _native.make_cfg(variant, split_k)
+    pa, pb, pc = a.data_ptr(), b.data_ptr(), out.data_ptr()
+    with torch.cuda.device(out.device):
+        stream = torch.cuda.current_stream(out.device).cuda_stream
+        ws_bytes = lib.tilec_mm_workspace_bytes(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg))
+        ws = None
+        if ws_bytes:
+            ws = torch.empty((ws_bytes + 3) // 4, dtype=torch.float32, device=out.device)
+        rc = lib.tilec_mm_f32(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg),
+                              ws.data_ptr() if ws is not None else None, ws_bytes, stream)
+    _native.check(rc, "tilec_mm_f32")
+    return out
+
+
+def _matrix_mul(x1, x2, variant=None, split_k=0, out=None):
+    """matrix_mul with explicit kernel choice.
+
+    variant: None (= $TILEC_MM_VARIANT or "auto"), "simt", "splitk", "tf32", "3xtf32",
+    "3xtf32_rawhi".  split_k: K slices for split variants (0 = library choice).
+    out: optional preallocated [M, N] float32 result (unit column stride).
+    """
+    M, K = x1.shape
+    K2, N = x2.shape
+    if K != K2:
+        raise ValueError(f"matrix_mul: shapes {tuple(x1.shape)} and {tuple(x2.shape)} don't match")
+    _check_operand(x1)
+    _check_operand(x2)
+    if x1.device.type != "cuda" or x2.device.type != "cuda":
+        raise ValueError(f"matrix_mul: inputs must be CUDA tensors (got {x1.device} and {x2.device}); "
+                         "tilec_b200 has no CPU path")
+    if x1.device != x2.device:
+        raise ValueError(f"matrix_mul: inputs on different devices ({x1.device}, {x2.device})")
+    a, lda = _rows(x1)
+    b, ldb = _rows(x2)
+    if out is None:
+        out = x1.new_empty(M, N)
+        ldc = max(N, 1)
+    else:
+        ldc = _check_out(out, M, N, x1.device)
+    if M == 0 or N == 0:
+        return out
+    return _launch(a, lda, b, ldb, out, ldc, M, N, K, variant or _default_variant(), split_k)
+
+
+def matrix_mul(x1, x2):
+    """C = x1 @ x2 for float32 CUDA tensors x1 [M, K], x2 [K, N] (tilec/ext.py:66-67)."""
+    return _matrix_mul(x1, x2)
+
+
+def plan(x1, x2, variant=None, split_k=0):
+    """The (variant name, split_k) that matrix_mul would launch for these operands."""
+    M, K = x1.shape
+    _, N = x2.shape
+    a, lda = _rows(x1)
+    b, ldb = _rows(x2)
+    lib = _native.load()
+    from . import select
+    select.ensure_installed()
+    cfg = _native.make_cfg(variant or _default_variant(), split_k)
+    res = _native.MMConfig()
+    with torch.cuda.device(x1.device):
+        rc = lib.tilec_mm_plan(a.data_ptr(), b.data_ptr(), None, M, N, K, lda, ldb, max(N, 1),
+                               ctypes.byref(cfg), ctypes.byref(res))
+    _native.check(rc, "tilec_mm_plan")
+    return _native.VARIANT_NAMES.get(res.variant, res.variant), res.split_k
+
+
+def mm_configs(M, K, N):
+    """Candidate (variant, split_k) launch configs for an [M,K]x[K,N] product.
+
+    B200 counterpart of the reference's config space (tilec/ext.py:48-51), which the
+    tuner sweeps (tilec/tune.py:82).  Tensor-core variants need 16-byte aligned rows
+    (K and N multiples of 4 for contiguous operands).
+    """
+    out = [("simt", 1)]
+    tiles = cdiv(M, 128) * cdiv(N, 128)
+    for s in (2, 4, 8, 16, 32):
+        if K >= s * 128 and tiles < 4 * 148:
+            out.append(("splitk", s))
+    if K % 4 == 0 and N % 4 == 0:
+        for v in ("3xtf32", "tf32"):
+            out.append((v, 1))
+            tiles_tc = cdiv(M, 128) * cdiv(N, 256 if N > 128 else (128 if N > 64 else 64))
+            for s in (2, 4, 8, 16, 32):
+                if K >= s * 256 and tiles_tc < 2 * 148:
+                    out.append((v, s))
+    return out
