@@ -67,7 +67,7 @@ def variant_peak(variant, pk, sustained):
     """(peak TFLOP/s of the pipe the variant uses, note)."""
     bf16 = pk["bf16_sus"] if sustained else pk["bf16"]
     tag = f"{pk['src']} bf16 {'sustained' if sustained else 'burst'} {bf16:.0f}"
-    if variant in ("3xtf32", "3xtf32_rawhi"):
+    if variant in ("3xtf32", "3xtf32_masked"):
         return bf16 / 2 / 3, f"{tag} / 2 (tf32 rate) / 3 (MMAs per useful FLOP)"
     if variant == "tf32":
         return bf16 / 2, f"{tag} / 2 (tf32 rate)"

@@ -60,9 +60,11 @@ typedef enum tilec_mm_variant {
   TILEC_MM_SIMT = 1,      /* fp32 FFMA, exact fp32 products; any strides / alignment */
   TILEC_MM_SPLITK = 2,    /* SIMT with K split over CTAs + ordered reduction (skinny / small-M shapes) */
   TILEC_MM_TF32 = 3,      /* tcgen05 kind::tf32, TMEM accumulators; rows must be 16-byte aligned */
-  TILEC_MM_3XTF32 = 4,    /* tcgen05 kind::tf32 with hi/lo operand split (3 MMAs): fp32-class accuracy */
-  TILEC_MM_3XTF32_RAWHI = 5 /* as 3XTF32, but hi(x) is the tensor core's own tf32 reading of x (its low 13
-                               mantissa bits ignored) instead of an explicitly masked copy */
+  TILEC_MM_3XTF32 = 4,    /* tcgen05 kind::tf32 with hi/lo operand split (3 MMAs) and fp32 promotion of
+                             K-chunk partial sums: fp32-class accuracy; hi(x) is the tensor core's own
+                             tf32 reading of x (its low 13 mantissa bits ignored) */
+  TILEC_MM_3XTF32_MASKED = 5 /* as 3XTF32 with hi(x) written explicitly (low 13 bits cleared) in shared
+                                memory; same results, one more shared store per element (cross-check) */
 } tilec_mm_variant;
 
 /* Per-call configuration.  Zero-initialise, then set what you need. */

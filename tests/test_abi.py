@@ -49,7 +49,7 @@ def test_abi_constants_match_header():
     assert lib.tilec_mm_built_arch() == 100
     for name, code in re.findall(r"(TILEC_(?:OK|ERR_\w+))\s*=\s*(\d+)", h):
         assert _native.STATUS_NAMES[int(code)] == name
-    for name, code in re.findall(r"TILEC_MM_(AUTO|SIMT|SPLITK|TF32|3XTF32|3XTF32_RAWHI)\s*=\s*(\d+)", h):
+    for name, code in re.findall(r"TILEC_MM_(AUTO|SIMT|SPLITK|TF32|3XTF32|3XTF32_MASKED)\s*=\s*(\d+)", h):
         assert _native.VARIANTS[name.lower()] == int(code)
     assert ctypes.sizeof(_native.MMConfig) == 32
 

@@ -175,7 +175,10 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 //   bits  0-13 start address >> 4     bits 16-29 leading byte offset >> 4
 //   bits 32-45 stride byte offset >> 4 bits 46-47 version (1)
 //   bits 49-51 base offset (0: tiles are 1024-byte aligned)  bits 61-63 layout type
-enum : uint32_t { kLayoutSw128 = 2, kLayoutSw64 = 4, kLayoutSw32 = 6 };
+//   Layout types: 2 = 128B swizzle (16-byte granules, 8-row atoms), 4 = 64B, 6 = 32B,
+//   1 = 128B swizzle with 32-byte granules (4-row atoms of 128-byte rows) -- the only
+//   layout the tensor core accepts for MN-major 32-bit (tf32) operands.
+enum : uint32_t { kLayoutSw128 = 2, kLayoutSw64 = 4, kLayoutSw32 = 6, kLayoutSw128Base32 = 1 };
 
 __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
                                                    uint32_t layout) {

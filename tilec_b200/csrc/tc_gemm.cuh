@@ -4,22 +4,34 @@
 // out-of-range operand elements read as 0.0 (TMA zero fill, matching ext.py:21-22),
 // out-of-range outputs never stored (ext.py:24).
 //
-// One CTA owns a 128 x BN output tile (BN = 64/128/256) whose fp32 accumulator lives in
-// TMEM (BN columns x 128 lanes).  192 threads, warp-specialised:
+// One CTA owns a 128 x BN output tile (BN = 64/128/256); fp32 accumulators live in TMEM.
+// Warp-specialised:
 //   warp 0      TMA producer: A tile [128 x BK] K-major (128B/64B swizzle), B tile as
-//               BN/32 slabs of [BK x 32] MN-major (128B swizzle); one mbarrier per stage.
+//               BN/32 slabs of [BK x 32] MN-major (128B swizzle with 32-byte granules,
+//               the only MN-major layout kind::tf32 reads); one mbarrier per stage.
 //   warp 1      allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=BN, K=8 per
-//               instruction) and tcgen05.commit to release stages / signal the epilogue.
-//   warps 2..5  epilogue: tcgen05.ld 32x32b rows out of TMEM, masked stores to C (or to a
-//               split-K workspace slab).  In 3XTF32 mode they first act as the "split"
-//               stage: for every landed stage they write lo = x - hi(x) next to the raw
-//               tile (hi(x) = x with the low 13 mantissa bits cleared; optionally written
-//               back in place) so the MMA warp can issue  A_lo.B_hi + A_hi.B_lo + A_hi.B_hi.
+//               instruction) and tcgen05.commit to release stages / publish results.
+//   warps 2..   epilogue.
+//
+// TF32 (SPLIT3 = false): one TMEM accumulator over all of K; 4 epilogue warps read it
+// once (tcgen05.ld 32x32b) and store rows of C.
+//
+// 3XTF32 (SPLIT3 = true): C = A_lo.B_hi + A_hi.B_lo + A_hi.B_hi with hi(x) = x with the
+// low 13 mantissa bits cleared and lo(x) = x - hi(x) (exact in fp32).  The tensor core
+// reads only the top 19 bits of a tf32 operand, so the raw fp32 tile already *is* hi(x)
+// (HI_EXPLICIT = true writes the masked copy anyway; a GPU test checks both agree bit
+// for bit).  8 epilogue warps first act as the split stage (write lo next to each landed
+// tile, fence.proxy.async, arrive), then as accumulator drains:
+//   the tensor core accumulates with truncation, which biases long sums (relative error
+//   grows ~linearly with K: 5.8e-5 at K = 8192 measured on B200 with one accumulator).
+//   So the MMA accumulates K-chunks of KC_BLOCKS*BK into two ping-pong TMEM buffers, and
+//   every finished chunk is added into fp32 registers (round-to-nearest FADD) by the
+//   epilogue warps while the next chunk's MMAs run.  Each epilogue thread owns one row
+//   (TMEM lane) and BN/2 columns.
 //
 // Operands: A = x1 row-major (K contiguous) -> K-major; B = x2 row-major (N contiguous)
-// -> MN-major.  kind::tf32 accepts MN-major B, so x2 is consumed in place (no transpose).
-// TMA needs 16-byte aligned bases and row strides (lda, ldb multiples of 4); the host
-// routes anything else to the SIMT kernel.
+// -> MN-major, consumed in place (no transpose).  TMA needs 16-byte aligned bases and
+// row strides (lda, ldb multiples of 4); the host routes anything else to the SIMT kernel.
 #pragma once
 
 #include "common.cuh"
@@ -27,10 +39,11 @@
 namespace tilec {
 
 constexpr int kTcBM = 128;
-constexpr int kTcThreads = 192;
 
 template <int BN, int BK, int STAGES, bool SPLIT3>
 struct TcCfg {
+  static constexpr int kEpiWarps = SPLIT3 ? 8 : 4;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kABytes = kTcBM * BK * 4;
   static constexpr int kBBytes = BK * BN * 4;
   static constexpr int kStageBytes = (kABytes + kBBytes) * (SPLIT3 ? 2 : 1);
@@ -40,9 +53,13 @@ struct TcCfg {
   static constexpr uint32_t kALayout = (BK == 32) ? kLayoutSw128 : kLayoutSw64;
   static constexpr uint32_t kASbo = (BK == 32) ? 1024u : 512u;  // 8 rows x (BK*4) bytes
   static constexpr uint32_t kBLbo = BK * 128u;                  // stride between 32-column slabs
-  static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+  static constexpr uint32_t kBSbo = 512u;                       // stride between 4-row K groups
+  static constexpr uint32_t kTmemCols = SPLIT3 ? 2 * BN : BN;   // 3XTF32: two chunk buffers
+  static constexpr int kColsPerThread = SPLIT3 ? BN / 2 : 32;   // register totals per epilogue thread
+  static constexpr int kChunkBlocks = 8;                        // K-blocks per promoted chunk
   static_assert(BK == 16 || BK == 32, "BK");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
 __device__ __forceinline__ float tf32_hi(float x) {
@@ -57,13 +74,28 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// Grid: x = tile index (grouped raster, see tile_coords), z = K split.
+// Store `n` consecutive fp32 values of one output row (masked at N, vectorised when aligned).
+template <int NV>
+__device__ __forceinline__ void store_row(float* crow, int col, int N, int vec_out, const float (&v)[NV]) {
+  if (vec_out && col + NV - 1 < N) {
+#pragma unroll
+    for (int j = 0; j < NV; j += 4)
+      *reinterpret_cast<float4*>(crow + col + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+      if (col + j < N) crow[col + j] = v[j];
+  }
+}
+
+// Grid: x = tile index (grouped raster), z = K split.
 template <int BN, int BK, int STAGES, bool SPLIT3, bool HI_EXPLICIT>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    float* __restrict__ out, int M, int N, int64_t ldo, int64_t out_slab, int K, int k_chunk,
                    int m_tiles, int n_tiles, int group_m, int vec_out) {
   using Cfg = TcCfg<BN, BK, STAGES, SPLIT3>;
+  constexpr int KC = Cfg::kChunkBlocks;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -76,14 +108,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
   uint64_t* empty = full + STAGES;
   uint64_t* split = empty + STAGES;
-  uint64_t* acc_bar = split + STAGES;
+  uint64_t* chunk_full = split + STAGES;   // [2] MMA -> epilogue (3XTF32)
+  uint64_t* chunk_empty = chunk_full + 2;  // [2] epilogue -> MMA (3XTF32)
+  uint64_t* acc_bar = chunk_empty + 2;     // TF32: accumulator complete
   uint64_t* drain_bar = acc_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (blockDim.x != kTcThreads) {
+  if (blockDim.x != Cfg::kThreads) {
     if (threadIdx.x == 0) record_status(TILEC_DEV_BAD_LAUNCH);
     return;
   }
@@ -103,13 +137,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int k_begin = blockIdx.z * k_chunk;
   const int k_end = min(K, k_begin + k_chunk);
   const int nkb = k_end > k_begin ? (k_end - k_begin + BK - 1) / BK : 0;
+  const int n_chunks = (nkb + KC - 1) / KC;
   out += static_cast<int64_t>(blockIdx.z) * out_slab;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&split[s], 128);
+      mbar_init(&split[s], 32 * Cfg::kEpiWarps);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&chunk_full[b], 1);
+      mbar_init(&chunk_empty[b], Cfg::kEpiWarps);
     }
     mbar_init(acc_bar, 1);
     mbar_init(drain_bar, 1);
@@ -156,9 +195,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_tf32(kTcBM, BN);
       bool ok = true;
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = 0; kb < nkb && ok; ++kb) {
         const int s = kb % STAGES;
         const uint32_t ph = (kb / STAGES) & 1;
+        const int chunk = SPLIT3 ? kb / KC : 0;
+        const bool chunk_start = SPLIT3 ? (kb % KC == 0) : (kb == 0);
+        const uint32_t dcol = SPLIT3 ? static_cast<uint32_t>((chunk & 1) * BN) : 0u;
+        if (SPLIT3 && chunk_start && chunk >= 2) {
+          // Reuse of this buffer: its previous chunk must have been drained.
+          if (!mbar_wait(&chunk_empty[chunk & 1], ((chunk >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
+        }
         if (!mbar_wait(SPLIT3 ? &split[s] : &full[s], ph, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t a_hi_addr = smem_u32(a_raw(s));
@@ -166,86 +212,128 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < BK / 8; ++kk) {
           const uint64_t ad = make_smem_desc(a_hi_addr + kk * 32, 16, Cfg::kASbo, Cfg::kALayout);
-          const uint64_t bd = make_smem_desc(b_hi_addr + kk * 1024, Cfg::kBLbo, 1024, kLayoutSw128);
-          const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+          const uint64_t bd = make_smem_desc(b_hi_addr + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
+          const uint32_t accum = (chunk_start && kk == 0) ? 0u : 1u;
           if constexpr (SPLIT3) {
             const uint64_t adl = make_smem_desc(smem_u32(a_lo(s)) + kk * 32, 16, Cfg::kASbo, Cfg::kALayout);
-            const uint64_t bdl = make_smem_desc(smem_u32(b_lo(s)) + kk * 1024, Cfg::kBLbo, 1024, kLayoutSw128);
-            umma_tf32(tmem, adl, bd, idesc, accum);  // small terms first
-            umma_tf32(tmem, ad, bdl, idesc, 1u);
-            umma_tf32(tmem, ad, bd, idesc, 1u);
+            const uint64_t bdl =
+                make_smem_desc(smem_u32(b_lo(s)) + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
+            umma_tf32(tmem + dcol, adl, bd, idesc, accum);  // small terms first
+            umma_tf32(tmem + dcol, ad, bdl, idesc, 1u);
+            umma_tf32(tmem + dcol, ad, bd, idesc, 1u);
           } else {
             umma_tf32(tmem, ad, bd, idesc, accum);
           }
         }
         umma_commit(&empty[s]);
+        if (SPLIT3 && (kb % KC == KC - 1 || kb == nkb - 1)) umma_commit(&chunk_full[chunk & 1]);
       }
       if (ok) {
-        if (nkb > 0) umma_commit(acc_bar);
+        if (!SPLIT3 && nkb > 0) umma_commit(acc_bar);
       } else {
         umma_commit(drain_bar);
         mbar_drain(drain_bar, 0);
       }
     }
   } else {
-    // ------------------------------------------------------------ split + epilogue (warps 2..5)
-    const int et = threadIdx.x - 64;  // 0..127
+    // ------------------------------------------------------------ epilogue warps
+    const int e = warp - 2;                  // 0 .. kEpiWarps-1
+    const int q = warp & 3;                  // TMEM lane quadrant this warp may access
+    const int row = m0 + 32 * q + lane;
+    float* crow = out + static_cast<int64_t>(row) * ldo;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
     bool ok = true;
+
     if constexpr (SPLIT3) {
+      constexpr int COLS = Cfg::kColsPerThread;   // BN / 2
+      const int h = e >> 2;                       // which half of the BN columns
+      const int et = threadIdx.x - 64;            // 0 .. 255
+      float tot[COLS];
+#pragma unroll
+      for (int j = 0; j < COLS; ++j) tot[j] = 0.f;
+
+      auto drain = [&](int c) {
+        const int buf = c & 1;
+        if (!mbar_wait(&chunk_full[buf], (c >> 1) & 1, abort_flag)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < COLS / 32; ++j) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + buf * BN + h * COLS + j * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) tot[j * 32 + i] += __uint_as_float(r[i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&chunk_empty[buf]);
+        return true;
+      };
+
+      constexpr int kLag = 2;  // drain chunk c-1 after splitting this many blocks of chunk c
+      int drained = 0;
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % STAGES;
         const uint32_t ph = (kb / STAGES) & 1;
         if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
         float4* src_a = reinterpret_cast<float4*>(a_raw(s));
         float4* dst_a = reinterpret_cast<float4*>(a_lo(s));
-#pragma unroll 4
-        for (int i = et; i < Cfg::kABytes / 16; i += 128) {
+#pragma unroll
+        for (int i = et; i < Cfg::kABytes / 16; i += 32 * Cfg::kEpiWarps) {
           const float4 x = src_a[i];
-          const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-          dst_a[i] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
-          if constexpr (HI_EXPLICIT) src_a[i] = h;
+          const float4 hv = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+          dst_a[i] = make_float4(x.x - hv.x, x.y - hv.y, x.z - hv.z, x.w - hv.w);
+          if constexpr (HI_EXPLICIT) src_a[i] = hv;
         }
         float4* src_b = reinterpret_cast<float4*>(b_raw(s));
         float4* dst_b = reinterpret_cast<float4*>(b_lo(s));
-#pragma unroll 4
-        for (int i = et; i < Cfg::kBBytes / 16; i += 128) {
+#pragma unroll
+        for (int i = et; i < Cfg::kBBytes / 16; i += 32 * Cfg::kEpiWarps) {
           const float4 x = src_b[i];
-          const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-          dst_b[i] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
-          if constexpr (HI_EXPLICIT) src_b[i] = h;
+          const float4 hv = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+          dst_b[i] = make_float4(x.x - hv.x, x.y - hv.y, x.z - hv.z, x.w - hv.w);
+          if constexpr (HI_EXPLICIT) src_b[i] = hv;
         }
         fence_proxy_async_smem();
         mbar_arrive(&split[s]);
-      }
-    }
-    if (ok && nkb > 0) ok = mbar_wait(acc_bar, 0, abort_flag);
-    if (ok) {
-      tc_fence_after();
-      const int q = warp & 3;  // TMEM lane quadrant this warp may access
-      const int row = m0 + 32 * q + lane;
-      float* crow = out + static_cast<int64_t>(row) * ldo;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        if (nkb > 0) {
-          tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(32 * q) << 16) + c * 32, r);
-          tmem_ld_wait();
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = 0u;
+        // Chunk c-1 is finished once the MMAs of the first blocks of chunk c are queued.
+        if (kb % KC == (kLag < KC ? kLag : KC - 1) && kb / KC >= 1 && drained < kb / KC) {
+          if (!drain(drained)) { ok = false; break; }
+          ++drained;
         }
-        if (row < M) {
-          const int col = n0 + c * 32;
-          if (vec_out && col + 31 < N) {
+      }
+      while (ok && drained < n_chunks) {
+        if (!drain(drained)) { ok = false; break; }
+        ++drained;
+      }
+      if (ok && row < M) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(crow + col + j) =
-                  make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                              __uint_as_float(r[j + 3]));
+        for (int j = 0; j < COLS; j += 32) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = tot[j + i];
+          store_row<32>(crow, n0 + h * COLS + j, N, vec_out, v);
+        }
+      }
+    } else {
+      if (nkb > 0) ok = mbar_wait(acc_bar, 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          if (nkb > 0) {
+            tmem_ld_32x32b_x32(tmem + lane_base + c * 32, r);
+            tmem_ld_wait();
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col + j < N) crow[col + j] = __uint_as_float(r[j]);
+            for (int j = 0; j < 32; ++j) r[j] = 0u;
+          }
+          if (row < M) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            store_row<32>(crow, n0 + c * 32, N, vec_out, v);
           }
         }
       }

@@ -200,8 +200,8 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
   }
   if (requested_split < 0) return TILEC_ERR_BAD_ARG;
   if (variant == TILEC_MM_AUTO) choose_auto(d, A, B, M, N, K, lda, ldb, &variant, &requested_split);
-  if (variant < TILEC_MM_SIMT || variant > TILEC_MM_3XTF32_RAWHI) return TILEC_ERR_BAD_ARG;
-  const bool tensor = variant == TILEC_MM_TF32 || variant == TILEC_MM_3XTF32 || variant == TILEC_MM_3XTF32_RAWHI;
+  if (variant < TILEC_MM_SIMT || variant > TILEC_MM_3XTF32_MASKED) return TILEC_ERR_BAD_ARG;
+  const bool tensor = variant == TILEC_MM_TF32 || variant == TILEC_MM_3XTF32 || variant == TILEC_MM_3XTF32_MASKED;
   if (tensor && !tensor_path_ok(A, B, M, N, K, lda, ldb)) return TILEC_ERR_MISALIGNED;
 
   p->variant = variant;
@@ -228,11 +228,12 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
   return TILEC_OK;
 }
 
+// need_c: tilec_mm_f32 writes C; tilec_mm_plan / tilec_mm_workspace_bytes accept C == NULL.
 int check_args(const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
-               int64_t ldb, int64_t ldc) {
+               int64_t ldb, int64_t ldc, bool need_c = true) {
   if (M < 0 || N < 0 || K < 0) return TILEC_ERR_BAD_ARG;
   if (M == 0 || N == 0) return TILEC_OK;
-  if (C == nullptr || ldc < N) return TILEC_ERR_BAD_ARG;
+  if ((need_c && C == nullptr) || ldc < N) return TILEC_ERR_BAD_ARG;
   if (K > 0 && (A == nullptr || B == nullptr || lda < K || ldb < N)) return TILEC_ERR_BAD_ARG;
   return TILEC_OK;
 }
@@ -264,7 +265,7 @@ int encode_maps(const float* A, const float* B, int64_t M, int64_t N, int64_t K,
     cuuint32_t box[2] = {32, cuuint32_t(bk)};
     cuuint32_t estr[2] = {1, 1};
     if (enc(mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(B), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return TILEC_ERR_BAD_ARG;
   }
@@ -279,7 +280,7 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t 
   const int n_tiles = static_cast<int>(cdiv(N, BN));
   const int group_m = 16;
   dim3 grid(static_cast<unsigned>(int64_t(m_tiles) * n_tiles), 1, static_cast<unsigned>(split));
-  tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI><<<grid, kTcThreads, Cfg::kSmemBytes, s>>>(
+  tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI><<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(
       ma, mb, out, static_cast<int>(M), static_cast<int>(N), ldo, slab, static_cast<int>(K),
       static_cast<int>(k_chunk), m_tiles, n_tiles, group_m, vec_out);
   return launch_status();
@@ -329,7 +330,7 @@ extern "C" {
 int tilec_mm_plan(const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                   int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg, tilec_mm_cfg* out) {
   if (!out) return TILEC_ERR_BAD_ARG;
-  int rc = check_args(A, B, C, M, N, K, lda, ldb, ldc);
+  int rc = check_args(A, B, C, M, N, K, lda, ldb, ldc, /*need_c=*/false);
   if (rc) return rc;
   DeviceInfo* d = nullptr;
   rc = current_device(&d);
@@ -414,9 +415,9 @@ int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
     if (p.variant == TILEC_MM_TF32)
       rc = dispatch_tc_bn<false, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
     else if (p.variant == TILEC_MM_3XTF32)
-      rc = dispatch_tc_bn<true, true>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
-    else
       rc = dispatch_tc_bn<true, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
+    else
+      rc = dispatch_tc_bn<true, true>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
   }
   if (rc) return rc;
   if (p.split > 1) rc = launch_reduce(static_cast<float*>(workspace), C, M, N, p.ldw, ldc, p.split, *d, s);
@@ -427,7 +428,7 @@ int tilec_mm_set_table(const int32_t* rows, int32_t nrows) {
   if (nrows < 0 || (nrows > 0 && rows == nullptr)) return TILEC_ERR_BAD_ARG;
   for (int32_t r = 0; r < nrows; ++r) {
     const int32_t v = rows[r * 8 + 6];
-    if (v < TILEC_MM_SIMT || v > TILEC_MM_3XTF32_RAWHI || rows[r * 8 + 7] < 0) return TILEC_ERR_BAD_ARG;
+    if (v < TILEC_MM_SIMT || v > TILEC_MM_3XTF32_MASKED || rows[r * 8 + 7] < 0) return TILEC_ERR_BAD_ARG;
   }
   std::lock_guard<std::mutex> lk(g_table_mu);
   g_table.assign(rows, rows + size_t(nrows) * 8);

@@ -84,7 +84,7 @@ def _matrix_mul(x1, x2, variant=None, split_k=0, out=None):
     """matrix_mul with explicit kernel choice.
 
     variant: None (= $TILEC_MM_VARIANT or "auto"), "simt", "splitk", "tf32", "3xtf32",
-    "3xtf32_rawhi".  split_k: K slices for split variants (0 = library choice).
+    "3xtf32_masked".  split_k: K slices for split variants (0 = library choice).
     out: optional preallocated [M, N] float32 result (unit column stride).
     """
     M, K = x1.shape
