@@ -1,0 +1,242 @@
+"""Per-shape kernel selection, retrained on B200 (counterpart of tilec/tune.py).
+
+    python -m tilec_b200.tune bench  [--shapes N] [--csv PATH]   sweep shapes x configs, append CSV
+    python -m tilec_b200.tune train  [--csv PATH] [--out PATH]   fit the JSON selection table
+    python -m tilec_b200.tune run    --shape M,K,N [--variant V] [--split S] [--reps R]
+
+``bench`` mirrors tilec/tune.py:68-87: seeded shapes, every candidate config of
+``ext.mm_configs`` timed, resumable (shapes already in the CSV are skipped).  Timing is
+CUDA events around back-to-back launches after warm-up (tilec/tune.py:35-51 used
+perf_counter + synchronize and a median of 5), with the same early abort for configs far
+slower than the best so far.  The shape sampler follows tilec/tune.py:54-65 but spans
+[1, 8192] per dimension and includes M = 1 and N <= 64 cases.
+
+``train`` mirrors tilec/tune.py:99-132: a held-out 20% of shapes measures the geo-mean
+"x of best" of the fitted selector against the library's built-in rules
+(tilec/tune.py:125-128), then the table is refit on all shapes and written as JSON (the
+reference pickles a sklearn model, tune.py:131-132; a JSON table loads without running
+code).  The table maps log2-size boxes to (variant, split_k); see tilec_b200/select.py.
+
+``run`` launches one shape a few times (for profiler captures).
+"""
+import argparse
+import csv
+import json
+import math
+import os
+import random
+import sys
+
+FIELDS = ["device", "M", "K", "N", "variant", "split_k", "ms"]
+DEFAULT_CSV = os.path.join(os.path.dirname(os.path.abspath(__file__)), "mm_bench_b200.csv")
+
+
+def shapes(n=64, seed=4):
+    """Seeded log-uniform (M, K, N) over [1, 8192]^3; first M = 1, second N <= 64."""
+    rng = random.Random(seed)
+    out, seen = [], set()
+    while len(out) < n:
+        m, k, nn = (max(1, round(2 ** rng.uniform(0, 13))) for _ in range(3))
+        if len(out) == 0:
+            m = 1
+        elif len(out) == 1:
+            nn = min(nn, 64)
+        if (m, k, nn) in seen:
+            continue
+        seen.add((m, k, nn))
+        out.append((m, k, nn))
+    return out
+
+
+def time_ms(fn, best=None, reps=None):
+    """Mean CUDA-event time of fn() per call; aborts early when far slower than `best`."""
+    import torch
+    fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    fn()
+    e.record()
+    torch.cuda.synchronize()
+    first = s.elapsed_time(e)
+    if best is not None and first > 2 * best:
+        return first
+    if reps is None:
+        reps = max(3, min(200, int(20.0 / max(first, 1e-3))))
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def load(path=DEFAULT_CSV):
+    with open(path) as f:
+        rows = []
+        for r in csv.DictReader(f):
+            rows.append({"device": r["device"], "M": int(r["M"]), "K": int(r["K"]), "N": int(r["N"]),
+                         "variant": r["variant"], "split_k": int(r["split_k"]), "ms": float(r["ms"])})
+        return rows
+
+
+def bench(n=64, path=DEFAULT_CSV, seed=4):
+    import torch
+    from . import ext
+    dev = torch.cuda.get_device_name()
+    done = {(r["M"], r["K"], r["N"]) for r in load(path)} if os.path.exists(path) else set()
+    new = not os.path.exists(path)
+    with open(path, "a", newline="") as f:
+        w = csv.writer(f)
+        if new:
+            w.writerow(FIELDS)
+        for i, (m, k, nn) in enumerate(shapes(n, seed)):
+            if (m, k, nn) in done:
+                continue
+            g = torch.Generator(device="cuda").manual_seed(i)
+            a = torch.randn(m, k, device="cuda", generator=g)
+            b = torch.randn(k, nn, device="cuda", generator=g)
+            c = torch.empty(m, nn, device="cuda")
+            best = None
+            for v, s in ext.mm_configs(m, k, nn):
+                ms = time_ms(lambda: ext._matrix_mul(a, b, variant=v, split_k=s, out=c), best)
+                best = ms if best is None else min(best, ms)
+                w.writerow([dev, m, k, nn, v, s, f"{ms:.6f}"])
+            f.flush()
+            print(f"{i + 1}/{n}  {m}x{k} @ {k}x{nn}  best {best:.4f} ms", flush=True)
+
+
+def _box(m, k, n):
+    lg = lambda v: max(int(v), 1).bit_length() - 1  # noqa: E731
+    return lg(m), lg(n), lg(k)
+
+
+def fit(rows):
+    """Selection table: one log2 box per measured shape -> its fastest config."""
+    by_shape = {}
+    for r in rows:
+        by_shape.setdefault((r["M"], r["K"], r["N"]), []).append(r)
+    boxes = {}
+    for (m, k, n), rs in by_shape.items():
+        best = min(rs, key=lambda r: r["ms"])
+        boxes.setdefault(_box(m, k, n), []).append(best)
+    table = []
+    for (lm, ln, lk), bests in sorted(boxes.items()):
+        # Several shapes in one box: the config that is fastest most often.
+        votes = {}
+        for b in bests:
+            votes[(b["variant"], b["split_k"])] = votes.get((b["variant"], b["split_k"]), 0) + 1
+        (v, s), _ = max(votes.items(), key=lambda kv: kv[1])
+        table.append([lm, lm + 1, ln, ln + 1, lk, lk + 1, v, s])
+    return table
+
+
+def train(path=DEFAULT_CSV, out=None, test_frac=0.2, seed=0):
+    from . import select
+    rows = load(path)
+    keys = sorted({(r["M"], r["K"], r["N"]) for r in rows})
+    random.Random(seed).shuffle(keys)
+    test = set(keys[: int(len(keys) * test_frac)])
+    table = fit([r for r in rows if (r["M"], r["K"], r["N"]) not in test])
+    by_shape = {}
+    for r in rows:
+        by_shape.setdefault((r["M"], r["K"], r["N"]), []).append(r)
+    ratio_sel, ratio_default, matched = [], [], 0
+    for key in test:
+        rs = by_shape[key]
+        best = min(r["ms"] for r in rs)
+        pick = select.lookup([t[:6] + [_variant_code(t[6]), t[7]] for t in table], *_mnk(key))
+        default = next((r for r in rs if r.get("default")), None) or _default_row(rs)
+        chosen = None
+        if pick is not None:
+            matched += 1
+            chosen = next((r for r in rs if (r["variant"], r["split_k"]) == pick), None)
+        chosen = chosen or default
+        ratio_sel.append(chosen["ms"] / best)
+        ratio_default.append(default["ms"] / best)
+    gm = lambda v: math.exp(sum(math.log(a) for a in v) / max(len(v), 1))  # noqa: E731
+    print(f"held-out shapes: {len(test)} (table matched {matched})")
+    print(f"selector: {gm(ratio_sel):.3f}x of best (geo mean), worst {max(ratio_sel, default=1):.2f}x")
+    print(f"default : {gm(ratio_default):.3f}x of best (geo mean), worst {max(ratio_default, default=1):.2f}x")
+    table = fit(rows)
+    doc = {"device": rows[0]["device"] if rows else "", "source": os.path.basename(path),
+           "shapes": len(keys), "rows": table,
+           "heldout": {"shapes": len(test), "selector_x_of_best": round(gm(ratio_sel), 4),
+                       "default_x_of_best": round(gm(ratio_default), 4)}}
+    out = out or select.TABLE_PATH
+    with open(out, "w") as f:
+        json.dump(doc, f, indent=1)
+    print("wrote", out)
+    return doc
+
+
+def _variant_code(v):
+    from . import _native
+    return _native.VARIANTS[v]
+
+
+def _mnk(key):
+    m, k, n = key
+    return m, n, k
+
+
+def _default_row(rs):
+    """The row the library's built-in rules would launch (split_k 0 = library choice ->
+    recorded as the variant's first candidate)."""
+    from . import _native  # noqa: F401
+    m, k, n = rs[0]["M"], rs[0]["K"], rs[0]["N"]
+    aligned = k % 4 == 0 and n % 4 == 0
+    v = "3xtf32" if aligned and 2.0 * m * n * k >= 1e8 else "simt"
+    cands = [r for r in rs if r["variant"] == v] or rs
+    return min(cands, key=lambda r: r["split_k"])
+
+
+def pick(M, K, N):
+    """(variant, split_k) that matrix_mul launches for an [M,K] x [K,N] product."""
+    import torch
+    from . import ext
+    a = torch.empty(M, K, device="cuda")
+    b = torch.empty(K, N, device="cuda")
+    return ext.plan(a, b)
+
+
+def run(shape, variant="auto", split=0, reps=3, seed=0):
+    import torch
+    from . import ext
+    m, k, n = shape
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = torch.randn(m, k, device="cuda", generator=g)
+    b = torch.randn(k, n, device="cuda", generator=g)
+    c = torch.empty(m, n, device="cuda")
+    for _ in range(reps):
+        ext._matrix_mul(a, b, variant=variant, split_k=split, out=c)
+    torch.cuda.synchronize()
+    print(json.dumps({"shape": [m, k, n], "plan": ext.plan(a, b, variant=variant, split_k=split), "reps": reps}))
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser(prog="python -m tilec_b200.tune")
+    sub = p.add_subparsers(dest="cmd", required=True)
+    pb = sub.add_parser("bench")
+    pb.add_argument("--shapes", type=int, default=64)
+    pb.add_argument("--seed", type=int, default=4)
+    pb.add_argument("--csv", default=DEFAULT_CSV)
+    pt = sub.add_parser("train")
+    pt.add_argument("--csv", default=DEFAULT_CSV)
+    pt.add_argument("--out", default=None)
+    pr = sub.add_parser("run")
+    pr.add_argument("--shape", required=True)
+    pr.add_argument("--variant", default="auto")
+    pr.add_argument("--split", type=int, default=0)
+    pr.add_argument("--reps", type=int, default=3)
+    args = p.parse_args(argv)
+    if args.cmd == "bench":
+        bench(args.shapes, args.csv, args.seed)
+    elif args.cmd == "train":
+        train(args.csv, args.out)
+    else:
+        run(tuple(int(x) for x in args.shape.split(",")), args.variant, args.split, args.reps)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
