@@ -118,6 +118,36 @@ TILEC_API const char* tilec_strerror(int code);
 TILEC_API int tilec_mm_abi_version(void);
 TILEC_API int tilec_mm_built_arch(void);
 
+/* Size of the device-resident scratch behind tilec_mm_f32_splitk_noalloc (per GPU). */
+#define TILEC_MM_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* C = A . B with the SPLITK kernel, for callers that cannot allocate device memory.
+ * No counterpart in the reference (whose op always allocates its result, tilec/ext.py:61).
+ *
+ * Who needs it: a host that binds only this C ABI through an FFI (cgo, JNI, N-API) and
+ * owns no device allocator; a process that reserves all device memory up front and may
+ * not allocate afterwards; code for which cudaMalloc/cudaFree are off limits because
+ * they synchronise the whole device and would stall other streams.  The caller still
+ * provides A, B and C.
+ *
+ * The split-K partial sums live in a fixed array of TILEC_MM_NOALLOC_SCRATCH_BYTES that
+ * the library holds on every GPU it is loaded on until the process exits.  The first call
+ * on a device looks up that array's device address (cudaGetSymbolAddress) with the device
+ * current; make that first call before any stream capture.  Nothing is allocated and
+ * nothing is freed, here or in any later call.
+ *
+ * split_k: number of K slices, or 0 to let the library choose (it then picks at most as
+ * many as fit).  An explicit split_k > 1 whose partial sums need more than
+ * split_k * M * round_up(N, 4) * 4 > TILEC_MM_NOALLOC_SCRATCH_BYTES bytes returns
+ * TILEC_ERR_TOO_LARGE.  Every partial sum the reduction reads is written earlier in the
+ * same call, so the array needs no clearing between calls; but all calls share it, so
+ * calls that may overlap on the GPU (different streams, or different host threads without
+ * ordering) race: serialise them on one stream. */
+TILEC_API int tilec_mm_f32_splitk_noalloc(const float* A, const float* B, float* C,
+                                          int64_t M, int64_t N, int64_t K,
+                                          int64_t lda, int64_t ldb, int64_t ldc,
+                                          int32_t split_k, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

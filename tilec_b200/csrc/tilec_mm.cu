@@ -472,3 +472,98 @@ int tilec_mm_abi_version(void) { return TILEC_MM_ABI_VERSION; }
 int tilec_mm_built_arch(void) { return 100; }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ allocation-free split-K
+// Scratch for tilec_mm_f32_splitk_noalloc: split-K partial-sum slabs, shared by every call
+// on a device.  Host code must not pass the symbol itself to a kernel (on the host it
+// names a host-side stand-in); the device address is looked up once per device below.
+namespace {
+static __device__ __align__(256) float g_noalloc_scratch[TILEC_MM_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+std::once_flag g_noalloc_once[kMaxDevices];
+float* g_noalloc_ptr[kMaxDevices];
+cudaError_t g_noalloc_err[kMaxDevices];
+
+// Device address of g_noalloc_scratch on the current device (set up on first use).
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return TILEC_ERR_NO_DEVICE;
+  }
+  std::call_once(g_noalloc_once[dev], [dev]() {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    g_noalloc_err[dev] = e;
+    g_noalloc_ptr[dev] = e == cudaSuccess ? static_cast<float*>(p) : nullptr;
+    if (e != cudaSuccess) cudaGetLastError();
+  });
+  if (g_noalloc_err[dev] != cudaSuccess || g_noalloc_ptr[dev] == nullptr) return TILEC_ERR_DEVICE;
+  *out = g_noalloc_ptr[dev];
+  return TILEC_OK;
+}
+}  // namespace
+
+extern "C" int tilec_mm_f32_splitk_noalloc(const float* A, const float* B, float* C, int64_t M, int64_t N,
+                                           int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int32_t split_k,
+                                           void* stream) {
+  int rc = check_args(A, B, C, M, N, K, lda, ldb, ldc);
+  if (rc) return rc;
+  if (split_k < 0) return TILEC_ERR_BAD_ARG;
+  if (M == 0 || N == 0) return TILEC_OK;
+  DeviceInfo* d = nullptr;
+  rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0) {
+    int64_t blocks = cdiv(M * N, 256);
+    if (blocks > int64_t(d->sms) * 8) blocks = int64_t(d->sms) * 8;
+    fill_zero_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(C, M, N, ldc);
+    return launch_status();
+  }
+  float* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+
+  const int bn = N <= 64 ? 64 : 128;
+  const int64_t mt = cdiv(M, kSimtBM), nt = cdiv(N, bn);
+  if (nt > 65535) return TILEC_ERR_UNSUPPORTED;
+  const int64_t ldw = round_up(N, 4);
+  const int64_t slab = M * ldw;
+  const int64_t fit = static_cast<int64_t>(TILEC_MM_NOALLOC_SCRATCH_BYTES / sizeof(float)) / slab;
+  int64_t split;
+  if (split_k > 0) {
+    split = split_k > kMaxSplit ? kMaxSplit : split_k;
+    if (split > 1 && split > fit) return TILEC_ERR_TOO_LARGE;
+  } else {
+    split = choose_split(mt * nt, K, kSimtBK, d->sms, 0);
+    if (split > fit) split = fit < 1 ? 1 : fit;
+  }
+  const int64_t k_chunk = round_up(cdiv(K, split), kSimtBK);
+  split = cdiv(K, k_chunk);
+
+  float* out = split > 1 ? scratch : C;
+  const int64_t ldo = split > 1 ? ldw : ldc;
+  const int64_t out_slab = split > 1 ? slab : 0;
+  const int vec_out = split > 1 ? 1 : (aligned16(C) && (ldc % 4 == 0) ? 1 : 0);
+  const bool vec = aligned16(A) && aligned16(B) && (lda % 4 == 0) && (ldb % 4 == 0);
+  dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(split));
+  if (bn == 64) {
+    if (vec)
+      simt_gemm_kernel<64, true><<<grid, kSimtThreads, simt_smem_bytes<64>(), s>>>(A, B, out, M, N, K, lda, ldb,
+                                                                                  ldo, out_slab, k_chunk, vec_out);
+    else
+      simt_gemm_kernel<64, false><<<grid, kSimtThreads, simt_smem_bytes<64>(), s>>>(A, B, out, M, N, K, lda, ldb,
+                                                                                   ldo, out_slab, k_chunk, vec_out);
+  } else {
+    if (vec)
+      simt_gemm_kernel<128, true><<<grid, kSimtThreads, simt_smem_bytes<128>(), s>>>(A, B, out, M, N, K, lda, ldb,
+                                                                                    ldo, out_slab, k_chunk, vec_out);
+    else
+      simt_gemm_kernel<128, false><<<grid, kSimtThreads, simt_smem_bytes<128>(), s>>>(
+          A, B, out, M, N, K, lda, ldb, ldo, out_slab, k_chunk, vec_out);
+  }
+  rc = launch_status();
+  if (rc || split == 1) return rc;
+  return launch_reduce(scratch, C, M, N, ldw, ldc, static_cast<int>(split), *d, s);
+}
