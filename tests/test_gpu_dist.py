@@ -40,6 +40,10 @@ def _worker(rank, world, port, q, M, K, N, panels):
         x2 = x2_full if rank == 0 else None
         c_full = op(x1_full[r0:r1].contiguous(), x2, gather=True, M=M)
         torch.cuda.synchronize()
+        # host-buffer path on the same data must give the same rows
+        h_rows = op.run_host(x1_full[r0:r1].cpu().pin_memory(), x2_full.cpu().pin_memory() if rank == 0 else None,
+                             chunks=3)
+        same = torch.equal(h_rows, c_full[r0:r1].cpu())
         ok = True
         info = ""
         if rank == 0:
@@ -50,6 +54,9 @@ def _worker(rank, world, port, q, M, K, N, panels):
             err_rs = ((c_full.double().sum(1) - rs).norm() / rs.norm()).item()
             ok = err <= 1e-5 and err_rs <= 1e-5 and tuple(c_full.shape) == (M, N)
             info = f"rows relFrob {err:.2e}, checksum {err_rs:.2e}"
+        ok = ok and same
+        if not same:
+            info += " host-path rows differ from device-path rows"
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, ok, info))

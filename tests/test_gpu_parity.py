@@ -46,8 +46,6 @@ def _status_clean():
 @pytest.mark.parametrize("shape", gen.REF_TEST_SHAPES)
 def test_reference_test_shapes(shape, variant):
     m, k, n = shape
-    if variant in TENSOR and not _aligned(k, n):
-        pytest.skip("tensor-core variants need 16-byte aligned rows")
     x1, x2 = gen.randn_inputs(m, k, n, 42)
     got = _run(x1, x2, variant)
     if variant != "tf32":
@@ -65,8 +63,6 @@ GOLDEN_CASES = sorted(k[:-7] for k in GOLDEN.files if k.endswith("_digest"))
 def test_golden_vectors(base, variant):
     tag, shape, s = base.split("_")
     m, k, n = map(int, shape.split("x"))
-    if variant in TENSOR and not _aligned(k, n):
-        pytest.skip("tensor-core variants need 16-byte aligned rows")
     x1, x2 = (gen.randn_inputs if tag == "randn" else gen.exact_inputs)(m, k, n, int(s[1:]))
     assert gen.digest(x1, x2) == str(GOLDEN[base + "_digest"])
     got = _run(x1, x2, variant)
@@ -92,8 +88,6 @@ def _config_inputs(cfg, seed):
 @pytest.mark.parametrize("cfg", [gen.CONFIG1, gen.CONFIG2, gen.CONFIG3], ids=["config1", "config2", "config3"])
 def test_baseline_configs(cfg, variant):
     m, k, n, _ = cfg
-    if variant in TENSOR and not _aligned(k, n):
-        pytest.skip("config 3 rows are not 16-byte aligned")
     x1, x2 = _config_inputs(cfg, 11)
     ref = oracle.mm_tiled(x1.numpy(), x2.numpy()) if m * n * k <= 2 ** 31 else oracle.mm_torch(x1, x2)
     got = _run(x1, x2, variant)
@@ -120,7 +114,7 @@ def test_config4_sweep(shape):
     x1 = torch.randn(m, k, generator=g)
     x2 = torch.randn(k, n, generator=g)
     d1, d2 = x1.to(DEV), x2.to(DEV)
-    variants = ["auto", "simt", "splitk"] + (["3xtf32", "tf32"] if _aligned(k, n) else [])
+    variants = ["auto", "simt", "splitk", "3xtf32", "tf32"]
     for v in variants:
         got = ext._matrix_mul(d1, d2, variant=v).cpu()
         _sampled_check(x1, x2, got, TOL[v])
@@ -151,8 +145,6 @@ def test_forced_split_k(variant, split_k):
 @pytest.mark.parametrize("variant", ALL)
 def test_edge_sizes(variant):
     for (m, k, n) in [(1, 4, 4), (4, 0, 8), (0, 8, 4), (8, 8, 0), (129, 4, 260), (3, 4100, 5 * 4), (300, 8, 1000)]:
-        if variant in TENSOR and not _aligned(k, n):
-            continue
         x1, x2 = gen.exact_inputs(m, k, n, 5)
         got = _run(x1, x2, variant)
         assert got.shape == (m, n)
@@ -192,14 +184,18 @@ def test_deterministic(variant):
     assert torch.equal(a, b)
 
 
-def test_misaligned_tensor_variant_is_an_error():
-    x1 = torch.randn(64, 30, device=DEV)
-    x2 = torch.randn(30, 64, device=DEV)
-    with pytest.raises(TilecError, match="MISALIGNED"):
-        ext._matrix_mul(x1, x2, variant="3xtf32")
-    # AUTO picks a kernel that handles it
-    got = ext.matrix_mul(x1, x2).cpu().numpy()
-    assert oracle.rel_frob(got, oracle.mm_tiled(x1.cpu().numpy(), x2.cpu().numpy())) <= 1e-5
+def test_misaligned_rows_are_packed_for_tensor_cores():
+    """Rows that are not 16-byte aligned (K, N not multiples of 4, or an odd view offset)
+    are packed into an aligned workspace copy so the TMA/tensor-core path still applies."""
+    g = torch.Generator(device=DEV).manual_seed(2)
+    base = torch.randn(300 * 1001 + 1, device=DEV, generator=g)
+    x1 = base[1:].view(300, 1001)[:, :999]        # odd offset and odd row stride
+    x2 = torch.randn(999, 333, device=DEV, generator=g)
+    ref = oracle.mm_tiled(x1.contiguous().cpu().numpy(), x2.cpu().numpy())
+    for v in ("3xtf32", "tf32", "3xtf32_masked", "auto"):
+        got = ext._matrix_mul(x1, x2, variant=v).cpu().numpy()
+        assert oracle.rel_frob(got, ref) <= TOL[v], v
+    assert ext.plan(torch.empty(1000, 3001, device=DEV), torch.empty(3001, 777, device=DEV))[0] == "3xtf32"
 
 
 def test_plan_and_status():
@@ -231,3 +227,16 @@ def test_3xtf32_error_flat_in_k(k):
         got = ext._matrix_mul(a, b, variant=v, split_k=1)
         err = ((got.double() - ref).norm() / ref.norm()).item()
         assert err <= 1e-5, f"{v} K={k}: relFrob {err:.3e}"
+
+
+@pytest.mark.parametrize("chunks", (1, 3, 8))
+def test_matrix_mul_host_pipelined(chunks):
+    """Host-buffer API: row chunks stream H2D -> GEMM -> D2H on overlapping streams."""
+    g = torch.Generator().manual_seed(chunks)
+    x1 = torch.randn(1000, 3001, generator=g).pin_memory()
+    x2 = torch.randn(3001, 777, generator=g).pin_memory()
+    out = ext.matrix_mul_host(x1, x2, chunks=chunks)
+    assert out.device.type == "cpu" and out.shape == (1000, 777)
+    assert oracle.rel_frob(out.numpy(), oracle.mm_tiled(x1.numpy(), x2.numpy())) <= 1e-5
+    with pytest.raises(ValueError, match="host tensors"):
+        ext.matrix_mul_host(x1.to(DEV), x2)

@@ -126,6 +126,10 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
 
+// Workspace layout (each region 256-byte aligned):
+//   [packed A: M x round_up(K,4)] [packed B: K x round_up(N,4)] [split-K slabs: split x M x round_up(N,4)]
+// Packed copies exist only for operands whose rows are not 16-byte aligned and only on
+// the tensor-core path (TMA needs 16-byte aligned bases and row strides).
 struct Plan {
   int variant = TILEC_MM_SIMT;
   int split = 1;
@@ -133,12 +137,22 @@ struct Plan {
   int bn = 128;
   size_t ws_bytes = 0;
   int64_t ldw = 0;
+  bool pack_a = false, pack_b = false;
+  size_t off_a = 0, off_b = 0, off_slabs = 0;
 };
 
-bool tensor_path_ok(const float* A, const float* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb) {
+inline bool rows_aligned(const float* X, int64_t ld) { return aligned16(X) && (ld % 4 == 0); }
+
+bool tensor_dims_ok(int64_t M, int64_t N, int64_t K) {
   const int64_t lim = (int64_t(1) << 31) - 256;
-  return aligned16(A) && aligned16(B) && (lda % 4 == 0) && (ldb % 4 == 0) && M < lim && N < lim && K < lim;
+  return M < lim && N < lim && K < lim;
 }
+
+bool tensor_path_ok(const float* A, const float* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb) {
+  return rows_aligned(A, lda) && rows_aligned(B, ldb) && tensor_dims_ok(M, N, K);
+}
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 int ilog2_floor(int64_t v) {
   int r = 0;
@@ -157,8 +171,8 @@ void choose_auto(const DeviceInfo& d, const float* A, const float* B, int64_t M,
         const int32_t* t = &g_table[r];
         if (lm >= t[0] && lm < t[1] && ln >= t[2] && ln < t[3] && lk2 >= t[4] && lk2 < t[5]) {
           int v = t[6];
-          if ((v == TILEC_MM_TF32 || v == TILEC_MM_3XTF32) && !tensor_path_ok(A, B, M, N, K, lda, ldb))
-            v = TILEC_MM_SIMT;
+          const bool tc = v == TILEC_MM_TF32 || v == TILEC_MM_3XTF32 || v == TILEC_MM_3XTF32_MASKED;
+          if (tc && !tensor_dims_ok(M, N, K)) v = TILEC_MM_SIMT;
           *variant = v;
           *split = t[7];
           return;
@@ -169,7 +183,10 @@ void choose_auto(const DeviceInfo& d, const float* A, const float* B, int64_t M,
   (void)d;
   *split = 0;
   const double flops = 2.0 * double(M) * double(N) * double(K);
-  if (tensor_path_ok(A, B, M, N, K, lda, ldb) && flops >= 1.0e8) {
+  const bool aligned = tensor_path_ok(A, B, M, N, K, lda, ldb);
+  // Misaligned operands are packed first (2 x (MK + KN) x 4 bytes of traffic): worth it
+  // once the product is large enough for the tensor cores to win by a wide margin.
+  if (tensor_dims_ok(M, N, K) && flops >= (aligned ? 1.0e8 : 5.0e8)) {
     *variant = TILEC_MM_3XTF32;
     return;
   }
@@ -177,15 +194,31 @@ void choose_auto(const DeviceInfo& d, const float* A, const float* B, int64_t M,
   *variant = (tiles < d.sms && K >= 1024) ? TILEC_MM_SPLITK : TILEC_MM_SIMT;
 }
 
-int choose_split(int64_t tiles, int64_t K, int bk, int sms, int requested) {
+// K slices for a grid of `tiles` output tiles: minimise (waves of CTAs) / slices, i.e. the
+// time of one full-K tile divided across slices, plus the reduction's traffic (each slice
+// writes and the reduction reads an M x N slab) and a fixed cost for its extra launch.
+// flops_per_sm: sustained useful FLOP/s of one SM on this kernel.
+int choose_split(int64_t tiles, int64_t M, int64_t N, int64_t K, int bm, int bn, int bk, int sms, int requested,
+                 double flops_per_sm) {
   if (requested > 0) return requested > kMaxSplit ? kMaxSplit : requested;
   if (tiles >= sms) return 1;
-  int64_t s = cdiv(2 * int64_t(sms), tiles);
-  const int64_t max_by_k = K / (int64_t(bk) * 8);  // keep >= 8 K-steps per slice
-  if (s > max_by_k) s = max_by_k;
-  if (s > kMaxSplit) s = kMaxSplit;
-  if (s < 1) s = 1;
-  return static_cast<int>(s);
+  int64_t smax = K / (int64_t(bk) * 8);  // keep >= 8 K-steps per slice
+  if (smax > kMaxSplit) smax = kMaxSplit;
+  if (smax < 1) smax = 1;
+  const double tile_s = 2.0 * bm * bn * double(K) / flops_per_sm;  // one full-K tile on one SM
+  const double hbm = 6.0e12;                                          // bytes/s, reduction traffic
+  int best = 1;
+  double best_cost = 1e30;
+  for (int64_t s = 1; s <= smax; ++s) {
+    const double waves = double(cdiv(tiles * s, sms));
+    double cost = waves * tile_s / double(s);
+    if (s > 1) cost += double(s) * double(M) * double(round_up(N, 4)) * 8.0 / hbm + 3.0e-6;
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = static_cast<int>(s);
+    }
+  }
+  return best;
 }
 
 int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K,
@@ -202,14 +235,19 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
   if (variant == TILEC_MM_AUTO) choose_auto(d, A, B, M, N, K, lda, ldb, &variant, &requested_split);
   if (variant < TILEC_MM_SIMT || variant > TILEC_MM_3XTF32_MASKED) return TILEC_ERR_BAD_ARG;
   const bool tensor = variant == TILEC_MM_TF32 || variant == TILEC_MM_3XTF32 || variant == TILEC_MM_3XTF32_MASKED;
-  if (tensor && !tensor_path_ok(A, B, M, N, K, lda, ldb)) return TILEC_ERR_MISALIGNED;
+  if (tensor && !tensor_dims_ok(M, N, K)) return TILEC_ERR_UNSUPPORTED;
+  if (tensor) {
+    p->pack_a = !rows_aligned(A, lda);
+    p->pack_b = !rows_aligned(B, ldb);
+  }
 
   p->variant = variant;
   if (tensor) {
     p->bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
     const int bk = variant == TILEC_MM_TF32 ? 32 : 16;
     const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
-    p->split = choose_split(tiles, K, bk, d.sms, requested_split);
+    p->split = choose_split(tiles, M, N, K, kTcBM, p->bn, bk, d.sms, requested_split,
+                            variant == TILEC_MM_TF32 ? 4.0e12 : 1.4e12);
     p->k_chunk = round_up(cdiv(K, p->split), bk);
     p->split = static_cast<int>(cdiv(K, p->k_chunk > 0 ? p->k_chunk : 1));
     if (p->split < 1) p->split = 1;
@@ -217,14 +255,26 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
     p->bn = N <= 64 ? 64 : 128;
     const int64_t tiles = cdiv(M, kSimtBM) * cdiv(N, p->bn);
     int split = 1;
-    if (variant == TILEC_MM_SPLITK) split = choose_split(tiles, K, kSimtBK, d.sms, requested_split);
+    if (variant == TILEC_MM_SPLITK)
+      split = choose_split(tiles, M, N, K, kSimtBM, p->bn, kSimtBK, d.sms, requested_split, 0.3e12);
     p->k_chunk = round_up(cdiv(K, split), kSimtBK);
     split = static_cast<int>(cdiv(K, p->k_chunk > 0 ? p->k_chunk : 1));
     p->split = split < 1 ? 1 : split;
   }
   if (p->k_chunk <= 0) p->k_chunk = 16;
   p->ldw = round_up(N, 4);
-  p->ws_bytes = p->split > 1 ? size_t(p->split) * size_t(M) * size_t(p->ldw) * sizeof(float) : 0;
+  size_t off = 0;
+  if (p->pack_a) {
+    p->off_a = off;
+    off += align256(size_t(M) * size_t(round_up(K, 4)) * sizeof(float));
+  }
+  if (p->pack_b) {
+    p->off_b = off;
+    off += align256(size_t(K) * size_t(round_up(N, 4)) * sizeof(float));
+  }
+  p->off_slabs = off;
+  if (p->split > 1) off += size_t(p->split) * size_t(M) * size_t(p->ldw) * sizeof(float);
+  p->ws_bytes = off;
   return TILEC_OK;
 }
 
@@ -307,6 +357,25 @@ int dispatch_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, float* 
   }
 }
 
+// dst[r, 0:cols] = src[r, 0:cols] with row strides lds / ldd (one CTA per row, grid-stride).
+__global__ void __launch_bounds__(256) pack_rows_kernel(const float* __restrict__ src, int64_t lds,
+                                                        float* __restrict__ dst, int64_t ldd, int64_t rows,
+                                                        int64_t cols) {
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* s = src + r * lds;
+    float* d = dst + r * ldd;
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) d[c] = s[c];
+  }
+}
+
+int launch_pack(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows, int64_t cols,
+                const DeviceInfo& d, cudaStream_t s) {
+  int64_t blocks = rows < int64_t(d.sms) * 16 ? rows : int64_t(d.sms) * 16;
+  if (blocks < 1) blocks = 1;
+  pack_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(src, lds, dst, ldd, rows, cols);
+  return launch_status();
+}
+
 int launch_reduce(const float* ws, float* C, int64_t M, int64_t N, int64_t ldw, int64_t ldc, int split,
                   const DeviceInfo& d, cudaStream_t s) {
   const int64_t groups = M * cdiv(N, 4);
@@ -378,10 +447,27 @@ int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
   Plan p;
   rc = make_plan(*d, A, B, C, M, N, K, lda, ldb, ldc, cfg, &p);
   if (rc) return rc;
-  if (p.split > 1) {
-    if (!workspace || ws_bytes < p.ws_bytes || !aligned16(workspace)) return TILEC_ERR_WORKSPACE;
+  if (p.ws_bytes > 0) {
+    if (!workspace || ws_bytes < p.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+      return TILEC_ERR_WORKSPACE;
   }
-  float* out = p.split > 1 ? static_cast<float*>(workspace) : C;
+  uint8_t* wsb = static_cast<uint8_t*>(workspace);
+  if (p.pack_a) {
+    float* pa = reinterpret_cast<float*>(wsb + p.off_a);
+    rc = launch_pack(A, lda, pa, round_up(K, 4), M, K, *d, s);
+    if (rc) return rc;
+    A = pa;
+    lda = round_up(K, 4);
+  }
+  if (p.pack_b) {
+    float* pb = reinterpret_cast<float*>(wsb + p.off_b);
+    rc = launch_pack(B, ldb, pb, round_up(N, 4), K, N, *d, s);
+    if (rc) return rc;
+    B = pb;
+    ldb = round_up(N, 4);
+  }
+  float* slabs = reinterpret_cast<float*>(wsb + p.off_slabs);
+  float* out = p.split > 1 ? slabs : C;
   const int64_t ldo = p.split > 1 ? p.ldw : ldc;
   const int64_t slab = p.split > 1 ? M * p.ldw : 0;
   const int vec_out = p.split > 1 ? 1 : (aligned16(C) && (ldc % 4 == 0) ? 1 : 0);
@@ -420,7 +506,7 @@ int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
       rc = dispatch_tc_bn<true, true>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
   }
   if (rc) return rc;
-  if (p.split > 1) rc = launch_reduce(static_cast<float*>(workspace), C, M, N, p.ldw, ldc, p.split, *d, s);
+  if (p.split > 1) rc = launch_reduce(slabs, C, M, N, p.ldw, ldc, p.split, *d, s);
   return rc;
 }
 
@@ -536,7 +622,7 @@ extern "C" int tilec_mm_f32_splitk_noalloc(const float* A, const float* B, float
     split = split_k > kMaxSplit ? kMaxSplit : split_k;
     if (split > 1 && split > fit) return TILEC_ERR_TOO_LARGE;
   } else {
-    split = choose_split(mt * nt, K, kSimtBK, d->sms, 0);
+    split = choose_split(mt * nt, M, N, K, kSimtBM, bn, kSimtBK, d->sms, 0, 0.3e12);
     if (split > fit) split = fit < 1 ? 1 : fit;
   }
   const int64_t k_chunk = round_up(cdiv(K, split), kSimtBK);

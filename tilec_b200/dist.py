@@ -121,6 +121,39 @@ class RowShardedMatmul:
             return gather_rows(out, M, self.group)
         return out
 
+    def run_host(self, h_x1_shard, h_x2=None, h_out=None, chunks=4, sync=True):
+        """Host-buffer variant: x2 (rank src) and this rank's rows of x1 come from host memory
+        and this rank's rows of C go back to it.  x2 is copied to the device and broadcast in
+        panels first; then row chunks of x1 stream through H2D -> GEMM (all panels) -> D2H
+        with the three overlapping (tilec_b200.ext.pipelined_rows)."""
+        from . import ext
+        rows = h_x1_shard.shape[0]
+        if h_out is None:
+            h_out = torch.empty(rows, self.N, dtype=torch.float32, pin_memory=True)
+        dev = self.device
+        with torch.cuda.device(dev):
+            d_x2 = None
+            if self.rank == self.src:
+                d_x2 = torch.empty(self.K, self.N, dtype=torch.float32, device=dev)
+                d_x2.copy_(h_x2, non_blocking=True)
+            if self.world == 1:
+                ext.pipelined_rows(h_x1_shard, h_out, dev, lambda a, c: ext._matrix_mul(a, d_x2, out=c),
+                                   chunks=chunks, sync=sync)
+                return h_out
+            if self.rank == self.src:
+                pack_panels(d_x2, self.bounds, self.bufs)
+            works = broadcast_panels(self.bufs, self.src, self.group)
+
+            def waited():
+                for w in works:
+                    w.wait()
+
+            def compute(a, c):
+                for (n0, n1), buf in zip(self.bounds, self.bufs):
+                    ext._matrix_mul(a, buf, out=c[:, n0:n1])
+            ext.pipelined_rows(h_x1_shard, h_out, dev, compute, chunks=chunks, before=waited, sync=sync)
+        return h_out
+
 
 def matrix_mul_rowsharded(x1_shard, x2, group=None, src=0, gather=False, M=None, panels=2):
     """One-shot row-sharded matrix_mul (allocates panel buffers per call)."""

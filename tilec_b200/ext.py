@@ -137,19 +137,100 @@ def mm_configs(M, K, N):
     """Candidate (variant, split_k) launch configs for an [M,K]x[K,N] product.
 
     B200 counterpart of the reference's config space (tilec/ext.py:48-51), which the
-    tuner sweeps (tilec/tune.py:82).  Tensor-core variants need 16-byte aligned rows
-    (K and N multiples of 4 for contiguous operands).
+    tuner sweeps (tilec/tune.py:82).  Tensor-core variants pack operands whose rows are
+    not 16-byte aligned into an aligned workspace copy first.
     """
     out = [("simt", 1)]
-    tiles = cdiv(M, 128) * cdiv(N, 128)
-    for s in (2, 4, 8, 16, 32):
-        if K >= s * 128 and tiles < 4 * 148:
+    tiles = cdiv(M, 128) * cdiv(N, 128 if N > 64 else 64)
+    for s in (2, 4, 8, 16, 32, 64):
+        if K >= s * 128 and tiles * s <= 4 * 148:
             out.append(("splitk", s))
-    if K % 4 == 0 and N % 4 == 0:
-        for v in ("3xtf32", "tf32"):
-            out.append((v, 1))
-            tiles_tc = cdiv(M, 128) * cdiv(N, 256 if N > 128 else (128 if N > 64 else 64))
-            for s in (2, 4, 8, 16, 32):
-                if K >= s * 256 and tiles_tc < 2 * 148:
-                    out.append((v, s))
+    tiles_tc = cdiv(M, 128) * cdiv(N, 256 if N > 128 else (128 if N > 64 else 64))
+    for v in ("3xtf32", "tf32"):
+        out.append((v, 1))
+        for s in (2, 4, 8, 16, 32, 64):
+            if K >= s * 128 and tiles_tc * s <= 2 * 148:
+                out.append((v, s))
+    return out
+
+
+_SIDE_STREAMS = {}
+
+
+def _side_streams(dev):
+    """(h2d, d2h) copy streams of a device, created once."""
+    if dev not in _SIDE_STREAMS:
+        _SIDE_STREAMS[dev] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return _SIDE_STREAMS[dev]
+
+
+def _row_chunks(M, chunks, align=128):
+    chunks = max(1, min(int(chunks), max(1, M // align)))
+    step = -(-M // chunks)
+    step = -(-step // align) * align
+    return [(r, min(M, r + step)) for r in range(0, M, step)]
+
+
+def pipelined_rows(h_x1, h_out, dev, compute, chunks=8, before=None, sync=True):
+    """Stream host rows through the GPU: H2D of chunk i+1, compute(chunk i) and D2H of
+    chunk i-1 overlap on three streams (copies on two side streams, compute on the current
+    stream).  compute(d_x1_rows, d_out_rows) launches the work for one chunk of rows;
+    before() (optional) runs on the current stream first (e.g. staging x2)."""
+    M, K = h_x1.shape
+    N = h_out.shape[1]
+    cur = torch.cuda.current_stream(dev)
+    h2d, d2h = _side_streams(dev)
+    d_x1 = torch.empty(M, K, dtype=torch.float32, device=dev)
+    d_out = torch.empty(M, N, dtype=torch.float32, device=dev)
+    h2d.wait_stream(cur)
+    d2h.wait_stream(cur)
+    spans = _row_chunks(M, chunks)
+    ev_in = []
+    with torch.cuda.stream(h2d):
+        for r0, r1 in spans:
+            d_x1[r0:r1].copy_(h_x1[r0:r1], non_blocking=True)
+            ev_in.append(h2d.record_event())
+    if before is not None:
+        before()
+    for (r0, r1), e in zip(spans, ev_in):
+        cur.wait_event(e)
+        compute(d_x1[r0:r1], d_out[r0:r1])
+        d2h.wait_event(cur.record_event())
+        with torch.cuda.stream(d2h):
+            h_out[r0:r1].copy_(d_out[r0:r1], non_blocking=True)
+    d_x1.record_stream(h2d)
+    d_out.record_stream(d2h)
+    cur.wait_stream(d2h)
+    if sync:
+        cur.synchronize()
+    return h_out
+
+
+def matrix_mul_host(x1, x2, out=None, chunks=8, device=None, sync=True):
+    """C = x1 @ x2 for float32 tensors in host memory, computed on the GPU.
+
+    The same product as matrix_mul, for data that lives on the host: x2 is copied once,
+    then row chunks of x1 are copied in, multiplied and copied back with the three
+    overlapping (use pinned tensors for asynchronous copies).  Returns `out` (a new pinned
+    [M, N] tensor by default), complete when the call returns (sync=True) or once the
+    current stream is synchronised (sync=False).
+    """
+    M, K = x1.shape
+    K2, N = x2.shape
+    if K != K2:
+        raise ValueError(f"matrix_mul: shapes {tuple(x1.shape)} and {tuple(x2.shape)} don't match")
+    _check_operand(x1)
+    _check_operand(x2)
+    if x1.device.type != "cpu" or x2.device.type != "cpu":
+        raise ValueError("matrix_mul_host: x1 and x2 must be host tensors (use matrix_mul for CUDA tensors)")
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32, pin_memory=True)
+    if M == 0 or N == 0:
+        return out
+    x1 = x1.contiguous()
+    with torch.cuda.device(dev):
+        d_x2 = torch.empty(K, N, dtype=torch.float32, device=dev)
+        d_x2.copy_(x2.contiguous(), non_blocking=True)
+        pipelined_rows(x1, out, dev, lambda a, c: _matrix_mul(a, d_x2, out=c), chunks=chunks, sync=sync)
     return out
