@@ -254,7 +254,21 @@ def extra_configs(pk):
             i[0] += 1
             ext._matrix_mul(a, b, out=c)
         reps = max(20, min(400, int(2e11 / (2 * m * n * k))))
-        ms = time_launches(step, reps)
+        ms_eager = time_launches(step, reps)
+        # Device time per launch: a CUDA graph of one launch per input set, replayed.
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(copies):
+                step()
+        replays = max(3, -(-reps // copies))
+        ms = time_launches(graph.replay, replays, warm=2) / copies
         flops = 2.0 * m * n * k
         tfl = flops / (ms * 1e-3) / 1e12
         peak, note = variant_peak(variant, pk, sustained=False)
@@ -265,7 +279,11 @@ def extra_configs(pk):
                      "roofline_frac": round(tfl / roof, 4),
                      "bound": "hbm" if bw_bound < peak else ("tensor" if "tf32" in variant else "fp32"),
                      "peak_note": note, "l2": f"rotating {copies} input sets ({copies * per / 2**20:.0f} MiB > L2)",
-                     "timing": f"mean of {reps} back-to-back launches, CUDA events, incl. host launch path"}
+                     "timing": f"CUDA graph of {copies} launches (one per input set) replayed {replays}x, CUDA "
+                               "events; device time per launch incl. inter-kernel gaps",
+                     "ms_eager": round(ms_eager, 5),
+                     "eager_timing": f"mean of {reps} back-to-back Python calls (host launch path included)"}
+        del graph
         del xs
         torch.cuda.empty_cache()
     return out
@@ -425,7 +443,8 @@ def main():
             "roofline": {"bound": "tensor" if "tf32" in variant else "fp32", "achieved": round(achieved, 2),
                          "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "algorithmic_bytes": int(bytes_launch),
-                         "kernel": f"tc_gemm ({variant}) on [{rows},{K5}] @ [{K5},{panel_w}]",
+                         "kernel": (f"{'tc2_gemm (CTA pair)' if variant.startswith('3xtf32') and rows >= 256 and panel_w > 128 else 'tc_gemm'}"
+                                    f" ({variant}) on [{rows},{K5}] @ [{K5},{panel_w}]"),
                          "launch_ms": round(gemm_ms_max, 4), "peak_note": peak_note + " (of measured)"
                          if pk["src"] == "measured" else peak_note},
             "cpu_baseline": cpu,

@@ -95,7 +95,19 @@ def check(code, where):
         raise TilecError(code, where)
 
 
+_CFG_CACHE = {}
+
+
 def make_cfg(variant="auto", split_k=0):
+    key = (variant, split_k)
+    cfg = _CFG_CACHE.get(key)
+    if cfg is None:
+        cfg = _make_cfg(variant, split_k)
+        _CFG_CACHE[key] = cfg
+    return cfg
+
+
+def _make_cfg(variant, split_k):
     if isinstance(variant, str):
         try:
             v = VARIANTS[variant.lower()]

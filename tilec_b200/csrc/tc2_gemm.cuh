@@ -1,0 +1,325 @@
+// tc2_gemm.cuh -- 3XTF32 GEMM on a CTA pair (tcgen05 cta_group::2), sm_100a.
+//
+// Same contraction and edge semantics as tc_gemm.cuh (tilec/ext.py:13-24: zero-filled
+// out-of-range operands, masked stores), same hi/lo split and K-chunk promotion; the
+// difference is the MMA shape.  Two CTAs of a cluster (2,1,1) own a 256 x BN output tile:
+// CTA r holds A rows [128r, 128r+128) and the BN/2 columns [r*BN/2, (r+1)*BN/2) of B, and
+// the leader (r = 0) issues tcgen05.mma.cta_group::2 with M = 256, N = BN, which reads A
+// and B from both CTAs' shared memory and writes each CTA's 128 rows of the accumulator
+// into that CTA's TMEM.  Per SM the tensor core then reads 8 KB of operands per K=8 step
+// instead of 12 KB (1-CTA M=128 x N=256), which is what keeps the shared-memory port
+// (TMA writes + split stage + MMA operand reads) below its bandwidth.
+//
+// Data movement stays local: each CTA TMA-loads only its own halves into its own shared
+// memory with its own mbarriers (plain cta_group::1 TMA, no multicast).  Cross-CTA
+// signalling:
+//   split[s]      (leader)  <- 8 split warps of each CTA, remote mbarrier arrive (release.cluster)
+//   empty[s]      (each)    <- leader's tcgen05.commit, once to its own, once to the peer's barrier
+//   chunk_full[b] (each)    <- leader's tcgen05.commit, both CTAs
+//   chunk_empty[b](leader)  <- 8 epilogue warps of each CTA after draining their TMEM rows
+// TMEM is allocated and freed by warp 1 of both CTAs together (cta_group::2).  A cluster
+// barrier after set-up and another before teardown keep either CTA from touching the
+// peer's barriers before they exist or after they are gone.
+#pragma once
+
+#include "common.cuh"
+#include "tc_gemm.cuh"
+
+// How the split warps and the epilogue warps signal the leader CTA:
+//   1 (default) remote mbarrier arrive with release at CTA scope, after
+//     fence.proxy.async.shared::cta has made the warp's shared-memory writes visible to the
+//     async proxy (the tensor core reads them only after the leader observes the arrive);
+//   0 the same arrive with release at cluster scope (a cluster memory barrier per warp and
+//     stage: measured 147 vs 245 TFLOP/s at 8192^3);
+//   2 eight local arrives, then one cluster-scope release per stage (139 TFLOP/s).
+#ifndef TILEC_PAIR_SIGNAL
+#define TILEC_PAIR_SIGNAL 1
+#endif
+
+namespace tilec {
+
+template <int BN, int STAGES>
+struct Tc2Cfg {
+  static constexpr int BK = 16;
+  static constexpr int kBNHalf = BN / 2;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kABytes = 128 * BK * 4;          // own A rows
+  static constexpr int kBBytes = BK * kBNHalf * 4;      // own half of B
+  static constexpr int kStageBytes = 2 * (kABytes + kBBytes);  // raw + lo
+  static constexpr int kTxBytes = kABytes + kBBytes;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + 1024 + 1024;
+  static constexpr uint32_t kASbo = 512u;               // 8 rows x 64 B (64B swizzle)
+  static constexpr uint32_t kBLbo = BK * 128u;          // stride between 32-column slabs
+  static constexpr uint32_t kBSbo = 512u;               // stride between 4-row K groups
+  static constexpr uint32_t kTmemCols = 2 * BN;         // two chunk buffers of BN columns
+  static constexpr int kColsPerThread = BN / 2;
+  static constexpr int kChunkBlocks = 8;
+  static_assert(BN == 256 || BN == 128, "BN");
+  static_assert(kSmemBytes <= 232448, "shared memory");
+};
+
+// M = 256 (pair), N = BN, kind::tf32, A K-major, B MN-major.
+template <int BN, int STAGES, bool HI_EXPLICIT>
+__global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
+    tc2_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    float* __restrict__ out, int M, int N, int64_t ldo, int64_t out_slab, int K, int k_chunk,
+                    int mp_tiles, int n_tiles, int group_m, int vec_out) {
+  using Cfg = Tc2Cfg<BN, STAGES>;
+  constexpr int BK = Cfg::BK;
+  constexpr int KC = Cfg::kChunkBlocks;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  auto a_raw = [&](int s) { return smem + s * Cfg::kStageBytes; };
+  auto b_raw = [&](int s) { return smem + s * Cfg::kStageBytes + Cfg::kABytes; };
+  auto a_lo = [&](int s) { return smem + s * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes; };
+  auto b_lo = [&](int s) { return smem + s * Cfg::kStageBytes + 2 * Cfg::kABytes + Cfg::kBBytes; };
+
+  uint8_t* bar_area = smem + STAGES * Cfg::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
+  uint64_t* empty = full + STAGES;
+  uint64_t* split = empty + STAGES;
+  uint64_t* chunk_full = split + STAGES;
+  uint64_t* chunk_empty = chunk_full + 2;
+  uint64_t* drain_bar = chunk_empty + 2;
+  uint64_t* split_local = drain_bar + 1;   // [STAGES] split warps of this CTA -> publishing warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(split_local + STAGES);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (blockDim.x != Cfg::kThreads) {  // uniform across the cluster: every CTA returns
+    if (threadIdx.x == 0) record_status(TILEC_DEV_BAD_LAUNCH);
+    return;
+  }
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  // Grouped raster over pair tiles (256 x BN).
+  const int tile = blockIdx.x >> 1;
+  const int band = tile / (group_m * n_tiles);
+  const int first_m = band * group_m;
+  const int band_rows = min(group_m, mp_tiles - first_m);
+  const int in_band = tile - band * group_m * n_tiles;
+  const int tile_m = first_m + in_band % band_rows;
+  const int tile_n = in_band / band_rows;
+  const int m0 = tile_m * 256 + static_cast<int>(rank) * 128;  // this CTA's rows
+  const int n0 = tile_n * BN;                                   // the pair's columns
+  const int nb0 = n0 + static_cast<int>(rank) * Cfg::kBNHalf;   // this CTA's B columns
+
+  const int k_begin = blockIdx.z * k_chunk;
+  const int k_end = min(K, k_begin + k_chunk);
+  const int nkb = k_end > k_begin ? (k_end - k_begin + BK - 1) / BK : 0;
+  const int n_chunks = (nkb + KC - 1) / KC;
+  out += static_cast<int64_t>(blockIdx.z) * out_slab;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&split[s], TILEC_PAIR_SIGNAL == 2 ? 2 : 2 * Cfg::kEpiWarps);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&chunk_full[b], 1);
+      mbar_init(&chunk_empty[b], 2 * Cfg::kEpiWarps);
+    }
+    mbar_init(drain_bar, 1);
+    for (int st = 0; st < STAGES; ++st) mbar_init(&split_local[st], Cfg::kEpiWarps);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  __syncwarp();
+  cluster_sync();  // both CTAs' barriers exist before anyone arrives remotely
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait_cluster(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&full[s], Cfg::kTxBytes);
+        const int k0 = k_begin + kb * BK;
+        tma_load_2d(a_raw(s), &tmA, &full[s], k0, m0);
+#pragma unroll
+        for (int j = 0; j < Cfg::kBNHalf / 32; ++j)
+          tma_load_2d(b_raw(s) + j * BK * 128, &tmB, &full[s], nb0 + 32 * j, k0);
+        ++issued;
+      }
+      if (ok) {
+        // Producer tail: wait for the release (leader's commit) of each of the last fills,
+        // so no arrival targets this CTA's barriers after it exits.
+        for (int kb = nkb - STAGES < 0 ? 0 : nkb - STAGES; kb < nkb; ++kb)
+          if (!mbar_wait_cluster(&empty[kb % STAGES], (kb / STAGES) & 1, abort_flag)) break;
+      } else {
+        for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb)
+          mbar_drain(&full[kb % STAGES], (kb / STAGES) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA only)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = make_idesc_tf32(256, BN);
+      const uint32_t peer = 1u;
+      bool ok = true;
+      for (int kb = 0; kb < nkb && ok; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        const int chunk = kb / KC;
+        const bool chunk_start = (kb % KC == 0);
+        const uint32_t dcol = static_cast<uint32_t>((chunk & 1) * BN);
+        if (chunk_start && chunk >= 2) {
+          if (!mbar_wait_cluster(&chunk_empty[chunk & 1], ((chunk >> 1) - 1) & 1, abort_flag)) { ok = false; break; }
+        }
+        if (!mbar_wait_cluster(&split[s], ph, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_hi = smem_u32(a_raw(s)), b_hi = smem_u32(b_raw(s));
+        const uint32_t a_l = smem_u32(a_lo(s)), b_l = smem_u32(b_lo(s));
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          const uint64_t ad = make_smem_desc(a_hi + kk * 32, 16, Cfg::kASbo, kLayoutSw64);
+          const uint64_t bd = make_smem_desc(b_hi + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
+          const uint64_t adl = make_smem_desc(a_l + kk * 32, 16, Cfg::kASbo, kLayoutSw64);
+          const uint64_t bdl = make_smem_desc(b_l + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
+          const uint32_t accum = (chunk_start && kk == 0) ? 0u : 1u;
+          umma_tf32_pair(tmem + dcol, adl, bd, idesc, accum);  // small terms first
+          umma_tf32_pair(tmem + dcol, ad, bdl, idesc, 1u);
+          umma_tf32_pair(tmem + dcol, ad, bd, idesc, 1u);
+        }
+        const uint32_t e_local = smem_u32(&empty[s]);
+        umma_commit_pair(e_local);
+        umma_commit_pair(mapa_shared(e_local, peer));
+        if (kb % KC == KC - 1 || kb == nkb - 1) {
+          const uint32_t c_local = smem_u32(&chunk_full[chunk & 1]);
+          umma_commit_pair(c_local);
+          umma_commit_pair(mapa_shared(c_local, peer));
+        }
+      }
+      if (!ok) {
+        umma_commit_pair(smem_u32(drain_bar));
+        mbar_drain(drain_bar, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ split + promotion epilogue (both CTAs)
+    constexpr int COLS = Cfg::kColsPerThread;
+    const int e = warp - 2;
+    const int q = warp & 3;
+    const int h = e >> 2;
+    const int et = threadIdx.x - 64;
+    const int row = m0 + 32 * q + lane;
+    float* crow = out + static_cast<int64_t>(row) * ldo;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
+    bool ok = true;
+    float tot[COLS];
+#pragma unroll
+    for (int j = 0; j < COLS; ++j) tot[j] = 0.f;
+
+    auto drain = [&](int c) {
+      const int buf = c & 1;
+      if (!mbar_wait_cluster(&chunk_full[buf], (c >> 1) & 1, abort_flag)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int j = 0; j < COLS / 32; ++j) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + buf * BN + h * COLS + j * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) tot[j * 32 + i] += __uint_as_float(r[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+#if TILEC_PAIR_SIGNAL == 0
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&chunk_empty[buf]), 0));
+#else
+      if (lane == 0) mbar_arrive_remote_cta(mapa_shared(smem_u32(&chunk_empty[buf]), 0));
+#endif
+      return true;
+    };
+
+    constexpr int kLag = 2;
+    int drained = 0;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t ph = (kb / STAGES) & 1;
+      if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
+      float4* src_a = reinterpret_cast<float4*>(a_raw(s));
+      float4* dst_a = reinterpret_cast<float4*>(a_lo(s));
+#pragma unroll
+      for (int i = et; i < Cfg::kABytes / 16; i += 32 * Cfg::kEpiWarps) {
+        const float4 x = src_a[i];
+        const float4 hv = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+        dst_a[i] = make_float4(x.x - hv.x, x.y - hv.y, x.z - hv.z, x.w - hv.w);
+        if constexpr (HI_EXPLICIT) src_a[i] = hv;
+      }
+      float4* src_b = reinterpret_cast<float4*>(b_raw(s));
+      float4* dst_b = reinterpret_cast<float4*>(b_lo(s));
+#pragma unroll
+      for (int i = et; i < Cfg::kBBytes / 16; i += 32 * Cfg::kEpiWarps) {
+        const float4 x = src_b[i];
+        const float4 hv = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+        dst_b[i] = make_float4(x.x - hv.x, x.y - hv.y, x.z - hv.z, x.w - hv.w);
+        if constexpr (HI_EXPLICIT) src_b[i] = hv;
+      }
+      fence_proxy_async_smem();
+#if TILEC_PAIR_SIGNAL == 2
+      // Each split warp reports to a local barrier; one of them (rotating with the stage)
+      // waits for all eight and publishes the stage to the leader with one cluster release.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&split_local[s]);
+      if (e == (kb % Cfg::kEpiWarps)) {
+        if (!mbar_wait(&split_local[s], ph, abort_flag)) { ok = false; break; }
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&split[s]), 0));
+      }
+#elif TILEC_PAIR_SIGNAL == 1
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote_cta(mapa_shared(smem_u32(&split[s]), 0));
+#else
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&split[s]), 0));
+#endif
+      if (kb % KC == (kLag < KC ? kLag : KC - 1) && kb / KC >= 1 && drained < kb / KC) {
+        if (!drain(drained)) { ok = false; break; }
+        ++drained;
+      }
+    }
+    while (ok && drained < n_chunks) {
+      if (!drain(drained)) { ok = false; break; }
+      ++drained;
+    }
+    if (ok && row < M) {
+#pragma unroll
+      for (int j = 0; j < COLS; j += 32) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = tot[j + i];
+        store_row<32>(crow, n0 + h * COLS + j, N, vec_out, v);
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // every remote arrive / commit targeting either CTA has landed
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace tilec

@@ -22,6 +22,7 @@
 #include "common.cuh"
 #include "simt.cuh"
 #include "tc_gemm.cuh"
+#include "tc2_gemm.cuh"
 
 namespace tilec {
 namespace {
@@ -62,6 +63,16 @@ struct TcShape {
   static constexpr int k3xStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
 };
 
+// CTA-pair 3XTF32 kernel (tc2_gemm_kernel): 256 x 256 tiles, stages of 32 KB, used for
+// M >= TILEC_PAIR_MIN_M and N > 128 (B200: 245 vs 210 TFLOP/s for the 1-CTA kernel at 8192^3).
+#ifndef TILEC_PAIR_STAGES
+#define TILEC_PAIR_STAGES 6
+#endif
+#ifndef TILEC_PAIR_MIN_M
+#define TILEC_PAIR_MIN_M 256
+#endif
+constexpr int kPairStages = TILEC_PAIR_STAGES;
+
 cudaError_t init_device_attrs() {
   cudaError_t e = cudaSuccess;
   auto acc = [&](cudaError_t x) {
@@ -84,6 +95,10 @@ cudaError_t init_device_attrs() {
   acc(set_tc_attr<256, 16, TcShape<256>::k3xStages, true, false>());
   acc(set_tc_attr<128, 16, TcShape<128>::k3xStages, true, false>());
   acc(set_tc_attr<64, 16, TcShape<64>::k3xStages, true, false>());
+  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           Tc2Cfg<256, kPairStages>::kSmemBytes));
+  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           Tc2Cfg<256, kPairStages>::kSmemBytes));
   return e;
 }
 
@@ -138,6 +153,7 @@ struct Plan {
   size_t ws_bytes = 0;
   int64_t ldw = 0;
   bool pack_a = false, pack_b = false;
+  bool pair = false;  // 3XTF32 on a CTA pair (tc2_gemm_kernel, 256 x 256 tiles)
   size_t off_a = 0, off_b = 0, off_slabs = 0;
 };
 
@@ -244,6 +260,7 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
   p->variant = variant;
   if (tensor) {
     p->bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
+    p->pair = variant != TILEC_MM_TF32 && p->bn == 256 && M > 128 && M >= TILEC_PAIR_MIN_M;
     const int bk = variant == TILEC_MM_TF32 ? 32 : 16;
     const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
     p->split = choose_split(tiles, M, N, K, kTcBM, p->bn, bk, d.sms, requested_split,
@@ -345,6 +362,35 @@ int launch_tc_mode(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int
   else
     return launch_tc<BN, 32, TcShape<BN>::kTf32Stages, false, false>(ma, mb, out, M, N, ldo, slab, K, k_chunk,
                                                                      split, vec_out, s);
+}
+
+template <bool HI>
+int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N, int64_t ldo,
+               int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, cudaStream_t s) {
+  using Cfg = Tc2Cfg<256, kPairStages>;
+  const int mp_tiles = static_cast<int>(cdiv(M, 256));
+  const int n_tiles = static_cast<int>(cdiv(N, 256));
+  const int group_m = 8;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(static_cast<unsigned>(2 * int64_t(mp_tiles) * n_tiles), 1, static_cast<unsigned>(split));
+  lc.blockDim = dim3(Cfg::kThreads, 1, 1);
+  lc.dynamicSmemBytes = Cfg::kSmemBytes;
+  lc.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&lc, tc2_gemm_kernel<256, kPairStages, HI>, ma, mb, out, static_cast<int>(M),
+                                           static_cast<int>(N), ldo, slab, static_cast<int>(K),
+                                           static_cast<int>(k_chunk), mp_tiles, n_tiles, group_m, vec_out);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return TILEC_ERR_LAUNCH;
+  }
+  return launch_status();
 }
 
 template <bool SPLIT3, bool HI>
@@ -498,7 +544,11 @@ int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
     const int bk = p.variant == TILEC_MM_TF32 ? 32 : 16;
     rc = encode_maps(A, B, M, N, K, lda, ldb, bk, bk * 4, &ma, &mb);
     if (rc) return rc;
-    if (p.variant == TILEC_MM_TF32)
+    if (p.pair)
+      rc = p.variant == TILEC_MM_3XTF32
+               ? launch_tc2<false>(ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s)
+               : launch_tc2<true>(ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
+    else if (p.variant == TILEC_MM_TF32)
       rc = dispatch_tc_bn<false, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
     else if (p.variant == TILEC_MM_3XTF32)
       rc = dispatch_tc_bn<true, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);

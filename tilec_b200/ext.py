@@ -62,20 +62,47 @@ def _check_out(out, M, N, device):
     return out.stride(0) if M > 1 else max(N, 1)
 
 
+_WS_BYTES = {}   # (shape, strides, 16-byte alignment of A/B/C, variant, split) -> workspace bytes
+_WS = {}         # (device index, stream handle) -> grow-only workspace tensor
+_installed = False
+
+
+def _workspace(dev, stream, nbytes):
+    """A workspace of >= nbytes for work ordered on `stream` (reused across calls)."""
+    key = (dev.index, stream)
+    ws = _WS.get(key)
+    if ws is None or ws.numel() * 4 < nbytes:
+        ws = torch.empty((nbytes + 4095) // 4096 * 1024, dtype=torch.float32, device=dev)
+        _WS[key] = ws
+    return ws
+
+
 def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k):
+    global _installed
     lib = _native.load()
-    from . import select  # installs the B200 selection table on first use
-    select.ensure_installed()
+    if not _installed:
+        from . import select  # installs the B200 selection table on first use
+        select.ensure_installed()
+        _installed = True
     cfg = _native.make_cfg(variant, split_k)
     pa, pb, pc = a.data_ptr(), b.data_ptr(), out.data_ptr()
-    with torch.cuda.device(out.device):
-        stream = torch.cuda.current_stream(out.device).cuda_stream
-        ws_bytes = lib.tilec_mm_workspace_bytes(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg))
-        ws = None
-        if ws_bytes:
-            ws = torch.empty((ws_bytes + 3) // 4, dtype=torch.float32, device=out.device)
-        rc = lib.tilec_mm_f32(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg),
-                              ws.data_ptr() if ws is not None else None, ws_bytes, stream)
+    dev = out.device
+    switch = torch.cuda.current_device() != dev.index
+    prev = torch.cuda.current_device()
+    if switch:
+        torch.cuda.set_device(dev)
+    try:
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        key = (M, N, K, lda, ldb, ldc, pa & 15 == 0, pb & 15 == 0, pc & 15 == 0, cfg.variant, cfg.split_k, dev.index)
+        ws_bytes = _WS_BYTES.get(key)
+        if ws_bytes is None:
+            ws_bytes = lib.tilec_mm_workspace_bytes(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg))
+            _WS_BYTES[key] = ws_bytes
+        ws_ptr = _workspace(dev, stream, ws_bytes).data_ptr() if ws_bytes else None
+        rc = lib.tilec_mm_f32(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg), ws_ptr, ws_bytes, stream)
+    finally:
+        if switch:
+            torch.cuda.set_device(prev)
     _native.check(rc, "tilec_mm_f32")
     return out
 

@@ -54,6 +54,8 @@ def load_table(path=None):
 def install(rows):
     """Install int32 rows into the C library (an empty list restores the built-in rules)."""
     lib = _native.load()
+    from . import ext
+    ext._WS_BYTES.clear()  # cached workspace sizes depend on the plans the table selects
     flat = [x for r in rows for x in r]
     arr = (ctypes.c_int32 * max(len(flat), 1))(*flat)
     _native.check(lib.tilec_mm_set_table(arr, len(rows)), "tilec_mm_set_table")
