@@ -210,8 +210,17 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     const int64_t n = (g % groups_per_row) * 4;
     const float* w = W + m * ldw + n;
     float4 s = *reinterpret_cast<const float4*>(w);
-    for (int z = 1; z < S; ++z) {
-      const float4 v = *reinterpret_cast<const float4*>(w + z * slab);
+    // Eight slab loads in flight per step; the adds stay in slab order (deterministic).
+    int z = 1;
+    for (; z + 8 <= S; z += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(reinterpret_cast<const float4*>(w + (z + u) * slab));
+#pragma unroll
+      for (int u = 0; u < 8; ++u) { s.x += v[u].x; s.y += v[u].y; s.z += v[u].z; s.w += v[u].w; }
+    }
+    for (; z < S; ++z) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(w + z * slab));
       s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
     }
     float* c = C + m * ldc + n;

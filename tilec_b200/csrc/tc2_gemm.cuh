@@ -302,6 +302,7 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
       if (!drain(drained)) { ok = false; break; }
       ++drained;
     }
+
     if (ok && row < M) {
 #pragma unroll
       for (int j = 0; j < COLS; j += 32) {

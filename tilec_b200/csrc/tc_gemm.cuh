@@ -42,10 +42,13 @@ constexpr int kTcBM = 128;
 
 template <int BN, int BK, int STAGES, bool SPLIT3>
 struct TcCfg {
-  static constexpr int kEpiWarps = SPLIT3 ? 8 : 4;
+  static constexpr int kEpiWarps = (SPLIT3 && BN >= 128) ? 8 : 4;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kABytes = kTcBM * BK * 4;
   static constexpr int kBBytes = BK * BN * 4;
+  // A stage holds the raw TMA tiles and, for 3XTF32, their lo(x) tiles next to them.  (A
+  // separate, shallower lo ring was measured slower: it bounds how far the split stage can
+  // run ahead of the MMA.)
   static constexpr int kStageBytes = (kABytes + kBBytes) * (SPLIT3 ? 2 : 1);
   static constexpr int kTxBytes = kABytes + kBBytes;
   static constexpr int kBarBytes = 1024;  // barriers + tmem slot + flags
@@ -55,11 +58,12 @@ struct TcCfg {
   static constexpr uint32_t kBLbo = BK * 128u;                  // stride between 32-column slabs
   static constexpr uint32_t kBSbo = 512u;                       // stride between 4-row K groups
   static constexpr uint32_t kTmemCols = SPLIT3 ? 2 * BN : BN;   // 3XTF32: two chunk buffers
-  static constexpr int kColsPerThread = SPLIT3 ? BN / 2 : 32;   // register totals per epilogue thread
+  static constexpr int kColsPerThread = SPLIT3 ? BN / (kEpiWarps / 4) : 32;  // register totals per thread
   static constexpr int kChunkBlocks = 8;                        // K-blocks per promoted chunk
   static_assert(BK == 16 || BK == 32, "BK");
-  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(kSmemBytes <= 232448, "shared memory");
+  static_assert(kColsPerThread % 32 == 0, "epilogue reads 32 TMEM columns at a time");
 };
 
 __device__ __forceinline__ float tf32_hi(float x) {
@@ -88,7 +92,7 @@ __device__ __forceinline__ void store_row(float* crow, int col, int N, int vec_o
   }
 }
 
-// Grid: x = tile index (grouped raster), z = K split.
+// Grid: x = tile index (grouped raster), z = K split (slabs of `out`).
 template <int BN, int BK, int STAGES, bool SPLIT3, bool HI_EXPLICIT>
 __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -107,7 +111,7 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
   uint8_t* bar_area = smem + STAGES * Cfg::kStageBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
   uint64_t* empty = full + STAGES;
-  uint64_t* split = empty + STAGES;
+  uint64_t* split = empty + STAGES;        // [STAGES] split warps -> MMA (3XTF32)
   uint64_t* chunk_full = split + STAGES;   // [2] MMA -> epilogue (3XTF32)
   uint64_t* chunk_empty = chunk_full + 2;  // [2] epilogue -> MMA (3XTF32)
   uint64_t* acc_bar = chunk_empty + 2;     // TF32: accumulator complete
@@ -131,14 +135,15 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
   const int in_band = tile - band * group_m * n_tiles;
   const int tile_m = first_m + in_band % band_rows;
   const int tile_n = in_band / band_rows;
+  const int kslice = static_cast<int>(blockIdx.z);
+  out += static_cast<int64_t>(blockIdx.z) * out_slab;
   const int m0 = tile_m * kTcBM;
   const int n0 = tile_n * BN;
 
-  const int k_begin = blockIdx.z * k_chunk;
+  const int k_begin = kslice * k_chunk;
   const int k_end = min(K, k_begin + k_chunk);
   const int nkb = k_end > k_begin ? (k_end - k_begin + BK - 1) / BK : 0;
   const int n_chunks = (nkb + KC - 1) / KC;
-  out += static_cast<int64_t>(blockIdx.z) * out_slab;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -184,7 +189,11 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
         for (int j = 0; j < BN / 32; ++j) tma_load_2d(b_raw(s) + j * BK * 128, &tmB, &full[s], n0 + 32 * j, k0);
         ++issued;
       }
-      if (!ok) {
+      if (ok) {
+        // Tail: the MMA's release of the last fills has arrived before the CTA exits.
+        for (int kb = nkb - STAGES < 0 ? 0 : nkb - STAGES; kb < nkb; ++kb)
+          if (!mbar_wait(&empty[kb % STAGES], (kb / STAGES) & 1, abort_flag)) break;
+      } else {
         // Let copies already in flight land before the CTA's shared memory goes away.
         for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb)
           mbar_drain(&full[kb % STAGES], (kb / STAGES) & 1);
@@ -306,6 +315,7 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
         if (!drain(drained)) { ok = false; break; }
         ++drained;
       }
+
       if (ok && row < M) {
 #pragma unroll
         for (int j = 0; j < COLS; j += 32) {

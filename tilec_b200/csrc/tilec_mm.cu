@@ -31,6 +31,7 @@ constexpr int kMaxDevices = 64;
 constexpr int kMaxSplit = 64;
 
 struct DeviceInfo {
+  int dev = 0;
   int sms = 0;
   int cc_major = 0;
   int cc_minor = 0;
@@ -54,14 +55,19 @@ cudaError_t set_tc_attr() {
                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
 }
 
-// Tensor-kernel instantiations: (BN, BK, STAGES) per mode.
-//   TF32   : BK = 32 (128B-swizzled A), 4 stages.
-//   3XTF32 : BK = 16 (64B-swizzled A), raw + lo buffers per stage.
+// Stages per mode (a 3XTF32 stage holds raw + lo tiles): BN 256: 4 x 48 KB; 128: 6 x 32 KB;
+// 64: 8 x 24 KB; 32: 8 x 20 KB.
+#ifndef TILEC_3X_BK
+#define TILEC_3X_BK 16
+#endif
+constexpr int k3xBK = TILEC_3X_BK;  // K per stage of the 1-CTA 3XTF32 kernel
 template <int BN>
 struct TcShape {
   static constexpr int kTf32Stages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int k3xStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int k3xStages = (BN == 256 ? 4 : (BN == 128 ? 6 : 8)) * 16 / k3xBK;
 };
+
+
 
 // CTA-pair 3XTF32 kernel (tc2_gemm_kernel): 256 x 256 tiles, stages of 32 KB, used for
 // M >= TILEC_PAIR_MIN_M and N > 128 (B200: 245 vs 210 TFLOP/s for the 1-CTA kernel at 8192^3).
@@ -89,12 +95,12 @@ cudaError_t init_device_attrs() {
   acc(set_tc_attr<256, 32, TcShape<256>::kTf32Stages, false, false>());
   acc(set_tc_attr<128, 32, TcShape<128>::kTf32Stages, false, false>());
   acc(set_tc_attr<64, 32, TcShape<64>::kTf32Stages, false, false>());
-  acc(set_tc_attr<256, 16, TcShape<256>::k3xStages, true, true>());
-  acc(set_tc_attr<128, 16, TcShape<128>::k3xStages, true, true>());
-  acc(set_tc_attr<64, 16, TcShape<64>::k3xStages, true, true>());
-  acc(set_tc_attr<256, 16, TcShape<256>::k3xStages, true, false>());
-  acc(set_tc_attr<128, 16, TcShape<128>::k3xStages, true, false>());
-  acc(set_tc_attr<64, 16, TcShape<64>::k3xStages, true, false>());
+  acc(set_tc_attr<256, k3xBK, TcShape<256>::k3xStages, true, true>());
+  acc(set_tc_attr<128, k3xBK, TcShape<128>::k3xStages, true, true>());
+  acc(set_tc_attr<64, k3xBK, TcShape<64>::k3xStages, true, true>());
+  acc(set_tc_attr<256, k3xBK, TcShape<256>::k3xStages, true, false>());
+  acc(set_tc_attr<128, k3xBK, TcShape<128>::k3xStages, true, false>());
+  acc(set_tc_attr<64, k3xBK, TcShape<64>::k3xStages, true, false>());
   acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            Tc2Cfg<256, kPairStages>::kSmemBytes));
   acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -110,6 +116,7 @@ int current_device(DeviceInfo** out) {
   }
   std::call_once(g_dev_once[dev], [dev]() {
     DeviceInfo& d = g_dev[dev];
+    d.dev = dev;
     cudaError_t e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
@@ -261,7 +268,7 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
   if (tensor) {
     p->bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
     p->pair = variant != TILEC_MM_TF32 && p->bn == 256 && M > 128 && M >= TILEC_PAIR_MIN_M;
-    const int bk = variant == TILEC_MM_TF32 ? 32 : 16;
+    const int bk = variant == TILEC_MM_TF32 ? 32 : (p->pair ? 16 : k3xBK);
     const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
     p->split = choose_split(tiles, M, N, K, kTcBM, p->bn, bk, d.sms, requested_split,
                             variant == TILEC_MM_TF32 ? 4.0e12 : 1.4e12);
@@ -357,8 +364,8 @@ template <int BN, bool SPLIT3, bool HI>
 int launch_tc_mode(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N, int64_t ldo,
                    int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, cudaStream_t s) {
   if constexpr (SPLIT3)
-    return launch_tc<BN, 16, TcShape<BN>::k3xStages, true, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split,
-                                                               vec_out, s);
+    return launch_tc<BN, k3xBK, TcShape<BN>::k3xStages, true, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split,
+                                                                  vec_out, s);
   else
     return launch_tc<BN, 32, TcShape<BN>::kTf32Stages, false, false>(ma, mb, out, M, N, ldo, slab, K, k_chunk,
                                                                      split, vec_out, s);
@@ -425,12 +432,12 @@ int launch_pack(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t 
 int launch_reduce(const float* ws, float* C, int64_t M, int64_t N, int64_t ldw, int64_t ldc, int split,
                   const DeviceInfo& d, cudaStream_t s) {
   const int64_t groups = M * cdiv(N, 4);
-  int64_t blocks = cdiv(groups, 256);
-  const int64_t cap = int64_t(d.sms) * 8;
+  int64_t blocks = cdiv(groups, 128);
+  const int64_t cap = int64_t(d.sms) * 16;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   const int vec_out = aligned16(C) && (ldc % 4 == 0);
-  splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(ws, C, M, N, ldw, ldc, M * ldw, split,
+  splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 128, 0, s>>>(ws, C, M, N, ldw, ldc, M * ldw, split,
                                                                      vec_out);
   return launch_status();
 }
@@ -541,7 +548,7 @@ int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
     rc = launch_status();
   } else {
     CUtensorMap ma, mb;
-    const int bk = p.variant == TILEC_MM_TF32 ? 32 : 16;
+    const int bk = p.variant == TILEC_MM_TF32 ? 32 : (p.pair ? 16 : k3xBK);
     rc = encode_maps(A, B, M, N, K, lda, ldb, bk, bk * 4, &ma, &mb);
     if (rc) return rc;
     if (p.pair)
