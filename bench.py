@@ -363,7 +363,14 @@ def main():
     value = flops_step * args.steps / (ms_total * 1e-3) / 1e12
 
     pk = peaks()
-    peak, peak_note = variant_peak(variant, pk, sustained=True)
+    # Sustained (power-capped) peak when the clock record shows the power cap during the
+    # timed region, burst peak otherwise.
+    capped = bool(clk and "sw_power_cap" in clk.get("reasons", []))
+    if world > 1:
+        flag = torch.tensor([1.0 if capped else 0.0], device=dev)
+        dist.broadcast(flag, src=0)
+        capped = bool(flag.item())
+    peak, peak_note = variant_peak(variant, pk, sustained=capped)
     flops_launch = 2.0 * rows * panel_w * K5
     bytes_launch = 4.0 * (rows * K5 + K5 * panel_w + rows * panel_w)
     achieved = flops_launch / (gemm_ms_max * 1e-3) / 1e12
