@@ -98,7 +98,13 @@ def bench(n=64, path=DEFAULT_CSV, seed=4):
             b = torch.randn(k, nn, device="cuda", generator=g)
             c = torch.empty(m, nn, device="cuda")
             best = None
-            for v, s in ext.mm_configs(m, k, nn):
+            # Built-in rules (no table) and each variant family with the library's own split.
+            from . import select
+            select.install([])
+            ms = time_ms(lambda: ext._matrix_mul(a, b, variant="auto", out=c))
+            w.writerow([dev, m, k, nn, "builtin", 0, f"{ms:.6f}"])
+            cands = [("simt", 0), ("splitk", 0), ("3xtf32", 0), ("tf32", 0)] + ext.mm_configs(m, k, nn)
+            for v, s in cands:
                 ms = time_ms(lambda: ext._matrix_mul(a, b, variant=v, split_k=s, out=c), best)
                 best = ms if best is None else min(best, ms)
                 w.writerow([dev, m, k, nn, v, s, f"{ms:.6f}"])
@@ -111,58 +117,78 @@ def _box(m, k, n):
     return lg(m), lg(n), lg(k)
 
 
-def fit(rows):
-    """Selection table: one log2 box per measured shape -> its fastest config."""
+# AUTO must keep fp32-class accuracy (relFrob <= 1e-5), so plain TF32 is measured but never chosen.
+FP32_CLASS = ("simt", "splitk", "3xtf32")
+GRID_EDGES = (0, 2, 4, 6, 8, 10, 12, 64)   # log2-size bins (2 octaves wide; the last is open)
+
+
+def _family_rows(rows):
+    """Rows timed with the library's own split choice (split_k == 0), fp32-class only."""
+    return [r for r in rows if r["variant"] in FP32_CLASS and r["split_k"] == 0]
+
+
+def _best_family(rs):
+    return min(rs, key=lambda r: r["ms"])["variant"]
+
+
+def fit(rows, k_nn=3):
+    """Selection table over a coarse log2 grid: each cell gets the variant family that is
+    fastest for most of the k_nn measured shapes nearest to the cell centre (log2 space);
+    the split count is left to the library (split_k = 0)."""
     by_shape = {}
-    for r in rows:
+    for r in _family_rows(rows):
         by_shape.setdefault((r["M"], r["K"], r["N"]), []).append(r)
-    boxes = {}
+    pts = []
     for (m, k, n), rs in by_shape.items():
-        best = min(rs, key=lambda r: r["ms"])
-        boxes.setdefault(_box(m, k, n), []).append(best)
+        pts.append(((math.log2(max(m, 1)), math.log2(max(n, 1)), math.log2(max(k, 1))), _best_family(rs)))
+    if not pts:
+        return []
     table = []
-    for (lm, ln, lk), bests in sorted(boxes.items()):
-        # Several shapes in one box: the config that is fastest most often.
-        votes = {}
-        for b in bests:
-            votes[(b["variant"], b["split_k"])] = votes.get((b["variant"], b["split_k"]), 0) + 1
-        (v, s), _ = max(votes.items(), key=lambda kv: kv[1])
-        table.append([lm, lm + 1, ln, ln + 1, lk, lk + 1, v, s])
+    e = GRID_EDGES
+    for i in range(len(e) - 1):
+        for j in range(len(e) - 1):
+            for l in range(len(e) - 1):
+                c = tuple(min(e[x] + 1.0, 13.0) for x in (i, j, l))
+                near = sorted(pts, key=lambda p: sum((p[0][d] - c[d]) ** 2 for d in range(3)))[:k_nn]
+                votes = {}
+                for _, v in near:
+                    votes[v] = votes.get(v, 0) + 1
+                v = max(votes.items(), key=lambda kv: (kv[1], kv[0] == "3xtf32"))[0]
+                table.append([e[i], e[i + 1], e[j], e[j + 1], e[l], e[l + 1], v, 0])
     return table
 
 
 def train(path=DEFAULT_CSV, out=None, test_frac=0.2, seed=0):
     from . import select
     rows = load(path)
-    keys = sorted({(r["M"], r["K"], r["N"]) for r in rows})
+    fam = _family_rows(rows)
+    keys = sorted({(r["M"], r["K"], r["N"]) for r in fam})
     random.Random(seed).shuffle(keys)
     test = set(keys[: int(len(keys) * test_frac)])
     table = fit([r for r in rows if (r["M"], r["K"], r["N"]) not in test])
     by_shape = {}
     for r in rows:
         by_shape.setdefault((r["M"], r["K"], r["N"]), []).append(r)
-    ratio_sel, ratio_default, matched = [], [], 0
+    ratio_sel, ratio_default = [], []
     for key in test:
         rs = by_shape[key]
-        best = min(r["ms"] for r in rs)
+        best = min(r["ms"] for r in rs if r["variant"] in FP32_CLASS)
         pick = select.lookup([t[:6] + [_variant_code(t[6]), t[7]] for t in table], *_mnk(key))
-        default = next((r for r in rs if r.get("default")), None) or _default_row(rs)
-        chosen = None
-        if pick is not None:
-            matched += 1
-            chosen = next((r for r in rs if (r["variant"], r["split_k"]) == pick), None)
-        chosen = chosen or default
+        chosen = next(r for r in rs if r["variant"] == pick[0] and r["split_k"] == 0)
+        default = next(r for r in rs if r["variant"] == "builtin")
         ratio_sel.append(chosen["ms"] / best)
         ratio_default.append(default["ms"] / best)
     gm = lambda v: math.exp(sum(math.log(a) for a in v) / max(len(v), 1))  # noqa: E731
-    print(f"held-out shapes: {len(test)} (table matched {matched})")
+    print(f"held-out shapes: {len(test)}")
     print(f"selector: {gm(ratio_sel):.3f}x of best (geo mean), worst {max(ratio_sel, default=1):.2f}x")
     print(f"default : {gm(ratio_default):.3f}x of best (geo mean), worst {max(ratio_default, default=1):.2f}x")
     table = fit(rows)
     doc = {"device": rows[0]["device"] if rows else "", "source": os.path.basename(path),
-           "shapes": len(keys), "rows": table,
+           "shapes": len(keys), "grid_log2_edges": list(GRID_EDGES), "rows": table,
            "heldout": {"shapes": len(test), "selector_x_of_best": round(gm(ratio_sel), 4),
-                       "default_x_of_best": round(gm(ratio_default), 4)}}
+                       "builtin_x_of_best": round(gm(ratio_default), 4),
+                       "selector_worst": round(max(ratio_sel, default=1), 3),
+                       "builtin_worst": round(max(ratio_default, default=1), 3)}}
     out = out or select.TABLE_PATH
     with open(out, "w") as f:
         json.dump(doc, f, indent=1)
@@ -178,17 +204,6 @@ def _variant_code(v):
 def _mnk(key):
     m, k, n = key
     return m, n, k
-
-
-def _default_row(rs):
-    """The row the library's built-in rules would launch (split_k 0 = library choice ->
-    recorded as the variant's first candidate)."""
-    from . import _native  # noqa: F401
-    m, k, n = rs[0]["M"], rs[0]["K"], rs[0]["N"]
-    aligned = k % 4 == 0 and n % 4 == 0
-    v = "3xtf32" if aligned and 2.0 * m * n * k >= 1e8 else "simt"
-    cands = [r for r in rs if r["variant"] == v] or rs
-    return min(cands, key=lambda r: r["split_k"])
 
 
 def pick(M, K, N):
