@@ -274,3 +274,53 @@ def test_skinny_split_k(shape):
     ref = a.double() @ b.double()
     assert ((got.double() - ref).norm() / ref.norm()).item() <= 1e-5
     assert _status_clean()
+
+
+@pytest.mark.parametrize("variant,split_k", [("3xtf32", 0), ("3xtf32", 29), ("splitk", 8), ("tf32", 5),
+                                             ("3xtf32", 1), ("simt", 0)])
+def test_back_to_back_launches_in_a_graph(variant, split_k):
+    """Kernels start while the previous one drains (programmatic dependent launch): a
+    CUDA graph of consecutive products that share one workspace and chain through their
+    outputs (each next input is the previous output) must equal the same calls run one
+    at a time with a device sync between them."""
+    g = torch.Generator(device=DEV).manual_seed(17)
+    m, k, n = 512, 2048, 64
+    a = torch.randn(m, k, device=DEV, generator=g)
+    bs = [torch.randn(k, n, device=DEV, generator=g) / k ** 0.5 for _ in range(3)]
+    w = torch.randn(n, k, device=DEV, generator=g) / n ** 0.5
+    outs = [torch.empty(m, n, device=DEV) for _ in range(3)]
+    mids = [torch.empty(m, k, device=DEV) for _ in range(3)]
+
+    def chain():
+        x = a
+        for i in range(3):
+            ext._matrix_mul(x, bs[i], variant=variant, split_k=split_k, out=outs[i])
+            ext._matrix_mul(outs[i], w, variant=variant, split_k=split_k, out=mids[i])
+            x = mids[i]
+
+    side = torch.cuda.Stream(device=DEV)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        chain()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        chain()
+    for o in outs + mids:
+        o.fill_(float("nan"))
+    graph.replay()
+    torch.cuda.synchronize()
+    got = [o.clone() for o in outs + mids]
+    # Reference: the same chain with a full device sync after every call.
+    x = a
+    for i in range(3):
+        ext._matrix_mul(x, bs[i], variant=variant, split_k=split_k, out=outs[i])
+        torch.cuda.synchronize()
+        ext._matrix_mul(outs[i], w, variant=variant, split_k=split_k, out=mids[i])
+        torch.cuda.synchronize()
+        x = mids[i]
+    for g_, r in zip(got, outs + mids):
+        assert torch.equal(g_, r)
+    del graph
+    assert _status_clean()

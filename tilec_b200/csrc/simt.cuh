@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1)
   float* As = smem;
   float* Bs = smem + kSimtStages * kSimtBM * kSimtBK;
 
+  pdl_wait();
   if (blockDim.x != kSimtThreads) {
     if (threadIdx.x == 0) record_status(TILEC_DEV_BAD_LAUNCH);
     return;
@@ -175,6 +176,9 @@ __global__ void __launch_bounds__(kSimtThreads, 1)
     }
   }
   cp_async_wait<0>();
+  // Let the next kernel launch only now: CTAs of a dependent kernel that wait resident on
+  // the SM while this FMA-bound loop runs cost it issue slots (measured 40% slower).
+  pdl_launch_dependents();
 
   // Epilogue: masked stores (ext.py:24).  Each warp writes two 256-byte row runs.
 #pragma unroll
@@ -197,44 +201,93 @@ __global__ void __launch_bounds__(kSimtThreads, 1)
   }
 }
 
-// C[m, n] = sum_{z < S} W[z][m, n], summed in z order.  W slabs have row stride ldw
-// (a multiple of 4) and slab stride `slab`.  One thread per 4 columns of one row.
+// C[m, n] = sum_{z < S} W[z][m, n].  W slabs have row stride ldw (a multiple of 4) and
+// slab stride `slab`.  A 256-thread block has P slab partitions of G = 256 / P lanes; a
+// lane handles U float4 column groups (G apart, so a warp reads contiguous runs).
+// Partition p sums slabs [p*S/P, (p+1)*S/P) of each group in z order, then partition 0
+// adds partitions 1..P-1 in p order.  The order is fixed by (S, P), so results are
+// bitwise reproducible.  P and U are chosen so that one pass of resident blocks covers
+// the output with every load in flight at once (up to eight per thread at a time):
+// separate grid-stride rounds would each pay the full L2 latency again.
+template <int P, int U>
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ W, float* __restrict__ C,
                                                             int64_t M, int64_t N, int64_t ldw, int64_t ldc,
                                                             int64_t slab, int S, int vec_out) {
+  static_assert(8 % U == 0, "U divides the load batch");
+  constexpr int G = 256 / P;
+  __shared__ float4 part[P > 1 ? P - 1 : 1][P > 1 ? U * G : 1];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int p = static_cast<int>(threadIdx.x) / G;
+  const int gi = static_cast<int>(threadIdx.x) % G;
+  const int z0 = (S * p) / P, nz = (S * (p + 1)) / P - z0;
   const int64_t groups_per_row = (N + 3) / 4;
   const int64_t total = M * groups_per_row;
-  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
-       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t m = g / groups_per_row;
-    const int64_t n = (g % groups_per_row) * 4;
-    const float* w = W + m * ldw + n;
-    float4 s = *reinterpret_cast<const float4*>(w);
-    // Eight slab loads in flight per step; the adds stay in slab order (deterministic).
-    int z = 1;
-    for (; z + 8 <= S; z += 8) {
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * G * U; base < total;
+       base += static_cast<int64_t>(gridDim.x) * G * U) {
+    const float* w[U];
+    int64_t mm[U], nn[U];
+    bool live[U];
+    float4 acc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t g = base + u * G + gi;
+      live[u] = g < total;
+      mm[u] = live[u] ? g / groups_per_row : 0;
+      nn[u] = live[u] ? (g % groups_per_row) * 4 : 0;
+      w[u] = W + mm[u] * ldw + nn[u] + static_cast<int64_t>(z0) * slab;
+      acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (live[u] && nz > 0) acc[u] = __ldg(reinterpret_cast<const float4*>(w[u]));
+    }
+    // Load t covers group t % U, slab z0 + t / U; batches of eight keep each group's adds
+    // in z order.
+    for (int t0 = U; t0 < U * nz; t0 += 8) {
       float4 v[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __ldg(reinterpret_cast<const float4*>(w + (z + u) * slab));
+      for (int j = 0; j < 8; ++j)
+        if (t0 + j < U * nz && live[j % U])
+          v[j] = __ldg(reinterpret_cast<const float4*>(w[j % U] + static_cast<int64_t>((t0 + j) / U) * slab));
 #pragma unroll
-      for (int u = 0; u < 8; ++u) { s.x += v[u].x; s.y += v[u].y; s.z += v[u].z; s.w += v[u].w; }
+      for (int j = 0; j < 8; ++j)
+        if (t0 + j < U * nz && live[j % U]) {
+          float4& a = acc[j % U];
+          a.x += v[j].x; a.y += v[j].y; a.z += v[j].z; a.w += v[j].w;
+        }
     }
-    for (; z < S; ++z) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(w + z * slab));
-      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+    if constexpr (P > 1) {
+      if (p > 0) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) part[p - 1][u * G + gi] = acc[u];
+      }
+      __syncthreads();
     }
-    float* c = C + m * ldc + n;
-    if (vec_out && n + 3 < N) {
-      *reinterpret_cast<float4*>(c) = s;
-    } else {
-      const float v[4] = {s.x, s.y, s.z, s.w};
-      for (int j = 0; j < 4 && n + j < N; ++j) c[j] = v[j];
+    if (p == 0) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (!live[u]) continue;
+        float4 s = acc[u];
+#pragma unroll
+        for (int q = 1; q < P; ++q) {
+          const float4 v = part[q - 1][u * G + gi];
+          s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+        }
+        float* c = C + mm[u] * ldc + nn[u];
+        if (vec_out && nn[u] + 3 < N) {
+          *reinterpret_cast<float4*>(c) = s;
+        } else {
+          const float sv[4] = {s.x, s.y, s.z, s.w};
+          for (int j = 0; j < 4 && nn[u] + j < N; ++j) c[j] = sv[j];
+        }
+      }
     }
+    if constexpr (P > 1) __syncthreads();
   }
 }
 
 // K == 0: the reference's accumulator stays 0 and is stored (ext.py:18,24).
 __global__ void __launch_bounds__(256) fill_zero_kernel(float* __restrict__ C, int64_t M, int64_t N, int64_t ldc) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t total = M * N;
   for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x)

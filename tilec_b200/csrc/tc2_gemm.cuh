@@ -57,6 +57,7 @@ struct Tc2Cfg {
   static constexpr int kChunkBlocks = 8;
   static_assert(BN == 256 || BN == 128, "BN");
   static_assert(kSmemBytes <= 232448, "shared memory");
+  static_assert(kEpiWarps * 32 * (kColsPerThread + 4) * 4 <= STAGES * kStageBytes, "output staging");
 };
 
 // M = 256 (pair), N = BN, kind::tf32, A K-major, B MN-major.
@@ -143,6 +144,8 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Barrier init, TMEM allocation and descriptor prefetch overlap the previous kernel.
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -222,8 +225,6 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
     const int q = warp & 3;
     const int h = e >> 2;
     const int et = threadIdx.x - 64;
-    const int row = m0 + 32 * q + lane;
-    float* crow = out + static_cast<int64_t>(row) * ldo;
     const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
     bool ok = true;
     float tot[COLS];
@@ -303,18 +304,17 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
       ++drained;
     }
 
-    if (ok && row < M) {
-#pragma unroll
-      for (int j = 0; j < COLS; j += 32) {
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = tot[j + i];
-        store_row<32>(crow, n0 + h * COLS + j, N, vec_out, v);
-      }
+    // Every MMA of the pair has completed (the last chunk was drained), so this CTA's stage
+    // buffers are free for the output staging.
+    pdl_launch_dependents();
+    if (ok) {
+      float* stage = reinterpret_cast<float*>(smem) + e * 32 * (COLS + 4);
+      store_rows_coalesced<COLS>(stage, tot, out, ldo, m0 + 32 * q, n0 + h * COLS, M, N, vec_out, lane);
     }
   }
 
   __syncwarp();
+  pdl_launch_dependents();
   tc_fence_before();
   cluster_sync();  // every remote arrive / commit targeting either CTA has landed
   if (warp == 1) {

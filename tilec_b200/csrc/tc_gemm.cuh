@@ -64,6 +64,10 @@ struct TcCfg {
   static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(kSmemBytes <= 232448, "shared memory");
   static_assert(kColsPerThread % 32 == 0, "epilogue reads 32 TMEM columns at a time");
+  // Output staging (reuses the stage buffers once every MMA has completed).
+  static constexpr int kStoreCols = SPLIT3 ? kColsPerThread : 32;
+  static constexpr int kStageFloatsPerWarp = 32 * (kStoreCols + 4);
+  static_assert(kEpiWarps * kStageFloatsPerWarp * 4 <= STAGES * kStageBytes, "output staging");
 };
 
 __device__ __forceinline__ float tf32_hi(float x) {
@@ -78,18 +82,38 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// Store `n` consecutive fp32 values of one output row (masked at N, vectorised when aligned).
-template <int NV>
-__device__ __forceinline__ void store_row(float* crow, int col, int N, int vec_out, const float (&v)[NV]) {
-  if (vec_out && col + NV - 1 < N) {
+// Writes a 32-row x NC-column block, held one row per lane in v[], to rows row0.. and
+// columns col0.. of `out` (masked at M and N).  The warp transposes it through its own
+// staging buffer `stage` (32 x (NC + 4) floats; the pitch of NC + 4 keeps both passes
+// free of bank conflicts) so that consecutive lanes store consecutive 16-byte pieces of
+// one row: the warp writes whole row runs instead of 32 rows 16 bytes at a time.
+template <int NC>
+__device__ __forceinline__ void store_rows_coalesced(float* stage, const float (&v)[NC], float* out, int64_t ldo,
+                                                     int row0, int col0, int M, int N, int vec_out, int lane) {
+  constexpr int kPitch = NC + 4;
+  constexpr int kChunks = NC / 4;  // 16-byte pieces per row
 #pragma unroll
-    for (int j = 0; j < NV; j += 4)
-      *reinterpret_cast<float4*>(crow + col + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-  } else {
+  for (int j = 0; j < NC; j += 4)
+    *reinterpret_cast<float4*>(stage + lane * kPitch + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  __syncwarp();
+#pragma unroll 4
+  for (int c = lane; c < 32 * kChunks; c += 32) {
+    const int r = c / kChunks, piece = c % kChunks;
+    const int grow = row0 + r, gcol = col0 + 4 * piece;
+    if (grow < M) {
+      const float4 x = *reinterpret_cast<const float4*>(stage + r * kPitch + 4 * piece);
+      float* dst = out + static_cast<int64_t>(grow) * ldo + gcol;
+      if (vec_out && gcol + 3 < N) {
+        *reinterpret_cast<float4*>(dst) = x;
+      } else {
+        const float xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-    for (int j = 0; j < NV; ++j)
-      if (col + j < N) crow[col + j] = v[j];
+        for (int j = 0; j < 4; ++j)
+          if (gcol + j < N) dst[j] = xs[j];
+      }
+    }
   }
+  __syncwarp();
 }
 
 // Grid: x = tile index (grouped raster), z = K split (slabs of `out`).
@@ -172,6 +196,8 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Barrier init, TMEM allocation and descriptor prefetch overlap the previous kernel.
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -248,8 +274,6 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
     // ------------------------------------------------------------ epilogue warps
     const int e = warp - 2;                  // 0 .. kEpiWarps-1
     const int q = warp & 3;                  // TMEM lane quadrant this warp may access
-    const int row = m0 + 32 * q + lane;
-    float* crow = out + static_cast<int64_t>(row) * ldo;
     const uint32_t lane_base = static_cast<uint32_t>(32 * q) << 16;
     bool ok = true;
 
@@ -316,19 +340,18 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
         ++drained;
       }
 
-      if (ok && row < M) {
-#pragma unroll
-        for (int j = 0; j < COLS; j += 32) {
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = tot[j + i];
-          store_row<32>(crow, n0 + h * COLS + j, N, vec_out, v);
-        }
+      // Every MMA has completed (the last chunk was drained), so the stage buffers are free.
+      pdl_launch_dependents();
+      if (ok) {
+        float* stage = reinterpret_cast<float*>(smem) + e * Cfg::kStageFloatsPerWarp;
+        store_rows_coalesced<COLS>(stage, tot, out, ldo, m0 + 32 * q, n0 + h * COLS, M, N, vec_out, lane);
       }
     } else {
       if (nkb > 0) ok = mbar_wait(acc_bar, 0, abort_flag);
+      pdl_launch_dependents();
       if (ok) {
         tc_fence_after();
+        float* stage = reinterpret_cast<float*>(smem) + e * Cfg::kStageFloatsPerWarp;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -339,18 +362,17 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) r[j] = 0u;
           }
-          if (row < M) {
-            float v[32];
+          float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            store_row<32>(crow, n0 + c * 32, N, vec_out, v);
-          }
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          store_rows_coalesced<32>(stage, v, out, ldo, m0 + 32 * q, n0 + c * 32, M, N, vec_out, lane);
         }
       }
     }
   }
 
   __syncwarp();  // lanes 1..31 of warps 0/1 wait here for their lane 0
+  pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

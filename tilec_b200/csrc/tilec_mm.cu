@@ -14,6 +14,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -221,28 +222,46 @@ void choose_auto(const DeviceInfo& d, const float* A, const float* B, int64_t M,
 // time of one full-K tile divided across slices, plus the reduction's traffic (each slice
 // writes and the reduction reads an M x N slab) and a fixed cost for its extra launch.
 // flops_per_sm: sustained useful FLOP/s of one SM on this kernel.
-int choose_split(int64_t tiles, int64_t M, int64_t N, int64_t K, int bm, int bn, int bk, int sms, int requested,
-                 double flops_per_sm) {
+// K-split count for a grid of `ctas` CTAs per K slice on `sms` SMs, each CTA needing
+// `cta_s` seconds for the full K on an SM of its own and writing `slab_bytes` per extra
+// slice.  Cost of s slices: waves(s) * cta_s / s (CTAs sharing an SM run one after the
+// other) + s * slab_bytes / 3 TB/s (slab written by the GEMM and read back by the
+// reduction) + 1.5 us (the reduction kernel).  Measured on B200 over 20 shapes, the
+// tcgen05 kernels lose 1.2-1.7x whenever a split spills into a second wave (their
+// per-wave set-up, pipeline fill and epilogue are long), so for them (`one_wave`) only
+// one-wave counts are considered; the SIMT kernel's second wave costs only its share of
+// the work.  `smax` bounds the count (at least four K-blocks per slice).
+int choose_split(int64_t ctas, int64_t sms, double cta_s, double slab_bytes, int64_t smax, int requested,
+                 bool one_wave) {
   if (requested > 0) return requested > kMaxSplit ? kMaxSplit : requested;
-  if (tiles >= sms) return 1;
-  int64_t smax = K / (int64_t(bk) * 8);  // keep >= 8 K-steps per slice
+  if (ctas >= sms || ctas <= 0) return 1;
   if (smax > kMaxSplit) smax = kMaxSplit;
-  if (smax < 1) smax = 1;
-  const double tile_s = 2.0 * bm * bn * double(K) / flops_per_sm;  // one full-K tile on one SM
-  const double hbm = 6.0e12;                                          // bytes/s, reduction traffic
+  int64_t top = one_wave ? sms / ctas : smax;
+  if (top > smax) top = smax;
   int best = 1;
-  double best_cost = 1e30;
-  for (int64_t s = 1; s <= smax; ++s) {
-    const double waves = double(cdiv(tiles * s, sms));
-    double cost = waves * tile_s / double(s);
-    if (s > 1) cost += double(s) * double(M) * double(round_up(N, 4)) * 8.0 / hbm + 3.0e-6;
-    if (cost < best_cost * 0.999) {
+  double best_cost = cta_s;
+  for (int64_t sp = 2; sp <= top; ++sp) {
+    const double waves = double(cdiv(ctas * sp, sms));
+    const double cost = waves * cta_s / double(sp) + double(sp) * slab_bytes / 3.0e12 + 1.5e-6;
+    if (cost < best_cost) {
       best_cost = cost;
-      best = static_cast<int>(s);
+      best = static_cast<int>(sp);
     }
   }
   return best;
 }
+
+// Per-CTA time for the full K: the larger of its arithmetic (at `flops` per CTA) and its
+// operand streaming (at `bw` bytes/s per CTA).
+double cta_seconds(int64_t rows, int64_t cols, int64_t b_cols, int64_t K, double flops, double bw) {
+  const double compute = 2.0 * double(rows) * double(cols) * double(K) / flops;
+  const double stream = double(rows + b_cols) * double(K) * 4.0 / bw;
+  return compute > stream ? compute : stream;
+}
+
+// Measured per-SM rates on B200: 3xTF32 ~1.7 TFLOP/s (250 TFLOP/s / 148), TF32 ~4.3, SIMT
+// FMA ~0.31; HBM share ~38 GB/s per SM with every SM streaming.
+constexpr double kRate3x = 1.7e12, kRateTf32 = 4.3e12, kRateSimt = 0.31e12, kBwPerSm = 38.0e9;
 
 int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K,
               int64_t lda, int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg, Plan* p) {
@@ -270,8 +289,13 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
     p->pair = variant != TILEC_MM_TF32 && p->bn == 256 && M > 128 && M >= TILEC_PAIR_MIN_M;
     const int bk = variant == TILEC_MM_TF32 ? 32 : (p->pair ? 16 : k3xBK);
     const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
-    p->split = choose_split(tiles, M, N, K, kTcBM, p->bn, bk, d.sms, requested_split,
-                            variant == TILEC_MM_TF32 ? 4.0e12 : 1.4e12);
+    // The CTA pair launches two CTAs per 256-row x 256-column tile; each computes 128 rows
+    // and loads half of the B columns.
+    const int64_t ctas = p->pair ? 2 * cdiv(M, 256) * cdiv(N, 256) : tiles;
+    const double cta_s = cta_seconds(kTcBM, p->bn, p->pair ? p->bn / 2 : p->bn, K,
+                                     variant == TILEC_MM_TF32 ? kRateTf32 : kRate3x, kBwPerSm);
+    p->split = choose_split(ctas, d.sms, cta_s, double(M) * double(round_up(N, 4)) * 4.0, K / (int64_t(bk) * 4),
+                            requested_split, /*one_wave=*/true);
     p->k_chunk = round_up(cdiv(K, p->split), bk);
     p->split = static_cast<int>(cdiv(K, p->k_chunk > 0 ? p->k_chunk : 1));
     if (p->split < 1) p->split = 1;
@@ -279,8 +303,11 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
     p->bn = N <= 64 ? 64 : 128;
     const int64_t tiles = cdiv(M, kSimtBM) * cdiv(N, p->bn);
     int split = 1;
-    if (variant == TILEC_MM_SPLITK)
-      split = choose_split(tiles, M, N, K, kSimtBM, p->bn, kSimtBK, d.sms, requested_split, 0.3e12);
+    if (variant == TILEC_MM_SPLITK) {
+      const double cta_s = cta_seconds(kSimtBM, p->bn, p->bn, K, kRateSimt, kBwPerSm);
+      split = choose_split(tiles, d.sms, cta_s, double(M) * double(round_up(N, 4)) * 4.0, K / (int64_t(kSimtBK) * 4),
+                           requested_split, /*one_wave=*/false);
+    }
     p->k_chunk = round_up(cdiv(K, split), kSimtBK);
     split = static_cast<int>(cdiv(K, p->k_chunk > 0 ? p->k_chunk : 1));
     p->split = split < 1 ? 1 : split;
@@ -346,6 +373,56 @@ int encode_maps(const float* A, const float* B, int64_t M, int64_t N, int64_t K,
   return TILEC_OK;
 }
 
+// Programmatic dependent launch is on unless TILEC_MM_PDL=0 (read once per process).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("TILEC_MM_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Launches `kern`, with programmatic stream serialisation when `pdl` (every kernel here
+// calls pdl_wait() before touching global memory) and, when cluster_x > 1, a cluster of
+// cluster_x CTAs along x.
+template <typename... KArgs, typename... Args>
+int launch_kx(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, int cluster_x,
+              Args... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = s;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl && pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  lc.attrs = attr;
+  lc.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&lc, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return TILEC_ERR_LAUNCH;
+  }
+  return launch_status();
+}
+
+template <typename... KArgs, typename... Args>
+int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, int cluster_x,
+             Args... args) {
+  return launch_kx(true, kern, grid, block, smem, s, cluster_x, args...);
+}
+
 template <int BN, int BK, int STAGES, bool SPLIT3, bool HI>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N, int64_t ldo,
               int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, cudaStream_t s) {
@@ -354,10 +431,9 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t 
   const int n_tiles = static_cast<int>(cdiv(N, BN));
   const int group_m = 16;
   dim3 grid(static_cast<unsigned>(int64_t(m_tiles) * n_tiles), 1, static_cast<unsigned>(split));
-  tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI><<<grid, Cfg::kThreads, Cfg::kSmemBytes, s>>>(
-      ma, mb, out, static_cast<int>(M), static_cast<int>(N), ldo, slab, static_cast<int>(K),
-      static_cast<int>(k_chunk), m_tiles, n_tiles, group_m, vec_out);
-  return launch_status();
+  return launch_k(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 1, ma,
+                  mb, out, static_cast<int>(M), static_cast<int>(N), ldo, slab, static_cast<int>(K),
+                  static_cast<int>(k_chunk), m_tiles, n_tiles, group_m, vec_out);
 }
 
 template <int BN, bool SPLIT3, bool HI>
@@ -378,26 +454,10 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t
   const int mp_tiles = static_cast<int>(cdiv(M, 256));
   const int n_tiles = static_cast<int>(cdiv(N, 256));
   const int group_m = 8;
-  cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3(static_cast<unsigned>(2 * int64_t(mp_tiles) * n_tiles), 1, static_cast<unsigned>(split));
-  lc.blockDim = dim3(Cfg::kThreads, 1, 1);
-  lc.dynamicSmemBytes = Cfg::kSmemBytes;
-  lc.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  lc.attrs = attr;
-  lc.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&lc, tc2_gemm_kernel<256, kPairStages, HI>, ma, mb, out, static_cast<int>(M),
-                                           static_cast<int>(N), ldo, slab, static_cast<int>(K),
-                                           static_cast<int>(k_chunk), mp_tiles, n_tiles, group_m, vec_out);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return TILEC_ERR_LAUNCH;
-  }
-  return launch_status();
+  const dim3 grid(static_cast<unsigned>(2 * int64_t(mp_tiles) * n_tiles), 1, static_cast<unsigned>(split));
+  return launch_k(tc2_gemm_kernel<256, kPairStages, HI>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 2, ma, mb,
+                  out, static_cast<int>(M), static_cast<int>(N), ldo, slab, static_cast<int>(K),
+                  static_cast<int>(k_chunk), mp_tiles, n_tiles, group_m, vec_out);
 }
 
 template <bool SPLIT3, bool HI>
@@ -414,6 +474,8 @@ int dispatch_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, float* 
 __global__ void __launch_bounds__(256) pack_rows_kernel(const float* __restrict__ src, int64_t lds,
                                                         float* __restrict__ dst, int64_t ldd, int64_t rows,
                                                         int64_t cols) {
+  pdl_wait();
+  pdl_launch_dependents();
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* s = src + r * lds;
     float* d = dst + r * ldd;
@@ -425,21 +487,63 @@ int launch_pack(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t 
                 const DeviceInfo& d, cudaStream_t s) {
   int64_t blocks = rows < int64_t(d.sms) * 16 ? rows : int64_t(d.sms) * 16;
   if (blocks < 1) blocks = 1;
-  pack_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(src, lds, dst, ldd, rows, cols);
-  return launch_status();
+  return launch_k(pack_rows_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, 1, src, lds, dst, ldd, rows,
+                  cols);
+}
+
+template <int P>
+int launch_reduce_p(int U, dim3 grid, const float* ws, float* C, int64_t M, int64_t N, int64_t ldw, int64_t ldc,
+                    int64_t slab, int split, int vec_out, cudaStream_t s) {
+  switch (U) {
+    case 4: return launch_k(splitk_reduce_kernel<P, 4>, grid, dim3(256), 0, s, 1, ws, C, M, N, ldw, ldc, slab, split, vec_out);
+    case 2: return launch_k(splitk_reduce_kernel<P, 2>, grid, dim3(256), 0, s, 1, ws, C, M, N, ldw, ldc, slab, split, vec_out);
+    default: return launch_k(splitk_reduce_kernel<P, 1>, grid, dim3(256), 0, s, 1, ws, C, M, N, ldw, ldc, slab, split, vec_out);
+  }
 }
 
 int launch_reduce(const float* ws, float* C, int64_t M, int64_t N, int64_t ldw, int64_t ldc, int split,
                   const DeviceInfo& d, cudaStream_t s) {
+  const int P = split >= 8 ? 8 : (split >= 4 ? 4 : (split >= 2 ? 2 : 1));
+  const int64_t G = 256 / P;
   const int64_t groups = M * cdiv(N, 4);
-  int64_t blocks = cdiv(groups, 128);
-  const int64_t cap = int64_t(d.sms) * 16;
-  if (blocks > cap) blocks = cap;
+  const int64_t resident = int64_t(d.sms) * 8;  // 256-thread blocks resident at once
+  const int U = groups <= resident * G ? 1 : (groups <= 2 * resident * G ? 2 : 4);
+  int64_t blocks = cdiv(groups, G * U);
+  if (blocks > resident) blocks = resident;
   if (blocks < 1) blocks = 1;
   const int vec_out = aligned16(C) && (ldc % 4 == 0);
-  splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 128, 0, s>>>(ws, C, M, N, ldw, ldc, M * ldw, split,
-                                                                     vec_out);
-  return launch_status();
+  const dim3 grid(static_cast<unsigned>(blocks));
+  const int64_t slab = M * ldw;
+  switch (P) {
+    case 8: return launch_reduce_p<8>(U, grid, ws, C, M, N, ldw, ldc, slab, split, vec_out, s);
+    case 4: return launch_reduce_p<4>(U, grid, ws, C, M, N, ldw, ldc, slab, split, vec_out, s);
+    case 2: return launch_reduce_p<2>(U, grid, ws, C, M, N, ldw, ldc, slab, split, vec_out, s);
+    default: return launch_reduce_p<1>(U, grid, ws, C, M, N, ldw, ldc, slab, split, vec_out, s);
+  }
+}
+
+int launch_fill_zero(float* C, int64_t M, int64_t N, int64_t ldc, const DeviceInfo& d, cudaStream_t s) {
+  int64_t blocks = cdiv(M * N, 256);
+  if (blocks > int64_t(d.sms) * 8) blocks = int64_t(d.sms) * 8;
+  return launch_k(fill_zero_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, 1, C, M, N, ldc);
+}
+
+int launch_simt(int bn, bool vec, dim3 grid, const float* A, const float* B, float* out, int64_t M, int64_t N,
+                int64_t K, int64_t lda, int64_t ldb, int64_t ldo, int64_t slab, int64_t k_chunk, int vec_out,
+                cudaStream_t s) {
+  // Launched without programmatic serialisation: a SIMT CTA fits twice on an SM, and CTAs
+  // placed while the previous kernel still occupies the GPU were measured to double up on
+  // some SMs (a 128-CTA grid ran 40% slower).
+  const dim3 block(kSimtThreads);
+  auto go = [&](auto kern, size_t smem) {
+    return launch_kx(false, kern, grid, block, smem, s, 1, A, B, out, M, N, K, lda, ldb, ldo, slab, k_chunk,
+                     vec_out);
+  };
+  if (bn == 64)
+    return vec ? go(simt_gemm_kernel<64, true>, simt_smem_bytes<64>())
+               : go(simt_gemm_kernel<64, false>, simt_smem_bytes<64>());
+  return vec ? go(simt_gemm_kernel<128, true>, simt_smem_bytes<128>())
+             : go(simt_gemm_kernel<128, false>, simt_smem_bytes<128>());
 }
 
 }  // namespace
@@ -490,12 +594,7 @@ int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-  if (K == 0) {
-    int64_t blocks = cdiv(M * N, 256);
-    if (blocks > int64_t(d->sms) * 8) blocks = int64_t(d->sms) * 8;
-    fill_zero_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(C, M, N, ldc);
-    return launch_status();
-  }
+  if (K == 0) return launch_fill_zero(C, M, N, ldc, *d, s);
 
   Plan p;
   rc = make_plan(*d, A, B, C, M, N, K, lda, ldb, ldc, cfg, &p);
@@ -530,22 +629,7 @@ int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
     const int64_t mt = cdiv(M, kSimtBM), nt = cdiv(N, p.bn);
     if (nt > 65535) return TILEC_ERR_UNSUPPORTED;
     dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(p.split));
-    if (p.bn == 64) {
-      if (vec)
-        simt_gemm_kernel<64, true><<<grid, kSimtThreads, simt_smem_bytes<64>(), s>>>(
-            A, B, out, M, N, K, lda, ldb, ldo, slab, p.k_chunk, vec_out);
-      else
-        simt_gemm_kernel<64, false><<<grid, kSimtThreads, simt_smem_bytes<64>(), s>>>(
-            A, B, out, M, N, K, lda, ldb, ldo, slab, p.k_chunk, vec_out);
-    } else {
-      if (vec)
-        simt_gemm_kernel<128, true><<<grid, kSimtThreads, simt_smem_bytes<128>(), s>>>(
-            A, B, out, M, N, K, lda, ldb, ldo, slab, p.k_chunk, vec_out);
-      else
-        simt_gemm_kernel<128, false><<<grid, kSimtThreads, simt_smem_bytes<128>(), s>>>(
-            A, B, out, M, N, K, lda, ldb, ldo, slab, p.k_chunk, vec_out);
-    }
-    rc = launch_status();
+    rc = launch_simt(p.bn, vec, grid, A, B, out, M, N, K, lda, ldb, ldo, slab, p.k_chunk, vec_out, s);
   } else {
     CUtensorMap ma, mb;
     const int bk = p.variant == TILEC_MM_TF32 ? 32 : (p.pair ? 16 : k3xBK);
@@ -658,12 +742,7 @@ extern "C" int tilec_mm_f32_splitk_noalloc(const float* A, const float* B, float
   rc = current_device(&d);
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (K == 0) {
-    int64_t blocks = cdiv(M * N, 256);
-    if (blocks > int64_t(d->sms) * 8) blocks = int64_t(d->sms) * 8;
-    fill_zero_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(C, M, N, ldc);
-    return launch_status();
-  }
+  if (K == 0) return launch_fill_zero(C, M, N, ldc, *d, s);
   float* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;
@@ -679,7 +758,9 @@ extern "C" int tilec_mm_f32_splitk_noalloc(const float* A, const float* B, float
     split = split_k > kMaxSplit ? kMaxSplit : split_k;
     if (split > 1 && split > fit) return TILEC_ERR_TOO_LARGE;
   } else {
-    split = choose_split(mt * nt, M, N, K, kSimtBM, bn, kSimtBK, d->sms, 0, 0.3e12);
+    const double cta_s = cta_seconds(kSimtBM, bn, bn, K, kRateSimt, kBwPerSm);
+    split = choose_split(mt * nt, d->sms, cta_s, double(slab) * 4.0, K / (int64_t(kSimtBK) * 4), 0,
+                         /*one_wave=*/false);
     if (split > fit) split = fit < 1 ? 1 : fit;
   }
   const int64_t k_chunk = round_up(cdiv(K, split), kSimtBK);
@@ -691,22 +772,7 @@ extern "C" int tilec_mm_f32_splitk_noalloc(const float* A, const float* B, float
   const int vec_out = split > 1 ? 1 : (aligned16(C) && (ldc % 4 == 0) ? 1 : 0);
   const bool vec = aligned16(A) && aligned16(B) && (lda % 4 == 0) && (ldb % 4 == 0);
   dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(split));
-  if (bn == 64) {
-    if (vec)
-      simt_gemm_kernel<64, true><<<grid, kSimtThreads, simt_smem_bytes<64>(), s>>>(A, B, out, M, N, K, lda, ldb,
-                                                                                  ldo, out_slab, k_chunk, vec_out);
-    else
-      simt_gemm_kernel<64, false><<<grid, kSimtThreads, simt_smem_bytes<64>(), s>>>(A, B, out, M, N, K, lda, ldb,
-                                                                                   ldo, out_slab, k_chunk, vec_out);
-  } else {
-    if (vec)
-      simt_gemm_kernel<128, true><<<grid, kSimtThreads, simt_smem_bytes<128>(), s>>>(A, B, out, M, N, K, lda, ldb,
-                                                                                    ldo, out_slab, k_chunk, vec_out);
-    else
-      simt_gemm_kernel<128, false><<<grid, kSimtThreads, simt_smem_bytes<128>(), s>>>(
-          A, B, out, M, N, K, lda, ldb, ldo, out_slab, k_chunk, vec_out);
-  }
-  rc = launch_status();
+  rc = launch_simt(bn, vec, grid, A, B, out, M, N, K, lda, ldb, ldo, out_slab, k_chunk, vec_out, s);
   if (rc || split == 1) return rc;
   return launch_reduce(scratch, C, M, N, ldw, ldc, static_cast<int>(split), *d, s);
 }
