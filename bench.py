@@ -47,7 +47,7 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--variant", default="auto")
     p.add_argument("--panels", type=int, default=2)
-    p.add_argument("--e2e-chunks", type=int, default=8)
+    p.add_argument("--e2e-chunks", type=int, default=16)
     p.add_argument("--no-extra", action="store_true", help="skip the configs 1-3 single-GPU figures")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (debug only)")
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end measurement (debug only)")
@@ -212,6 +212,42 @@ def reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def pcie_rates(h_buf, dev, world):
+    """Host<->device copy rates (GB/s) on a 512 MiB slice of pinned `h_buf`: each direction
+    alone, then both at once (every rank at the same time when world > 1)."""
+    n = min(h_buf.numel(), 128 * 2 ** 20)
+    h = h_buf.view(-1)[:n]
+    d = torch.empty(n, device=dev)
+    d2 = torch.empty(n, device=dev)
+    h_back = torch.empty(n, pin_memory=True)
+    side = torch.cuda.Stream(device=dev)
+
+    def rate(fn):
+        fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(3):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return round(3 * 4 * n / (s.elapsed_time(e) * 1e6), 1)
+
+    def both():
+        side.wait_stream(torch.cuda.current_stream())
+        d.copy_(h, non_blocking=True)
+        with torch.cuda.stream(side):
+            h_back.copy_(d2, non_blocking=True)
+        torch.cuda.current_stream().wait_stream(side)
+    out = {"h2d_GBps": rate(lambda: d.copy_(h, non_blocking=True)),
+           "d2h_GBps": rate(lambda: h_back.copy_(d2, non_blocking=True)),
+           "concurrent_each_GBps": rate(both)}
+    del d, d2
+    return out
+
+
 def time_launches(fn, reps, warm=10):
     """Mean CUDA-event time (ms) of fn() over reps back-to-back calls on the current stream."""
     for _ in range(warm):
@@ -363,14 +399,12 @@ def main():
     value = flops_step * args.steps / (ms_total * 1e-3) / 1e12
 
     pk = peaks()
-    # Sustained (power-capped) peak when the clock record shows the power cap during the
-    # timed region, burst peak otherwise.
-    capped = bool(clk and "sw_power_cap" in clk.get("reasons", []))
-    if world > 1:
-        flag = torch.tensor([1.0 if capped else 0.0], device=dev)
-        dist.broadcast(flag, src=0)
-        capped = bool(flag.item())
-    peak, peak_note = variant_peak(variant, pk, sustained=capped)
+    # The timed region is K launches of one GEMM (well under a second), so the burst peak
+    # is the denominator.  The sustained figure (cuBLAS bf16 back to back for seconds, at
+    # a lower power-capped clock) is reported beside it: this kernel holds a higher clock
+    # under the same cap, so the fraction against it can exceed 1.
+    peak, peak_note = variant_peak(variant, pk, sustained=False)
+    peak_sus, _ = variant_peak(variant, pk, sustained=True)
     flops_launch = 2.0 * rows * panel_w * K5
     bytes_launch = 4.0 * (rows * K5 + K5 * panel_w + rows * panel_w)
     achieved = flops_launch / (gemm_ms_max * 1e-3) / 1e12
@@ -421,9 +455,15 @@ def main():
         e2e = {"value": round(flops_step / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT,
                "h2d_bytes_per_step": int(4 * M5 * K5 + 4 * K5 * N5), "d2h_bytes_per_step": int(4 * M5 * N5),
                "ms_per_step": round(e2e_ms, 3), "steps": n_e2e,
-               "path": "RowShardedMatmul.run_host: pinned host x2 (rank 0) and x1 rows -> device in %d row "
-                       "chunks, H2D / GEMM / D2H overlapped on 3 streams, C rows -> pinned host, synchronised "
-                       "each step; this rank's h2d: %d bytes" % (args.e2e_chunks, h2d)}
+               "path": "RowShardedMatmul.run_host: pinned host x2 (rank 0) and x1 rows -> device in %d tapered "
+                       "row chunks, H2D / GEMM / D2H overlapped on 3 streams, C rows -> pinned host, synchronised "
+                       "each step; this rank's h2d: %d bytes" % (len(ext._row_chunks(rows, args.e2e_chunks)), h2d)}
+        link = pcie_rates(h_x1, dev, world)
+        d2h_rank = 4 * rows * N5
+        floor_ms = max(h2d, d2h_rank) / (link["concurrent_each_GBps"] * 1e6)
+        e2e["link"] = dict(link, bound="host link (PCIe): this rank's larger copy direction at the concurrent "
+                                        "H2D+D2H rate", floor_ms=round(floor_ms, 3),
+                           frac_of_floor=round(floor_ms / e2e_ms, 4))
 
     extra = None
     cpu = None
@@ -453,7 +493,10 @@ def main():
                          "kernel": (f"{'tc2_gemm (CTA pair)' if variant.startswith('3xtf32') and rows >= 256 and panel_w > 128 else 'tc_gemm'}"
                                     f" ({variant}) on [{rows},{K5}] @ [{K5},{panel_w}]"),
                          "launch_ms": round(gemm_ms_max, 4), "peak_note": peak_note + " (of measured)"
-                         if pk["src"] == "measured" else peak_note},
+                         if pk["src"] == "measured" else peak_note,
+                         "frac_of_sustained": round(achieved / peak_sus, 4),
+                         "sustained_note": "measured bf16 sustained (seconds back to back, power-capped clock) "
+                                           "on the same pipe; the clocks line gives this run's SM clock"},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": int(launches_per_step * args.steps),

@@ -107,9 +107,22 @@ TILEC_API int tilec_mm_plan(const float* A, const float* B, const float* C,
  * the table (built-in rules apply).  Not thread-safe against concurrent calls. */
 TILEC_API int tilec_mm_set_table(const int32_t* rows, int32_t nrows);
 
+/* Bits of the device status word. */
+#define TILEC_DEV_STATUS_TIMEOUT 1    /* a bounded wait gave up (time limit); the kernel unwound */
+#define TILEC_DEV_STATUS_TMEM 2       /* TMEM allocation returned an unexpected address */
+#define TILEC_DEV_STATUS_BAD_LAUNCH 4 /* a kernel was launched with a block shape it was not built for */
+
 /* Read and clear the device status word of the current device (0 = clean).
  * Synchronises `stream`. */
 TILEC_API int tilec_mm_device_status(void* stream, int32_t* status_out);
+
+/* Failure-detection self-test (no counterpart in the reference).  Launches one CTA on
+ * `stream` that waits on a shared-memory mbarrier nothing ever arrives on, through the
+ * same bounded wait every GEMM kernel uses, with a limit of `limit_ns` nanoseconds
+ * (clamped to [1 ms, 2 s]).  The wait gives up, records TILEC_DEV_STATUS_TIMEOUT and the
+ * kernel returns: no trap, no fault, the context stays usable.  Returns the launch status;
+ * read the outcome with tilec_mm_device_status. */
+TILEC_API int tilec_mm_selftest_wait(int64_t limit_ns, void* stream);
 
 /* Text for a tilec_status code (static storage). */
 TILEC_API const char* tilec_strerror(int code);

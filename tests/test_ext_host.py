@@ -65,3 +65,29 @@ def test_cdiv_and_configs():
     assert all(v in ("simt", "splitk", "tf32", "3xtf32") for v, _ in cfgs)
     # misaligned shapes still get tensor-core candidates (their operands are packed first)
     assert ("3xtf32", 1) in ext.mm_configs(1000, 3001, 777)
+
+
+@pytest.mark.parametrize("M,chunks", [(65536, 8), (65536, 16), (8192, 3), (4096, 4), (1000, 8), (300, 2), (1, 8),
+                                      (100000, 7)])
+def test_row_chunks_cover_rows_in_order(M, chunks):
+    spans = ext._row_chunks(M, chunks)
+    assert spans[0][0] == 0 and spans[-1][1] == M
+    assert all(a < b for a, b in spans)
+    assert all(spans[i][1] == spans[i + 1][0] for i in range(len(spans) - 1))
+    # every span but the last starts on a 256-row (CTA-pair tile) boundary
+    assert all(a % 256 == 0 for a, _ in spans)
+
+
+def test_row_chunks_taper_both_ends():
+    sizes = [b - a for a, b in ext._row_chunks(65536, 8)]
+    assert sizes[:3] == [2048, 2048, 4096] and sizes[-3:] == [4096, 2048, 2048]
+    assert set(sizes[3:-3]) == {8192}
+    assert [b - a for a, b in ext._row_chunks(65536, 8, taper=False)] == [8192] * 8
+
+
+def test_row_chunks_explicit_sizes():
+    assert ext._row_chunks(10, [3, 7]) == [(0, 3), (3, 10)]
+    with pytest.raises(ValueError):
+        ext._row_chunks(10, [3, 6])
+    with pytest.raises(ValueError):
+        ext._row_chunks(10, [0, 10])

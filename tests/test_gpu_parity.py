@@ -242,6 +242,21 @@ def test_matrix_mul_host_pipelined(chunks):
         ext.matrix_mul_host(x1.to(DEV), x2)
 
 
+@pytest.mark.parametrize("chunks", (4, 16, [100, 156, 3840], [4000, 96], [1536, 2560]))
+@pytest.mark.parametrize("shape", [(4096, 1024, 1024), (4096, 2048, 64), (4096, 999, 333)])
+def test_matrix_mul_host_equals_device_bitwise(shape, chunks):
+    """Chunked host-buffer product (tapered or explicit spans, chunks below one 256-row
+    CTA-pair tile included) = the unchunked device product, bit for bit: every chunk runs
+    the kernel and K split planned for the full product."""
+    m, k, n = shape
+    g = torch.Generator().manual_seed(m + k + n)
+    x1 = torch.randn(m, k, generator=g).pin_memory()
+    x2 = torch.randn(k, n, generator=g).pin_memory()
+    want = ext.matrix_mul(x1.to(DEV), x2.to(DEV)).cpu()
+    got = ext.matrix_mul_host(x1, x2, chunks=chunks)
+    assert torch.equal(got, want)
+
+
 @pytest.mark.parametrize("split_k", (1, 2, 3, 7))
 @pytest.mark.parametrize("shape", [(1024, 4096, 1024), (300, 2000, 520), (777, 1000, 333)])
 def test_cta_pair_kernel(shape, split_k):
@@ -323,4 +338,25 @@ def test_back_to_back_launches_in_a_graph(variant, split_k):
     for g_, r in zip(got, outs + mids):
         assert torch.equal(g_, r)
     del graph
+    assert _status_clean()
+
+
+def test_bounded_wait_times_out_and_context_survives():
+    """Failure detection without a fault: a wait on a barrier nothing arrives on gives up
+    after its limit (50 ms here), the kernel records TILEC_DEV_STATUS_TIMEOUT and returns;
+    the host reads the status, and the same context then computes a product correctly."""
+    import time
+    lib = _native.load()
+    assert _status_clean()
+    t0 = time.perf_counter()
+    _native.check(lib.tilec_mm_selftest_wait(50_000_000, None), "selftest_wait")
+    st = ctypes.c_int32(-1)
+    _native.check(lib.tilec_mm_device_status(None, ctypes.byref(st)), "device_status")
+    waited = time.perf_counter() - t0
+    assert st.value == 1, st.value               # TILEC_DEV_STATUS_TIMEOUT
+    assert 0.04 <= waited < 1.5, waited          # gave up near its limit, not the 2 s default
+    assert _status_clean()                       # reading cleared it
+    x1, x2 = _config_inputs(gen.CONFIG1, 6)
+    got = _run(x1, x2, "3xtf32")
+    assert oracle.rel_frob(got, oracle.mm_tiled(x1.numpy(), x2.numpy())) <= 1e-5
     assert _status_clean()

@@ -24,7 +24,7 @@ VARIANT_NAMES = {v: k for k, v in VARIANTS.items()}
 EXPORTS = [
     "tilec_mm_f32", "tilec_mm_workspace_bytes", "tilec_mm_plan", "tilec_mm_set_table",
     "tilec_mm_device_status", "tilec_strerror", "tilec_mm_abi_version", "tilec_mm_built_arch",
-    "tilec_mm_f32_splitk_noalloc",
+    "tilec_mm_f32_splitk_noalloc", "tilec_mm_selftest_wait",
 ]
 
 
@@ -82,6 +82,8 @@ def load():
         lib.tilec_mm_built_arch.restype = ctypes.c_int
         lib.tilec_mm_f32_splitk_noalloc.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int32, vp]
         lib.tilec_mm_f32_splitk_noalloc.restype = ctypes.c_int
+        lib.tilec_mm_selftest_wait.argtypes = [i64, vp]
+        lib.tilec_mm_selftest_wait.restype = ctypes.c_int
         _lib = lib
         return _lib
 

@@ -88,14 +88,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait for the phase with the given parity.  `abort_flag` (shared) lets
 // one role that gave up release every other role quickly.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         record_status(TILEC_DEV_TIMEOUT);
         return false;

@@ -25,6 +25,10 @@
 #include "tc_gemm.cuh"
 #include "tc2_gemm.cuh"
 
+static_assert(TILEC_DEV_STATUS_TIMEOUT == tilec::TILEC_DEV_TIMEOUT && TILEC_DEV_STATUS_TMEM == tilec::TILEC_DEV_TMEM &&
+                  TILEC_DEV_STATUS_BAD_LAUNCH == tilec::TILEC_DEV_BAD_LAUNCH,
+              "status bits in include/tilec_mm.h match the device enum");
+
 namespace tilec {
 namespace {
 
@@ -522,6 +526,22 @@ int launch_reduce(const float* ws, float* C, int64_t M, int64_t N, int64_t ldw, 
   }
 }
 
+// One warp waits, through mbar_wait, for phase 0 of a barrier nothing arrives on; the wait
+// must give up after limit_ns and record TILEC_DEV_TIMEOUT (tilec_mm_selftest_wait).
+__global__ void __launch_bounds__(32) selftest_wait_kernel(unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  pdl_wait();
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, limit_ns);
+  __syncwarp();
+}
+
 int launch_fill_zero(float* C, int64_t M, int64_t N, int64_t ldc, const DeviceInfo& d, cudaStream_t s) {
   int64_t blocks = cdiv(M * N, 256);
   if (blocks > int64_t(d.sms) * 8) blocks = int64_t(d.sms) * 8;
@@ -660,6 +680,15 @@ int tilec_mm_set_table(const int32_t* rows, int32_t nrows) {
   std::lock_guard<std::mutex> lk(g_table_mu);
   g_table.assign(rows, rows + size_t(nrows) * 8);
   return TILEC_OK;
+}
+
+int tilec_mm_selftest_wait(int64_t limit_ns, void* stream) {
+  DeviceInfo* d = nullptr;
+  const int rc = current_device(&d);
+  if (rc) return rc;
+  unsigned long long lim = limit_ns < 1000000 ? 1000000ull : static_cast<unsigned long long>(limit_ns);
+  if (lim > kWaitLimitNs) lim = kWaitLimitNs;
+  return launch_k(selftest_wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), 1, lim);
 }
 
 int tilec_mm_device_status(void* stream, int32_t* status_out) {

@@ -121,7 +121,7 @@ class RowShardedMatmul:
             return gather_rows(out, M, self.group)
         return out
 
-    def run_host(self, h_x1_shard, h_x2=None, h_out=None, chunks=4, sync=True):
+    def run_host(self, h_x1_shard, h_x2=None, h_out=None, chunks=16, sync=True):
         """Host-buffer variant: x2 (rank src) and this rank's rows of x1 come from host memory
         and this rank's rows of C go back to it.  x2 is copied to the device and broadcast in
         panels first; then row chunks of x1 stream through H2D -> GEMM (all panels) -> D2H
@@ -137,7 +137,7 @@ class RowShardedMatmul:
                 d_x2 = torch.empty(self.K, self.N, dtype=torch.float32, device=dev)
                 d_x2.copy_(h_x2, non_blocking=True)
             if self.world == 1:
-                ext.pipelined_rows(h_x1_shard, h_out, dev, lambda a, c: ext._matrix_mul(a, d_x2, out=c),
+                ext.pipelined_rows(h_x1_shard, h_out, dev, lambda d_x1, d_out: ext.chunk_compute(d_x1, d_x2),
                                    chunks=chunks, sync=sync)
                 return h_out
             if self.rank == self.src:
@@ -148,10 +148,14 @@ class RowShardedMatmul:
                 for w in works:
                     w.wait()
 
-            def compute(a, c):
-                for (n0, n1), buf in zip(self.bounds, self.bufs):
-                    ext._matrix_mul(a, buf, out=c[:, n0:n1])
-            ext.pipelined_rows(h_x1_shard, h_out, dev, compute, chunks=chunks, before=waited, sync=sync)
+            def make_compute(d_x1, d_out):
+                parts = [((n0, n1), ext.chunk_compute(d_x1, buf)) for (n0, n1), buf in zip(self.bounds, self.bufs)]
+
+                def compute(a, c):
+                    for (n0, n1), fn in parts:
+                        fn(a, c[:, n0:n1])
+                return compute
+            ext.pipelined_rows(h_x1_shard, h_out, dev, make_compute, chunks=chunks, before=waited, sync=sync)
         return h_out
 
 

@@ -191,24 +191,54 @@ def _side_streams(dev):
     return _SIDE_STREAMS[dev]
 
 
-def _row_chunks(M, chunks, align=128):
-    chunks = max(1, min(int(chunks), max(1, M // align)))
-    step = -(-M // chunks)
-    step = -(-step // align) * align
-    return [(r, min(M, r + step)) for r in range(0, M, step)]
+def _row_chunks(M, chunks, align=256, taper=True, min_rows=1024):
+    """Row spans for pipelined_rows.  `chunks` is a count (equal spans rounded up to
+    `align` rows, one 256-row CTA-pair tile, and at least `min_rows` rows so each span's
+    GEMM still fills the GPU) or an explicit sequence of row counts.
+
+    With taper, the first and last equal spans are cut into quarters, a quarter and a half
+    (head: 1/4, 1/4, 1/2; tail: 1/2, 1/4, 1/4).  While host<->device copies bound the
+    pipeline, a step ends at "last H2D + GEMM of the last span + its D2H" and the first
+    GEMM waits for the first span, so short end spans shorten the fill and the drain while
+    the middle spans stay large enough to fill whole waves of the GPU."""
+    if not isinstance(chunks, int):
+        sizes = [int(c) for c in chunks]
+        if any(c <= 0 for c in sizes) or sum(sizes) != M:
+            raise ValueError(f"chunk sizes {sizes} must be positive and sum to {M}")
+    else:
+        n = max(1, min(int(chunks), max(1, M // max(align, min_rows))))
+        step = -(-M // n)
+        step = -(-step // align) * align
+        sizes = [min(step, M - r) for r in range(0, M, step)]
+        if taper and len(sizes) >= 3:
+            q = (step // 4) // align * align
+            if q >= align:
+                head = [q, q, sizes[0] - 2 * q]
+                last = sizes[-1]
+                half, quarter = (last // 2) // align * align, (last // 4) // align * align
+                tail = [half, quarter, last - half - quarter] if quarter >= align else [last]
+                sizes = head + sizes[1:-1] + tail
+    spans, r = [], 0
+    for c in sizes:
+        spans.append((r, r + c))
+        r += c
+    return spans
 
 
-def pipelined_rows(h_x1, h_out, dev, compute, chunks=8, before=None, sync=True):
+def pipelined_rows(h_x1, h_out, dev, make_compute, chunks=16, before=None, sync=True):
     """Stream host rows through the GPU: H2D of chunk i+1, compute(chunk i) and D2H of
     chunk i-1 overlap on three streams (copies on two side streams, compute on the current
-    stream).  compute(d_x1_rows, d_out_rows) launches the work for one chunk of rows;
-    before() (optional) runs on the current stream first (e.g. staging x2)."""
+    stream).  make_compute(d_x1, d_out) receives the full-size device buffers (so the
+    caller can plan the unchunked product) and returns compute(d_x1_rows, d_out_rows),
+    which launches the work for one chunk of rows; before() (optional) runs on the
+    current stream first (e.g. staging x2).  `chunks`: see _row_chunks."""
     M, K = h_x1.shape
     N = h_out.shape[1]
     cur = torch.cuda.current_stream(dev)
     h2d, d2h = _side_streams(dev)
     d_x1 = torch.empty(M, K, dtype=torch.float32, device=dev)
     d_out = torch.empty(M, N, dtype=torch.float32, device=dev)
+    compute = make_compute(d_x1, d_out)
     h2d.wait_stream(cur)
     d2h.wait_stream(cur)
     spans = _row_chunks(M, chunks)
@@ -233,12 +263,13 @@ def pipelined_rows(h_x1, h_out, dev, compute, chunks=8, before=None, sync=True):
     return h_out
 
 
-def matrix_mul_host(x1, x2, out=None, chunks=8, device=None, sync=True):
+def matrix_mul_host(x1, x2, out=None, chunks=16, device=None, sync=True):
     """C = x1 @ x2 for float32 tensors in host memory, computed on the GPU.
 
     The same product as matrix_mul, for data that lives on the host: x2 is copied once,
     then row chunks of x1 are copied in, multiplied and copied back with the three
-    overlapping (use pinned tensors for asynchronous copies).  Returns `out` (a new pinned
+    overlapping (use pinned tensors for asynchronous copies).  `chunks` is a count
+    (tapered spans, see _row_chunks) or a sequence of row counts.  Returns `out` (a new pinned
     [M, N] tensor by default), complete when the call returns (sync=True) or once the
     current stream is synchronised (sync=False).
     """
@@ -259,5 +290,13 @@ def matrix_mul_host(x1, x2, out=None, chunks=8, device=None, sync=True):
     with torch.cuda.device(dev):
         d_x2 = torch.empty(K, N, dtype=torch.float32, device=dev)
         d_x2.copy_(x2.contiguous(), non_blocking=True)
-        pipelined_rows(x1, out, dev, lambda a, c: _matrix_mul(a, d_x2, out=c), chunks=chunks, sync=sync)
+        pipelined_rows(x1, out, dev, lambda d_x1, d_out: chunk_compute(d_x1, d_x2), chunks=chunks, sync=sync)
     return out
+
+
+def chunk_compute(d_x1, d_x2, variant=None, split_k=0):
+    """compute(rows_of_x1, rows_of_out) for one row chunk of the product d_x1 @ d_x2 with
+    the kernel and K split that the unchunked product uses (planned once on the full-size
+    buffers), so a chunked product equals the unchunked one bit for bit."""
+    v, s = plan(d_x1, d_x2, variant=variant, split_k=split_k)
+    return lambda a, c: _matrix_mul(a, d_x2, variant=v, split_k=s, out=c)
