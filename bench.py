@@ -459,11 +459,19 @@ def main():
                        "row chunks, H2D / GEMM / D2H overlapped on 3 streams, C rows -> pinned host, synchronised "
                        "each step; this rank's h2d: %d bytes" % (len(ext._row_chunks(rows, args.e2e_chunks)), h2d)}
         link = pcie_rates(h_x1, dev, world)
-        d2h_rank = 4 * rows * N5
-        floor_ms = max(h2d, d2h_rank) / (link["concurrent_each_GBps"] * 1e6)
-        e2e["link"] = dict(link, bound="host link (PCIe): this rank's larger copy direction at the concurrent "
-                                        "H2D+D2H rate", floor_ms=round(floor_ms, 3),
-                           frac_of_floor=round(floor_ms / e2e_ms, 4))
+        if world == 1:
+            floor_ms = max(h2d, 4 * rows * N5) / (link["concurrent_each_GBps"] * 1e6)
+            bound = "host link (PCIe): the larger copy direction at the measured concurrent H2D+D2H rate"
+        else:
+            # All ranks' copies share the host side: total bytes over the summed rates that
+            # the ranks measured while all copying at once.
+            agg = torch.tensor([2.0 * link["concurrent_each_GBps"]], device=dev, dtype=torch.float64)
+            dist.all_reduce(agg)
+            link["aggregate_GBps"] = round(agg.item(), 1)
+            floor_ms = (4.0 * (M5 * K5 + K5 * N5 + M5 * N5)) / (agg.item() * 1e6)
+            bound = ("host side shared by all ranks: all ranks' H2D + D2H bytes over the sum of the rates "
+                     "measured with every rank copying at once (per-rank rates below are under that contention)")
+        e2e["link"] = dict(link, bound=bound, floor_ms=round(floor_ms, 3), frac_of_floor=round(floor_ms / e2e_ms, 4))
 
     extra = None
     cpu = None
