@@ -12,7 +12,11 @@
  * Semantics (all entry points):
  *   C[m, n] = sum_k A[m, k] * B[k, n] for 0 <= m < M, 0 <= n < N, fp32 in, fp32 out,
  *   A row-major with row stride lda, B row-major with row stride ldb, C row-major
- *   with row stride ldc (strides in elements).  Elements of A/B outside [M,K]/[K,N]
+ *   with row stride ldc (strides in elements).  cfg->flags may instead declare A
+ *   stored transposed (TILEC_MM_TRANS_A: A[m, k] at A[k*lda + m]) and/or B stored
+ *   transposed (TILEC_MM_TRANS_B: B[k, n] at B[n*ldb + k]), i.e. the column-major
+ *   views x.t() of row-major tensors, read in place by the tensor-core variants
+ *   (the reference copies them, tilec/ext.py:59-60).  Elements of A/B outside [M,K]/[K,N]
  *   are never read (the reference reads them as 0.0, tilec/ext.py:21-22); elements
  *   of C outside [M,N] are never written (tilec/ext.py:24).  K == 0 writes zeros.
  *   M == 0 or N == 0 is a no-op.
@@ -33,7 +37,7 @@
 extern "C" {
 #endif
 
-#define TILEC_MM_ABI_VERSION 1
+#define TILEC_MM_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define TILEC_API __attribute__((visibility("default")))
@@ -71,8 +75,17 @@ typedef enum tilec_mm_variant {
 typedef struct tilec_mm_cfg {
   int32_t variant;     /* tilec_mm_variant */
   int32_t split_k;     /* SPLITK / tensor variants: number of K slices (0 = choose) */
-  int32_t reserved[6]; /* must be zero */
+  int32_t flags;       /* TILEC_MM_TRANS_A | TILEC_MM_TRANS_B (operand storage order), 0 = row-major */
+  int32_t reserved[5]; /* must be zero */
 } tilec_mm_cfg;
+
+/* cfg->flags.  With TRANS_A, lda >= M (A is K rows of M); with TRANS_B, ldb >= K (B is N
+ * rows of K).  The tensor-core variants read either order in place (TMA boxes and UMMA
+ * descriptors for K-major or MN-major tiles); SIMT / SPLITK first transpose a
+ * transposed operand into the workspace.  (ABI version 1 had no flags word: it was
+ * reserved[0] and had to be zero, so version-1 callers keep their meaning.) */
+#define TILEC_MM_TRANS_A 1
+#define TILEC_MM_TRANS_B 2
 
 /* C = A . B  (see the semantics block above).
  * cfg may be NULL (= AUTO).  workspace/ws_bytes: scratch for split-K partial sums;

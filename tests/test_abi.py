@@ -82,3 +82,24 @@ def test_bad_arguments_rejected_before_device():
     rows = (ctypes.c_int32 * 8)(0, 1, 0, 1, 0, 1, 9, 0)
     assert lib.tilec_mm_set_table(rows, 1) == 1  # unknown variant
     assert lib.tilec_mm_set_table(None, 0) == 0
+
+
+def test_transposed_operand_leading_dimensions():
+    """TILEC_MM_TRANS_A / _B change which extent the leading dimension must cover (A stored
+    K x M needs lda >= M, B stored N x K needs ldb >= K); checked before the device."""
+    h = _header()
+    assert int(re.search(r"#define TILEC_MM_TRANS_A (\d+)", h).group(1)) == _native.TRANS_A == 1
+    assert int(re.search(r"#define TILEC_MM_TRANS_B (\d+)", h).group(1)) == _native.TRANS_B == 2
+    lib = _native.load()
+    M, N, K = 8, 6, 20
+    ta = _native.make_cfg("auto", 0, _native.TRANS_A)
+    tb = _native.make_cfg("auto", 0, _native.TRANS_B)
+    # row-major A needs lda >= K = 20; transposed A needs lda >= M = 8
+    assert lib.tilec_mm_f32(16, 16, 16, M, N, K, 8, N, N, None, None, 0, None) == 1
+    assert lib.tilec_mm_f32(16, 16, 16, M, N, K, 7, N, N, ctypes.byref(ta), None, 0, None) == 1
+    # row-major B needs ldb >= N = 6; transposed B needs ldb >= K = 20
+    assert lib.tilec_mm_f32(16, 16, 16, M, N, K, K, 19, N, ctypes.byref(tb), None, 0, None) == 1
+    if not torch.cuda.is_available():
+        # valid for the transposed layouts: gets past the argument checks to the device
+        assert lib.tilec_mm_f32(16, 16, 16, M, N, K, 8, N, N, ctypes.byref(ta), None, 0, None) == 3
+        assert lib.tilec_mm_f32(16, 16, 16, M, N, K, K, K, N, ctypes.byref(tb), None, 0, None) == 3

@@ -47,15 +47,20 @@ def test_bad_variant_name():
         _native.make_cfg("fastest")
 
 
-def test_rows_view_passthrough():
+def test_operand_views_pass_through():
     x = torch.zeros(8, 10)
     v = x[:, 2:7]  # unit column stride, row stride 10: passed through, ld = 10
-    t, ld = ext._rows(v)
-    assert t.data_ptr() == v.data_ptr() and ld == 10
-    t, ld = ext._rows(x.t())  # transposed view: copied, like ext.py:59-60
-    assert t.is_contiguous() and ld == 8
-    t, ld = ext._rows(torch.zeros(1, 5).expand(4, 5))  # overlapping rows: copied
-    assert t.is_contiguous() and ld == 5
+    t, ld, trans = ext._operand(v)
+    assert t.data_ptr() == v.data_ptr() and ld == 10 and not trans
+    # transposed view: passed as transposed storage (the reference copies, ext.py:59-60)
+    t, ld, trans = ext._operand(x.t())
+    assert t.data_ptr() == x.data_ptr() and ld == 10 and trans
+    t, ld, trans = ext._operand(x[1:7, 2:9].t())  # transposed sub-view: ld = row stride of x
+    assert t.data_ptr() == x[1:7, 2:9].data_ptr() and ld == 10 and trans
+    t, ld, trans = ext._operand(torch.zeros(1, 5).expand(4, 5))  # overlapping rows: copied
+    assert t.is_contiguous() and ld == 5 and not trans
+    t, ld, trans = ext._operand(x[::2, ::3])  # no unit stride: copied
+    assert t.is_contiguous() and ld == 4 and not trans
 
 
 def test_cdiv_and_configs():

@@ -360,3 +360,46 @@ def test_bounded_wait_times_out_and_context_survives():
     got = _run(x1, x2, "3xtf32")
     assert oracle.rel_frob(got, oracle.mm_tiled(x1.numpy(), x2.numpy())) <= 1e-5
     assert _status_clean()
+
+
+def _stored(rows, cols, gen, ld_extra=0):
+    """A [rows, cols] row-major device tensor, optionally inside wider rows (ld > cols)."""
+    t = torch.randn(rows, cols + ld_extra, device=DEV, generator=gen)
+    return t[:, :cols] if ld_extra else t
+
+
+@pytest.mark.parametrize("variant", ALL)
+@pytest.mark.parametrize("ta,tb", [(False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("shape,ld_extra", [((512, 4096, 64), 0), ((1000, 3001, 777), 0), ((300, 520, 700), 8),
+                                            ((129, 64, 260), 0), ((2048, 1024, 2048), 0), ((7, 33, 5), 3),
+                                            ((256, 2048, 40), 4)])
+def test_transposed_views_read_in_place(shape, ld_extra, ta, tb, variant):
+    """x1 = y.t() and/or x2 = z.t() (column views) go to the library as transposed storage
+    (TILEC_MM_TRANS_A / _B): the tensor-core kernels read them in place through MN-major A
+    slabs / a K-major B tile, SIMT variants transpose into the workspace.  The product
+    equals, bit for bit, the same variant on contiguous copies (what the reference does,
+    tilec/ext.py:59-60), and meets the variant's error gate against fp64."""
+    m, k, n = shape
+    g = torch.Generator(device=DEV).manual_seed(m * 7 + k * 3 + n + 2 * ta + tb)
+    x1 = _stored(k, m, g, ld_extra).t() if ta else _stored(m, k, g, ld_extra)
+    x2 = _stored(n, k, g, ld_extra).t() if tb else _stored(k, n, g, ld_extra)
+    assert (x1.stride(0) == 1) == ta and (x2.stride(0) == 1) == tb
+    got = ext._matrix_mul(x1, x2, variant=variant)
+    if variant != "auto":
+        want = ext._matrix_mul(x1.contiguous(), x2.contiguous(), variant=variant)
+        assert torch.equal(got, want)
+    ref = x1.double() @ x2.double()
+    assert ((got.double() - ref).norm() / ref.norm()).item() <= TOL[variant]
+    assert _status_clean()
+
+
+def test_transposed_views_forced_split_and_pair():
+    """Transposed operands through split-K slabs and the CTA-pair kernel (ragged edges)."""
+    g = torch.Generator(device=DEV).manual_seed(11)
+    y = torch.randn(1500, 777, device=DEV, generator=g)       # x1 = y.t(): [777, 1500]
+    z = torch.randn(1000, 1500, device=DEV, generator=g)      # x2 = z.t(): [1500, 1000]
+    for split in (1, 3, 7):
+        got = ext._matrix_mul(y.t(), z.t(), variant="3xtf32", split_k=split)
+        want = ext._matrix_mul(y.t().contiguous(), z.t().contiguous(), variant="3xtf32", split_k=split)
+        assert torch.equal(got, want), split
+    assert ext.plan(y.t(), z.t(), variant="3xtf32")[0] == "3xtf32"

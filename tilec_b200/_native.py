@@ -29,7 +29,12 @@ EXPORTS = [
 
 
 class MMConfig(ctypes.Structure):
-    _fields_ = [("variant", ctypes.c_int32), ("split_k", ctypes.c_int32), ("reserved", ctypes.c_int32 * 6)]
+    _fields_ = [("variant", ctypes.c_int32), ("split_k", ctypes.c_int32), ("flags", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 5)]
+
+
+TRANS_A = 1   # TILEC_MM_TRANS_A: A stored K x M (x1 is a column view, e.g. y.t())
+TRANS_B = 2   # TILEC_MM_TRANS_B: B stored N x K
 
 
 class TilecError(RuntimeError):
@@ -100,16 +105,16 @@ def check(code, where):
 _CFG_CACHE = {}
 
 
-def make_cfg(variant="auto", split_k=0):
-    key = (variant, split_k)
+def make_cfg(variant="auto", split_k=0, flags=0):
+    key = (variant, split_k, flags)
     cfg = _CFG_CACHE.get(key)
     if cfg is None:
-        cfg = _make_cfg(variant, split_k)
+        cfg = _make_cfg(variant, split_k, flags)
         _CFG_CACHE[key] = cfg
     return cfg
 
 
-def _make_cfg(variant, split_k):
+def _make_cfg(variant, split_k, flags=0):
     if isinstance(variant, str):
         try:
             v = VARIANTS[variant.lower()]
@@ -117,4 +122,4 @@ def _make_cfg(variant, split_k):
             raise ValueError(f"unknown matrix_mul variant {variant!r}; expected one of {sorted(VARIANTS)}")
     else:
         v = int(variant)
-    return MMConfig(v, int(split_k))
+    return MMConfig(v, int(split_k), int(flags))

@@ -293,12 +293,23 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_
   return d;
 }
 
-// Instruction descriptor for kind::tf32, fp32 accumulate, A K-major, B MN-major.
+// Instruction descriptor for kind::tf32, fp32 accumulate.
 //   bits 4-5 D format (1 = f32), 7-9 A format (2 = tf32), 10-12 B format (2 = tf32),
-//   15 A major (0 = K), 16 B major (1 = MN), 17-22 N >> 3, 24-28 M >> 4.
-__host__ __device__ constexpr uint32_t make_idesc_tf32(int m, int n) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (1u << 16) | ((uint32_t(n) >> 3) << 17) |
-         ((uint32_t(m) >> 4) << 24);
+//   15 A major (0 = K, 1 = MN), 16 B major (0 = K, 1 = MN), 17-22 N >> 3, 24-28 M >> 4.
+// x1 row-major gives a K-major A and x2 row-major an MN-major B; their transposed views
+// flip each.
+__host__ __device__ constexpr uint32_t make_idesc_tf32(int m, int n, bool a_mn = false, bool b_mn = true) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
+         ((uint32_t(n) >> 3) << 17) | ((uint32_t(m) >> 4) << 24);
 }
+
+// Operand tile layouts of the tcgen05 kernels (runtime flags; the same bits as
+// TILEC_MM_TRANS_A / TILEC_MM_TRANS_B).
+//   default     A tile [128 x BK] K-major (one TMA box {BK, 128}, 64/128-byte swizzle);
+//               B tile as slabs of [BK x 32] MN-major (boxes {32, BK}, 128-byte swizzle
+//               with 32-byte granules).
+//   kOpAMN      A stored K x M: A tile as 128/32 slabs of [BK x 32] MN-major, like B.
+//   kOpBK       B stored N x K: B tile [BN x BK] K-major (one box {BK, BN}), like A.
+enum : int { kOpAMN = 1, kOpBK = 2 };
 
 }  // namespace tilec

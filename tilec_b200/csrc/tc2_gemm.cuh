@@ -60,12 +60,13 @@ struct Tc2Cfg {
   static_assert(kEpiWarps * 32 * (kColsPerThread + 4) * 4 <= STAGES * kStageBytes, "output staging");
 };
 
-// M = 256 (pair), N = BN, kind::tf32, A K-major, B MN-major.
+// M = 256 (pair), N = BN, kind::tf32; A K-major and B MN-major unless `layout` flips
+// them (kOpAMN / kOpBK, operands stored transposed).
 template <int BN, int STAGES, bool HI_EXPLICIT>
 __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
     tc2_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     float* __restrict__ out, int M, int N, int64_t ldo, int64_t out_slab, int K, int k_chunk,
-                    int mp_tiles, int n_tiles, int group_m, int vec_out) {
+                    int mp_tiles, int n_tiles, int group_m, int vec_out, int layout) {
   using Cfg = Tc2Cfg<BN, STAGES>;
   constexpr int BK = Cfg::BK;
   constexpr int KC = Cfg::kChunkBlocks;
@@ -158,10 +159,19 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
         if (!mbar_wait_cluster(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
         mbar_arrive_expect_tx(&full[s], Cfg::kTxBytes);
         const int k0 = k_begin + kb * BK;
-        tma_load_2d(a_raw(s), &tmA, &full[s], k0, m0);
+        if (layout & kOpAMN) {
 #pragma unroll
-        for (int j = 0; j < Cfg::kBNHalf / 32; ++j)
-          tma_load_2d(b_raw(s) + j * BK * 128, &tmB, &full[s], nb0 + 32 * j, k0);
+          for (int j = 0; j < 128 / 32; ++j) tma_load_2d(a_raw(s) + j * BK * 128, &tmA, &full[s], m0 + 32 * j, k0);
+        } else {
+          tma_load_2d(a_raw(s), &tmA, &full[s], k0, m0);
+        }
+        if (layout & kOpBK) {
+          tma_load_2d(b_raw(s), &tmB, &full[s], k0, nb0);
+        } else {
+#pragma unroll
+          for (int j = 0; j < Cfg::kBNHalf / 32; ++j)
+            tma_load_2d(b_raw(s) + j * BK * 128, &tmB, &full[s], nb0 + 32 * j, k0);
+        }
         ++issued;
       }
       if (ok) {
@@ -177,7 +187,16 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader CTA only)
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = make_idesc_tf32(256, BN);
+      const bool a_mn = (layout & kOpAMN) != 0, b_k = (layout & kOpBK) != 0;
+      const uint32_t idesc = make_idesc_tf32(256, BN, a_mn, !b_k);
+      auto desc_a = [&](uint32_t base, int kk) {
+        return a_mn ? make_smem_desc(base + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32)
+                    : make_smem_desc(base + kk * 32, 16, Cfg::kASbo, kLayoutSw64);
+      };
+      auto desc_b = [&](uint32_t base, int kk) {
+        return b_k ? make_smem_desc(base + kk * 32, 16, Cfg::kASbo, kLayoutSw64)
+                   : make_smem_desc(base + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
+      };
       const uint32_t peer = 1u;
       bool ok = true;
       for (int kb = 0; kb < nkb && ok; ++kb) {
@@ -195,10 +214,8 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
         const uint32_t a_l = smem_u32(a_lo(s)), b_l = smem_u32(b_lo(s));
 #pragma unroll
         for (int kk = 0; kk < BK / 8; ++kk) {
-          const uint64_t ad = make_smem_desc(a_hi + kk * 32, 16, Cfg::kASbo, kLayoutSw64);
-          const uint64_t bd = make_smem_desc(b_hi + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
-          const uint64_t adl = make_smem_desc(a_l + kk * 32, 16, Cfg::kASbo, kLayoutSw64);
-          const uint64_t bdl = make_smem_desc(b_l + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
+          const uint64_t ad = desc_a(a_hi, kk), bd = desc_b(b_hi, kk);
+          const uint64_t adl = desc_a(a_l, kk), bdl = desc_b(b_l, kk);
           const uint32_t accum = (chunk_start && kk == 0) ? 0u : 1u;
           umma_tf32_pair(tmem + dcol, adl, bd, idesc, accum);  // small terms first
           umma_tf32_pair(tmem + dcol, ad, bdl, idesc, 1u);

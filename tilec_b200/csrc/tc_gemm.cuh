@@ -30,8 +30,10 @@
 //   (TMEM lane) and BN/2 columns.
 //
 // Operands: A = x1 row-major (K contiguous) -> K-major; B = x2 row-major (N contiguous)
-// -> MN-major, consumed in place (no transpose).  TMA needs 16-byte aligned bases and
-// row strides (lda, ldb multiples of 4); the host routes anything else to the SIMT kernel.
+// -> MN-major, consumed in place (no transpose).  `layout` (kOpAMN / kOpBK) flips either
+// for operands stored transposed (x.t() views): A as MN-major slabs, B as a K-major tile.
+// TMA needs 16-byte aligned bases and row strides (multiples of 4 elements); the host
+// packs anything else into an aligned copy first.
 #pragma once
 
 #include "common.cuh"
@@ -121,7 +123,7 @@ template <int BN, int BK, int STAGES, bool SPLIT3, bool HI_EXPLICIT>
 __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    float* __restrict__ out, int M, int N, int64_t ldo, int64_t out_slab, int K, int k_chunk,
-                   int m_tiles, int n_tiles, int group_m, int vec_out) {
+                   int m_tiles, int n_tiles, int group_m, int vec_out, int layout) {
   using Cfg = TcCfg<BN, BK, STAGES, SPLIT3>;
   constexpr int KC = Cfg::kChunkBlocks;
   extern __shared__ uint8_t smem_raw[];
@@ -210,9 +212,18 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
         if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) { ok = false; break; }
         mbar_arrive_expect_tx(&full[s], Cfg::kTxBytes);
         const int k0 = k_begin + kb * BK;
-        tma_load_2d(a_raw(s), &tmA, &full[s], k0, m0);
+        if (layout & kOpAMN) {
 #pragma unroll
-        for (int j = 0; j < BN / 32; ++j) tma_load_2d(b_raw(s) + j * BK * 128, &tmB, &full[s], n0 + 32 * j, k0);
+          for (int j = 0; j < kTcBM / 32; ++j) tma_load_2d(a_raw(s) + j * BK * 128, &tmA, &full[s], m0 + 32 * j, k0);
+        } else {
+          tma_load_2d(a_raw(s), &tmA, &full[s], k0, m0);
+        }
+        if (layout & kOpBK) {
+          tma_load_2d(b_raw(s), &tmB, &full[s], k0, n0);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 32; ++j) tma_load_2d(b_raw(s) + j * BK * 128, &tmB, &full[s], n0 + 32 * j, k0);
+        }
         ++issued;
       }
       if (ok) {
@@ -228,7 +239,18 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_tf32(kTcBM, BN);
+      const bool a_mn = (layout & kOpAMN) != 0, b_k = (layout & kOpBK) != 0;
+      const uint32_t idesc = make_idesc_tf32(kTcBM, BN, a_mn, !b_k);
+      // K step kk (8 elements) of a tile: 32 bytes along a K-major row, or 8 rows of 128
+      // bytes in an MN-major slab.
+      auto desc_a = [&](uint32_t base, int kk) {
+        return a_mn ? make_smem_desc(base + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32)
+                    : make_smem_desc(base + kk * 32, 16, Cfg::kASbo, Cfg::kALayout);
+      };
+      auto desc_b = [&](uint32_t base, int kk) {
+        return b_k ? make_smem_desc(base + kk * 32, 16, Cfg::kASbo, Cfg::kALayout)
+                   : make_smem_desc(base + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
+      };
       bool ok = true;
       for (int kb = 0; kb < nkb && ok; ++kb) {
         const int s = kb % STAGES;
@@ -246,13 +268,12 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
         const uint32_t b_hi_addr = smem_u32(b_raw(s));
 #pragma unroll
         for (int kk = 0; kk < BK / 8; ++kk) {
-          const uint64_t ad = make_smem_desc(a_hi_addr + kk * 32, 16, Cfg::kASbo, Cfg::kALayout);
-          const uint64_t bd = make_smem_desc(b_hi_addr + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
+          const uint64_t ad = desc_a(a_hi_addr, kk);
+          const uint64_t bd = desc_b(b_hi_addr, kk);
           const uint32_t accum = (chunk_start && kk == 0) ? 0u : 1u;
           if constexpr (SPLIT3) {
-            const uint64_t adl = make_smem_desc(smem_u32(a_lo(s)) + kk * 32, 16, Cfg::kASbo, Cfg::kALayout);
-            const uint64_t bdl =
-                make_smem_desc(smem_u32(b_lo(s)) + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
+            const uint64_t adl = desc_a(smem_u32(a_lo(s)), kk);
+            const uint64_t bdl = desc_b(smem_u32(b_lo(s)), kk);
             umma_tf32(tmem + dcol, adl, bd, idesc, accum);  // small terms first
             umma_tf32(tmem + dcol, ad, bdl, idesc, 1u);
             umma_tf32(tmem + dcol, ad, bd, idesc, 1u);

@@ -28,6 +28,8 @@
 static_assert(TILEC_DEV_STATUS_TIMEOUT == tilec::TILEC_DEV_TIMEOUT && TILEC_DEV_STATUS_TMEM == tilec::TILEC_DEV_TMEM &&
                   TILEC_DEV_STATUS_BAD_LAUNCH == tilec::TILEC_DEV_BAD_LAUNCH,
               "status bits in include/tilec_mm.h match the device enum");
+static_assert(TILEC_MM_TRANS_A == tilec::kOpAMN && TILEC_MM_TRANS_B == tilec::kOpBK,
+              "cfg->flags are passed to the kernels as their operand layout");
 
 namespace tilec {
 namespace {
@@ -164,7 +166,9 @@ struct Plan {
   int bn = 128;
   size_t ws_bytes = 0;
   int64_t ldw = 0;
-  bool pack_a = false, pack_b = false;
+  int flags = 0;      // TILEC_MM_TRANS_A / TILEC_MM_TRANS_B: how A and B are stored
+  bool pack_a = false, pack_b = false;    // tensor variants: aligned copy, same storage order
+  bool tpose_a = false, tpose_b = false;  // SIMT variants: transposed operand -> row-major copy
   bool pair = false;  // 3XTF32 on a CTA pair (tc2_gemm_kernel, 256 x 256 tiles)
   size_t off_a = 0, off_b = 0, off_slabs = 0;
 };
@@ -273,10 +277,13 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
   (void)ldc;
   int variant = cfg ? cfg->variant : TILEC_MM_AUTO;
   int requested_split = cfg ? cfg->split_k : 0;
+  const int flags = cfg ? cfg->flags : 0;
+  if (flags & ~(TILEC_MM_TRANS_A | TILEC_MM_TRANS_B)) return TILEC_ERR_BAD_ARG;
   if (cfg) {
-    for (int i = 0; i < 6; ++i)
+    for (int i = 0; i < 5; ++i)
       if (cfg->reserved[i] != 0) return TILEC_ERR_BAD_ARG;
   }
+  p->flags = flags;
   if (requested_split < 0) return TILEC_ERR_BAD_ARG;
   if (variant == TILEC_MM_AUTO) choose_auto(d, A, B, M, N, K, lda, ldb, &variant, &requested_split);
   if (variant < TILEC_MM_SIMT || variant > TILEC_MM_3XTF32_MASKED) return TILEC_ERR_BAD_ARG;
@@ -285,6 +292,9 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
   if (tensor) {
     p->pack_a = !rows_aligned(A, lda);
     p->pack_b = !rows_aligned(B, ldb);
+  } else {
+    p->tpose_a = (flags & TILEC_MM_TRANS_A) != 0;
+    p->tpose_b = (flags & TILEC_MM_TRANS_B) != 0;
   }
 
   p->variant = variant;
@@ -318,14 +328,19 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
   }
   if (p->k_chunk <= 0) p->k_chunk = 16;
   p->ldw = round_up(N, 4);
+  // An aligned copy keeps the stored order (K x M for a transposed A); a SIMT transpose
+  // writes the row-major M x K (K x N) operand.
+  const bool ta = (flags & TILEC_MM_TRANS_A) != 0, tb = (flags & TILEC_MM_TRANS_B) != 0;
   size_t off = 0;
-  if (p->pack_a) {
+  if (p->pack_a || p->tpose_a) {
     p->off_a = off;
-    off += align256(size_t(M) * size_t(round_up(K, 4)) * sizeof(float));
+    const size_t elems = (p->pack_a && ta) ? size_t(K) * size_t(round_up(M, 4)) : size_t(M) * size_t(round_up(K, 4));
+    off += align256(elems * sizeof(float));
   }
-  if (p->pack_b) {
+  if (p->pack_b || p->tpose_b) {
     p->off_b = off;
-    off += align256(size_t(K) * size_t(round_up(N, 4)) * sizeof(float));
+    const size_t elems = (p->pack_b && tb) ? size_t(N) * size_t(round_up(K, 4)) : size_t(K) * size_t(round_up(N, 4));
+    off += align256(elems * sizeof(float));
   }
   p->off_slabs = off;
   if (p->split > 1) off += size_t(p->split) * size_t(M) * size_t(p->ldw) * sizeof(float);
@@ -335,11 +350,13 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
 
 // need_c: tilec_mm_f32 writes C; tilec_mm_plan / tilec_mm_workspace_bytes accept C == NULL.
 int check_args(const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
-               int64_t ldb, int64_t ldc, bool need_c = true) {
+               int64_t ldb, int64_t ldc, bool need_c = true, int flags = 0) {
   if (M < 0 || N < 0 || K < 0) return TILEC_ERR_BAD_ARG;
   if (M == 0 || N == 0) return TILEC_OK;
   if ((need_c && C == nullptr) || ldc < N) return TILEC_ERR_BAD_ARG;
-  if (K > 0 && (A == nullptr || B == nullptr || lda < K || ldb < N)) return TILEC_ERR_BAD_ARG;
+  const int64_t min_lda = (flags & TILEC_MM_TRANS_A) ? M : K;
+  const int64_t min_ldb = (flags & TILEC_MM_TRANS_B) ? K : N;
+  if (K > 0 && (A == nullptr || B == nullptr || lda < min_lda || ldb < min_ldb)) return TILEC_ERR_BAD_ARG;
   return TILEC_OK;
 }
 
@@ -348,33 +365,30 @@ int launch_status() {
   return e == cudaSuccess ? TILEC_OK : TILEC_ERR_LAUNCH;
 }
 
+// Tensor maps for the operand tiles (`layout`: kOpAMN / kOpBK, see common.cuh).  A K-major:
+// box {bk, 128} with a bk*4-byte swizzle; A MN-major (stored K x M): boxes {32, bk} with
+// the 128-byte / 32-byte-granule swizzle.  B MN-major: boxes {32, bk}, same swizzle; B
+// K-major (stored N x K): box {bk, b_rows}, bk*4-byte swizzle.
 int encode_maps(const float* A, const float* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
-                int bk, int a_swizzle_bytes, CUtensorMap* ma, CUtensorMap* mb) {
+                int bk, int layout, int b_rows, CUtensorMap* ma, CUtensorMap* mb) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode();
   if (!enc) return TILEC_ERR_NO_DEVICE;
-  {
-    cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(M)};
-    cuuint64_t strides[1] = {cuuint64_t(lda) * 4};
-    cuuint32_t box[2] = {cuuint32_t(bk), cuuint32_t(kTcBM)};
+  const CUtensorMapSwizzle k_sw = bk * 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  auto encode = [&](CUtensorMap* m, const float* base, int64_t inner, int64_t outer, int64_t ld, int box_in,
+                    int box_out, CUtensorMapSwizzle sw) {
+    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(outer)};
+    cuuint64_t strides[1] = {cuuint64_t(ld) * 4};
+    cuuint32_t box[2] = {cuuint32_t(box_in), cuuint32_t(box_out)};
     cuuint32_t estr[2] = {1, 1};
-    const CUtensorMapSwizzle sw =
-        a_swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-    if (enc(ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(A), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return TILEC_ERR_BAD_ARG;
-  }
-  {
-    cuuint64_t dims[2] = {cuuint64_t(N), cuuint64_t(K)};
-    cuuint64_t strides[1] = {cuuint64_t(ldb) * 4};
-    cuuint32_t box[2] = {32, cuuint32_t(bk)};
-    cuuint32_t estr[2] = {1, 1};
-    if (enc(mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(B), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return TILEC_ERR_BAD_ARG;
-  }
-  return TILEC_OK;
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  };
+  const bool ok_a = (layout & kOpAMN) ? encode(ma, A, M, K, lda, 32, bk, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
+                                      : encode(ma, A, K, M, lda, bk, kTcBM, k_sw);
+  const bool ok_b = (layout & kOpBK) ? encode(mb, B, K, N, ldb, bk, b_rows, k_sw)
+                                     : encode(mb, B, N, K, ldb, 32, bk, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  return ok_a && ok_b ? TILEC_OK : TILEC_ERR_BAD_ARG;
 }
 
 // Programmatic dependent launch is on unless TILEC_MM_PDL=0 (read once per process).
@@ -429,7 +443,7 @@ int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStr
 
 template <int BN, int BK, int STAGES, bool SPLIT3, bool HI>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N, int64_t ldo,
-              int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, cudaStream_t s) {
+              int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, int layout, cudaStream_t s) {
   using Cfg = TcCfg<BN, BK, STAGES, SPLIT3>;
   const int m_tiles = static_cast<int>(cdiv(M, kTcBM));
   const int n_tiles = static_cast<int>(cdiv(N, BN));
@@ -437,23 +451,23 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t 
   dim3 grid(static_cast<unsigned>(int64_t(m_tiles) * n_tiles), 1, static_cast<unsigned>(split));
   return launch_k(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 1, ma,
                   mb, out, static_cast<int>(M), static_cast<int>(N), ldo, slab, static_cast<int>(K),
-                  static_cast<int>(k_chunk), m_tiles, n_tiles, group_m, vec_out);
+                  static_cast<int>(k_chunk), m_tiles, n_tiles, group_m, vec_out, layout);
 }
 
 template <int BN, bool SPLIT3, bool HI>
 int launch_tc_mode(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N, int64_t ldo,
-                   int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, cudaStream_t s) {
+                   int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, int layout, cudaStream_t s) {
   if constexpr (SPLIT3)
     return launch_tc<BN, k3xBK, TcShape<BN>::k3xStages, true, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split,
-                                                                  vec_out, s);
+                                                                  vec_out, layout, s);
   else
     return launch_tc<BN, 32, TcShape<BN>::kTf32Stages, false, false>(ma, mb, out, M, N, ldo, slab, K, k_chunk,
-                                                                     split, vec_out, s);
+                                                                     split, vec_out, layout, s);
 }
 
 template <bool HI>
 int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N, int64_t ldo,
-               int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, cudaStream_t s) {
+               int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, int layout, cudaStream_t s) {
   using Cfg = Tc2Cfg<256, kPairStages>;
   const int mp_tiles = static_cast<int>(cdiv(M, 256));
   const int n_tiles = static_cast<int>(cdiv(N, 256));
@@ -461,16 +475,16 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t
   const dim3 grid(static_cast<unsigned>(2 * int64_t(mp_tiles) * n_tiles), 1, static_cast<unsigned>(split));
   return launch_k(tc2_gemm_kernel<256, kPairStages, HI>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 2, ma, mb,
                   out, static_cast<int>(M), static_cast<int>(N), ldo, slab, static_cast<int>(K),
-                  static_cast<int>(k_chunk), mp_tiles, n_tiles, group_m, vec_out);
+                  static_cast<int>(k_chunk), mp_tiles, n_tiles, group_m, vec_out, layout);
 }
 
 template <bool SPLIT3, bool HI>
 int dispatch_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N,
-                   int64_t ldo, int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, cudaStream_t s) {
+                   int64_t ldo, int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, int layout, cudaStream_t s) {
   switch (bn) {
-    case 64: return launch_tc_mode<64, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, s);
-    case 128: return launch_tc_mode<128, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, s);
-    default: return launch_tc_mode<256, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, s);
+    case 64: return launch_tc_mode<64, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, layout, s);
+    case 128: return launch_tc_mode<128, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, layout, s);
+    default: return launch_tc_mode<256, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, layout, s);
   }
 }
 
@@ -485,6 +499,40 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const float* __restrict_
     float* d = dst + r * ldd;
     for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) d[c] = s[c];
   }
+}
+
+// dst[c, r] = src[r, c] for r < rows, c < cols: 32 x 32 tiles through shared memory (the
+// +1 column keeps the transposed reads free of bank conflicts), coalesced on both sides.
+__global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict__ src, int64_t lds,
+                                                        float* __restrict__ dst, int64_t ldd, int64_t rows,
+                                                        int64_t cols) {
+  __shared__ float t[32][33];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int64_t tr = (rows + 31) / 32, tc = (cols + 31) / 32;
+  const int tx = static_cast<int>(threadIdx.x) & 31, ty = static_cast<int>(threadIdx.x) >> 5;  // 32 x 8
+  for (int64_t tile = blockIdx.x; tile < tr * tc; tile += gridDim.x) {
+    const int64_t r0 = (tile / tc) * 32, c0 = (tile % tc) * 32;
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t r = r0 + i, c = c0 + tx;
+      if (r < rows && c < cols) t[i][tx] = src[r * lds + c];
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+      const int64_t c = c0 + i, r = r0 + tx;
+      if (r < rows && c < cols) dst[c * ldd + r] = t[tx][i];
+    }
+    __syncthreads();
+  }
+}
+
+int launch_transpose(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows, int64_t cols,
+                     const DeviceInfo& d, cudaStream_t s) {
+  int64_t blocks = cdiv(rows, 32) * cdiv(cols, 32);
+  if (blocks > int64_t(d.sms) * 8) blocks = int64_t(d.sms) * 8;
+  if (blocks < 1) blocks = 1;
+  return launch_k(transpose_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, 1, src, lds, dst, ldd, rows,
+                  cols);
 }
 
 int launch_pack(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows, int64_t cols,
@@ -576,7 +624,7 @@ extern "C" {
 int tilec_mm_plan(const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                   int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg, tilec_mm_cfg* out) {
   if (!out) return TILEC_ERR_BAD_ARG;
-  int rc = check_args(A, B, C, M, N, K, lda, ldb, ldc, /*need_c=*/false);
+  int rc = check_args(A, B, C, M, N, K, lda, ldb, ldc, /*need_c=*/false, cfg ? cfg->flags : 0);
   if (rc) return rc;
   DeviceInfo* d = nullptr;
   rc = current_device(&d);
@@ -587,6 +635,7 @@ int tilec_mm_plan(const float* A, const float* B, const float* C, int64_t M, int
   std::memset(out, 0, sizeof(*out));
   out->variant = p.variant;
   out->split_k = p.split;
+  out->flags = p.flags;
   return TILEC_OK;
 }
 
@@ -606,7 +655,7 @@ size_t tilec_mm_workspace_bytes(const float* A, const float* B, const float* C, 
 int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                  int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg, void* workspace, size_t ws_bytes,
                  void* stream) {
-  int rc = check_args(A, B, C, M, N, K, lda, ldb, ldc);
+  int rc = check_args(A, B, C, M, N, K, lda, ldb, ldc, true, cfg ? cfg->flags : 0);
   if (rc) return rc;
   if (M == 0 || N == 0) return TILEC_OK;
   DeviceInfo* d = nullptr;
@@ -624,27 +673,45 @@ int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
       return TILEC_ERR_WORKSPACE;
   }
   uint8_t* wsb = static_cast<uint8_t*>(workspace);
-  if (p.pack_a) {
+  const bool ta = (p.flags & TILEC_MM_TRANS_A) != 0, tb = (p.flags & TILEC_MM_TRANS_B) != 0;
+  // Stored shapes: A is M x K (K x M when transposed), B is K x N (N x K when transposed).
+  const int64_t a_rows = ta ? K : M, a_cols = ta ? M : K;
+  const int64_t b_rows = tb ? N : K, b_cols = tb ? K : N;
+  if (p.pack_a || p.tpose_a) {
     float* pa = reinterpret_cast<float*>(wsb + p.off_a);
-    rc = launch_pack(A, lda, pa, round_up(K, 4), M, K, *d, s);
+    if (p.pack_a) {
+      rc = launch_pack(A, lda, pa, round_up(a_cols, 4), a_rows, a_cols, *d, s);
+      lda = round_up(a_cols, 4);
+    } else {
+      rc = launch_transpose(A, lda, pa, round_up(K, 4), K, M, *d, s);
+      lda = round_up(K, 4);
+    }
     if (rc) return rc;
     A = pa;
-    lda = round_up(K, 4);
   }
-  if (p.pack_b) {
+  if (p.pack_b || p.tpose_b) {
     float* pb = reinterpret_cast<float*>(wsb + p.off_b);
-    rc = launch_pack(B, ldb, pb, round_up(N, 4), K, N, *d, s);
+    if (p.pack_b) {
+      rc = launch_pack(B, ldb, pb, round_up(b_cols, 4), b_rows, b_cols, *d, s);
+      ldb = round_up(b_cols, 4);
+    } else {
+      rc = launch_transpose(B, ldb, pb, round_up(N, 4), N, K, *d, s);
+      ldb = round_up(N, 4);
+    }
     if (rc) return rc;
     B = pb;
-    ldb = round_up(N, 4);
   }
+  // The tensor-core kernels read either storage order in place; SIMT operands are now
+  // row-major.
+  const bool simt = p.variant == TILEC_MM_SIMT || p.variant == TILEC_MM_SPLITK;
+  const int layout = simt ? 0 : p.flags;
   float* slabs = reinterpret_cast<float*>(wsb + p.off_slabs);
   float* out = p.split > 1 ? slabs : C;
   const int64_t ldo = p.split > 1 ? p.ldw : ldc;
   const int64_t slab = p.split > 1 ? M * p.ldw : 0;
   const int vec_out = p.split > 1 ? 1 : (aligned16(C) && (ldc % 4 == 0) ? 1 : 0);
 
-  if (p.variant == TILEC_MM_SIMT || p.variant == TILEC_MM_SPLITK) {
+  if (simt) {
     const bool vec = aligned16(A) && aligned16(B) && (lda % 4 == 0) && (ldb % 4 == 0);
     const int64_t mt = cdiv(M, kSimtBM), nt = cdiv(N, p.bn);
     if (nt > 65535) return TILEC_ERR_UNSUPPORTED;
@@ -653,18 +720,20 @@ int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N,
   } else {
     CUtensorMap ma, mb;
     const int bk = p.variant == TILEC_MM_TF32 ? 32 : (p.pair ? 16 : k3xBK);
-    rc = encode_maps(A, B, M, N, K, lda, ldb, bk, bk * 4, &ma, &mb);
+    rc = encode_maps(A, B, M, N, K, lda, ldb, bk, layout, p.pair ? 128 : p.bn, &ma, &mb);
     if (rc) return rc;
     if (p.pair)
       rc = p.variant == TILEC_MM_3XTF32
-               ? launch_tc2<false>(ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s)
-               : launch_tc2<true>(ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
+               ? launch_tc2<false>(ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, layout, s)
+               : launch_tc2<true>(ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, layout, s);
     else if (p.variant == TILEC_MM_TF32)
-      rc = dispatch_tc_bn<false, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
+      rc = dispatch_tc_bn<false, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, layout,
+                                        s);
     else if (p.variant == TILEC_MM_3XTF32)
-      rc = dispatch_tc_bn<true, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
+      rc = dispatch_tc_bn<true, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, layout,
+                                       s);
     else
-      rc = dispatch_tc_bn<true, true>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, s);
+      rc = dispatch_tc_bn<true, true>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, layout, s);
   }
   if (rc) return rc;
   if (p.split > 1) rc = launch_reduce(slabs, C, M, N, p.ldw, ldc, p.split, *d, s);

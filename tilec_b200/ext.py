@@ -41,13 +41,20 @@ def _check_operand(x):
         raise TypeError(f"unsupported kernel argument of dtype {x.dtype} (use float32 tensors and ints)")
 
 
-def _rows(x):
-    """Return (tensor, row stride) with unit column stride; copies only when it must."""
+def _operand(x):
+    """(tensor, leading stride, transposed) for a 2-D operand, copying only when it must.
+
+    A row view (unit column stride) passes as is.  A column view (unit row stride, e.g.
+    y.t() of a row-major y) passes as the transposed storage it is: the tensor-core
+    kernels read it in place (TILEC_MM_TRANS_A / _B).  The reference makes both
+    contiguous (tilec/ext.py:59-60); anything else is still copied here."""
     r, c = x.shape
     if (c <= 1 or x.stride(1) == 1) and (r <= 1 or x.stride(0) >= max(c, 1)):
-        return x, (x.stride(0) if r > 1 else max(c, 1))
+        return x, (x.stride(0) if r > 1 else max(c, 1)), False
+    if x.stride(0) == 1 and x.stride(1) >= r:
+        return x, x.stride(1), True
     x = x.contiguous()
-    return x, max(c, 1)
+    return x, max(c, 1), False
 
 
 def _check_out(out, M, N, device):
@@ -77,14 +84,14 @@ def _workspace(dev, stream, nbytes):
     return ws
 
 
-def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k):
+def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k, flags=0):
     global _installed
     lib = _native.load()
     if not _installed:
         from . import select  # installs the B200 selection table on first use
         select.ensure_installed()
         _installed = True
-    cfg = _native.make_cfg(variant, split_k)
+    cfg = _native.make_cfg(variant, split_k, flags)
     pa, pb, pc = a.data_ptr(), b.data_ptr(), out.data_ptr()
     dev = out.device
     switch = torch.cuda.current_device() != dev.index
@@ -93,7 +100,8 @@ def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k):
         torch.cuda.set_device(dev)
     try:
         stream = torch.cuda.current_stream(dev).cuda_stream
-        key = (M, N, K, lda, ldb, ldc, pa & 15 == 0, pb & 15 == 0, pc & 15 == 0, cfg.variant, cfg.split_k, dev.index)
+        key = (M, N, K, lda, ldb, ldc, pa & 15 == 0, pb & 15 == 0, pc & 15 == 0, cfg.variant, cfg.split_k, flags,
+               dev.index)
         ws_bytes = _WS_BYTES.get(key)
         if ws_bytes is None:
             ws_bytes = lib.tilec_mm_workspace_bytes(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg))
@@ -125,8 +133,8 @@ def _matrix_mul(x1, x2, variant=None, split_k=0, out=None):
                          "tilec_b200 has no CPU path")
     if x1.device != x2.device:
         raise ValueError(f"matrix_mul: inputs on different devices ({x1.device}, {x2.device})")
-    a, lda = _rows(x1)
-    b, ldb = _rows(x2)
+    a, lda, ta = _operand(x1)
+    b, ldb, tb = _operand(x2)
     if out is None:
         out = x1.new_empty(M, N)
         ldc = max(N, 1)
@@ -134,7 +142,8 @@ def _matrix_mul(x1, x2, variant=None, split_k=0, out=None):
         ldc = _check_out(out, M, N, x1.device)
     if M == 0 or N == 0:
         return out
-    return _launch(a, lda, b, ldb, out, ldc, M, N, K, variant or _default_variant(), split_k)
+    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0)
+    return _launch(a, lda, b, ldb, out, ldc, M, N, K, variant or _default_variant(), split_k, flags)
 
 
 def matrix_mul(x1, x2):
@@ -146,12 +155,13 @@ def plan(x1, x2, variant=None, split_k=0):
     """The (variant name, split_k) that matrix_mul would launch for these operands."""
     M, K = x1.shape
     _, N = x2.shape
-    a, lda = _rows(x1)
-    b, ldb = _rows(x2)
+    a, lda, ta = _operand(x1)
+    b, ldb, tb = _operand(x2)
     lib = _native.load()
     from . import select
     select.ensure_installed()
-    cfg = _native.make_cfg(variant or _default_variant(), split_k)
+    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0)
+    cfg = _native.make_cfg(variant or _default_variant(), split_k, flags)
     res = _native.MMConfig()
     with torch.cuda.device(x1.device):
         rc = lib.tilec_mm_plan(a.data_ptr(), b.data_ptr(), None, M, N, K, lda, ldb, max(N, 1),
