@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define TILEC_MM_ABI_VERSION 2
+#define TILEC_MM_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define TILEC_API __attribute__((visibility("default")))
@@ -76,14 +76,20 @@ typedef struct tilec_mm_cfg {
   int32_t variant;     /* tilec_mm_variant */
   int32_t split_k;     /* SPLITK / tensor variants: number of K slices (0 = choose) */
   int32_t flags;       /* TILEC_MM_TRANS_A | TILEC_MM_TRANS_B (operand storage order), 0 = row-major */
-  int32_t reserved[5]; /* must be zero */
+  int32_t activation;  /* TILEC_MM_ACT_*: applied to every element of C as it is written */
+  int32_t reserved[4]; /* must be zero */
 } tilec_mm_cfg;
+
+/* cfg->activation: C = act(A.B + bias) (bias only through tilec_mm_f32_ex). */
+#define TILEC_MM_ACT_NONE 0
+#define TILEC_MM_ACT_RELU 1 /* max(x, 0) */
+#define TILEC_MM_ACT_GELU 2 /* x * (1 + erf(x / sqrt(2))) / 2 */
 
 /* cfg->flags.  With TRANS_A, lda >= M (A is K rows of M); with TRANS_B, ldb >= K (B is N
  * rows of K).  The tensor-core variants read either order in place (TMA boxes and UMMA
  * descriptors for K-major or MN-major tiles); SIMT / SPLITK first transpose a
- * transposed operand into the workspace.  (ABI version 1 had no flags word: it was
- * reserved[0] and had to be zero, so version-1 callers keep their meaning.) */
+ * transposed operand into the workspace.  (ABI version 1 had no flags or activation word:
+ * they were reserved[0..1] and had to be zero, so version-1 callers keep their meaning.) */
 #define TILEC_MM_TRANS_A 1
 #define TILEC_MM_TRANS_B 2
 
@@ -97,6 +103,31 @@ TILEC_API int tilec_mm_f32(const float* A, const float* B, float* C,
                  const tilec_mm_cfg* cfg,
                  void* workspace, size_t ws_bytes,
                  void* stream);
+
+/* Batched products with a fused epilogue (no counterpart in the reference; the next op
+ * surface its README names).  For b < batch:
+ *   C_b = act(A_b . B_b + bias)   A_b = A + b*stride_a, B_b = B + b*stride_b, C_b = C + b*stride_c
+ * (strides in elements; a zero stride_a / stride_b shares that operand across the batch;
+ * the batches of C must not overlap: stride_c >= (M-1)*ldc + N when batch > 1).  bias is
+ * N floats added per column, or NULL; act = cfg->activation.  Layout flags, variants and
+ * workspace rules as tilec_mm_f32 (size from tilec_mm_workspace_bytes_ex).  The tensor-
+ * core kernels take the batch as a grid dimension (3-D tensor maps) and apply the epilogue
+ * in their output stores (in the split-K reduction when K is split); batches beyond 65535
+ * run as consecutive launches. */
+TILEC_API int tilec_mm_f32_ex(const float* A, const float* B, float* C, const float* bias,
+                    int64_t M, int64_t N, int64_t K,
+                    int64_t lda, int64_t ldb, int64_t ldc,
+                    int64_t batch, int64_t stride_a, int64_t stride_b, int64_t stride_c,
+                    const tilec_mm_cfg* cfg,
+                    void* workspace, size_t ws_bytes,
+                    void* stream);
+
+/* Bytes of workspace tilec_mm_f32_ex needs (0 when none); NULL operands as below. */
+TILEC_API size_t tilec_mm_workspace_bytes_ex(const float* A, const float* B, const float* C,
+                                   int64_t M, int64_t N, int64_t K,
+                                   int64_t lda, int64_t ldb, int64_t ldc,
+                                   int64_t batch, int64_t stride_a, int64_t stride_b, int64_t stride_c,
+                                   const tilec_mm_cfg* cfg);
 
 /* Bytes of workspace tilec_mm_f32 needs for these arguments (0 when none).
  * Pointer alignment affects the AUTO choice, so pass the same pointers (or NULL

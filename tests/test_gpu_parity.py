@@ -403,3 +403,113 @@ def test_transposed_views_forced_split_and_pair():
         want = ext._matrix_mul(y.t().contiguous(), z.t().contiguous(), variant="3xtf32", split_k=split)
         assert torch.equal(got, want), split
     assert ext.plan(y.t(), z.t(), variant="3xtf32")[0] == "3xtf32"
+
+
+def _ref64(x1, x2, bias=None, act=None):
+    r = torch.matmul(x1.double(), x2.double())
+    if bias is not None:
+        r = r + bias.double()
+    if act == "relu":
+        r = torch.relu(r)
+    elif act == "gelu":
+        r = torch.nn.functional.gelu(r)
+    return r
+
+
+@pytest.mark.parametrize("variant", ("simt", "splitk", "tf32", "3xtf32", "3xtf32_masked"))
+@pytest.mark.parametrize("split_k", (1, 3))
+@pytest.mark.parametrize("shape", [(5, 300, 520, 700), (3, 512, 2048, 64), (4, 33, 129, 65), (2, 1000, 3001, 777)])
+def test_batched_equals_single_products(shape, split_k, variant):
+    """matrix_mul_ex on [B, M, K] @ [B, K, N]: every slice equals the single-product call
+    with the same variant and K split bit for bit (the batch is a grid dimension, nothing
+    else changes), and meets the variant's error gate."""
+    nb, m, k, n = shape
+    g = torch.Generator(device=DEV).manual_seed(nb * m + k + n + split_k)
+    x1 = torch.randn(nb, m, k, device=DEV, generator=g)
+    x2 = torch.randn(nb, k, n, device=DEV, generator=g)
+    got = ext.matrix_mul_ex(x1, x2, variant=variant, split_k=split_k)
+    for b in range(nb):
+        one = ext._matrix_mul(x1[b], x2[b], variant=variant, split_k=split_k)
+        assert torch.equal(got[b], one), b
+    ref = _ref64(x1, x2)
+    assert ((got.double() - ref).norm() / ref.norm()).item() <= TOL[variant]
+    assert _status_clean()
+
+
+@pytest.mark.parametrize("variant", ("auto", "simt", "3xtf32", "tf32"))
+def test_batched_shared_transposed_and_misaligned(variant):
+    """A shared by the batch (2-D x1), B shared (2-D x2), column views of each slice, and
+    batch strides that are not 16-byte multiples (packed for TMA)."""
+    g = torch.Generator(device=DEV).manual_seed(5)
+    nb, m, k, n = 6, 257, 300, 190
+    a2 = torch.randn(m, k, device=DEV, generator=g)
+    b3 = torch.randn(nb, k, n, device=DEV, generator=g)
+    a3 = torch.randn(nb, m, k, device=DEV, generator=g)
+    b2 = torch.randn(k, n, device=DEV, generator=g)
+    cases = [(a2, b3), (a3, b2),
+             (torch.randn(nb, k, m, device=DEV, generator=g).transpose(1, 2), b3),     # A column views
+             (a3, torch.randn(nb, n, k, device=DEV, generator=g).transpose(1, 2)),     # B column views
+             (torch.randn(nb, m, k + 1, device=DEV, generator=g)[:, :, 1:], b3)]      # odd offset / stride
+    for x1, x2 in cases:
+        got = ext.matrix_mul_ex(x1, x2, variant=variant)
+        ref = _ref64(x1, x2)
+        assert got.shape == ref.shape
+        assert ((got.double() - ref).norm() / ref.norm()).item() <= TOL[variant]
+    assert _status_clean()
+
+
+@pytest.mark.parametrize("act", (None, "relu", "gelu"))
+@pytest.mark.parametrize("variant,split_k", [("3xtf32", 0), ("3xtf32", 5), ("tf32", 1), ("simt", 0), ("splitk", 4),
+                                             ("auto", 0)])
+def test_fused_bias_activation(variant, split_k, act):
+    """C = act(A.B + bias) with the epilogue in the GEMM's store (one K slice) or in the
+    split-K reduction.  Bias-only and ReLU results are exactly torch's fp32
+    act(x1 @ x2 + bias) on the same product; GELU (erf form) within 1e-6 of it."""
+    g = torch.Generator(device=DEV).manual_seed(21)
+    nb, m, k, n = 3, 384, 1024, 333
+    x1 = torch.randn(nb, m, k, device=DEV, generator=g)
+    x2 = torch.randn(nb, k, n, device=DEV, generator=g)
+    bias = torch.randn(n, device=DEV, generator=g)
+    got = ext.matrix_mul_ex(x1, x2, bias=bias, activation=act, variant=variant, split_k=split_k)
+    plain = ext.matrix_mul_ex(x1, x2, variant=variant, split_k=split_k)
+    want = plain + bias
+    if act == "relu":
+        want = torch.relu(want)
+    if act == "gelu":
+        want = torch.nn.functional.gelu(want)
+        assert ((got - want).norm() / want.norm()).item() <= 1e-6
+    else:
+        assert torch.equal(got, want)
+    ref = _ref64(x1, x2, bias, act)
+    assert ((got.double() - ref).norm() / ref.norm()).item() <= TOL[variant]
+    assert _status_clean()
+
+
+def test_fused_k0_and_large_batch():
+    """K = 0 stores act(bias); a batch of 70000 tiny products (more than one launch's grid)
+    matches fp64."""
+    bias = torch.linspace(-2, 2, 5, device=DEV)
+    got = ext.matrix_mul_ex(torch.empty(3, 4, 0, device=DEV), torch.empty(3, 0, 5, device=DEV), bias=bias,
+                            activation="relu")
+    assert torch.equal(got, torch.relu(bias).expand(3, 4, 5))
+    g = torch.Generator(device=DEV).manual_seed(3)
+    x1 = torch.randn(70000, 4, 8, device=DEV, generator=g)
+    x2 = torch.randn(70000, 8, 4, device=DEV, generator=g)
+    for variant in ("simt", "3xtf32"):
+        got = ext.matrix_mul_ex(x1, x2, variant=variant)
+        ref = _ref64(x1, x2)
+        assert ((got.double() - ref).norm() / ref.norm()).item() <= 1e-5, variant
+    assert _status_clean()
+
+
+def test_fused_argument_errors():
+    x1 = torch.randn(2, 8, 16, device=DEV)
+    x2 = torch.randn(2, 16, 4, device=DEV)
+    with pytest.raises(ValueError, match="activation"):
+        ext.matrix_mul_ex(x1, x2, activation="tanh")
+    with pytest.raises(ValueError, match="bias"):
+        ext.matrix_mul_ex(x1, x2, bias=torch.zeros(5, device=DEV))
+    with pytest.raises(ValueError, match="batch sizes"):
+        ext.matrix_mul_ex(x1, torch.randn(3, 16, 4, device=DEV))
+    with pytest.raises(ValueError, match="overlap"):
+        ext.matrix_mul_ex(x1, x2, out=torch.empty(8, 4, device=DEV).expand(2, 8, 4))

@@ -24,17 +24,18 @@ VARIANT_NAMES = {v: k for k, v in VARIANTS.items()}
 EXPORTS = [
     "tilec_mm_f32", "tilec_mm_workspace_bytes", "tilec_mm_plan", "tilec_mm_set_table",
     "tilec_mm_device_status", "tilec_strerror", "tilec_mm_abi_version", "tilec_mm_built_arch",
-    "tilec_mm_f32_splitk_noalloc", "tilec_mm_selftest_wait",
+    "tilec_mm_f32_splitk_noalloc", "tilec_mm_selftest_wait", "tilec_mm_f32_ex", "tilec_mm_workspace_bytes_ex",
 ]
 
 
 class MMConfig(ctypes.Structure):
     _fields_ = [("variant", ctypes.c_int32), ("split_k", ctypes.c_int32), ("flags", ctypes.c_int32),
-                ("reserved", ctypes.c_int32 * 5)]
+                ("activation", ctypes.c_int32), ("reserved", ctypes.c_int32 * 4)]
 
 
 TRANS_A = 1   # TILEC_MM_TRANS_A: A stored K x M (x1 is a column view, e.g. y.t())
 TRANS_B = 2   # TILEC_MM_TRANS_B: B stored N x K
+ACTIVATIONS = {None: 0, "none": 0, "relu": 1, "gelu": 2}   # TILEC_MM_ACT_*
 
 
 class TilecError(RuntimeError):
@@ -89,6 +90,12 @@ def load():
         lib.tilec_mm_f32_splitk_noalloc.restype = ctypes.c_int
         lib.tilec_mm_selftest_wait.argtypes = [i64, vp]
         lib.tilec_mm_selftest_wait.restype = ctypes.c_int
+        lib.tilec_mm_f32_ex.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64, cfgp, vp,
+                                        sz, vp]
+        lib.tilec_mm_f32_ex.restype = ctypes.c_int
+        lib.tilec_mm_workspace_bytes_ex.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64,
+                                                    cfgp]
+        lib.tilec_mm_workspace_bytes_ex.restype = sz
         _lib = lib
         return _lib
 
@@ -105,16 +112,16 @@ def check(code, where):
 _CFG_CACHE = {}
 
 
-def make_cfg(variant="auto", split_k=0, flags=0):
-    key = (variant, split_k, flags)
+def make_cfg(variant="auto", split_k=0, flags=0, activation=0):
+    key = (variant, split_k, flags, activation)
     cfg = _CFG_CACHE.get(key)
     if cfg is None:
-        cfg = _make_cfg(variant, split_k, flags)
+        cfg = _make_cfg(variant, split_k, flags, activation)
         _CFG_CACHE[key] = cfg
     return cfg
 
 
-def _make_cfg(variant, split_k, flags=0):
+def _make_cfg(variant, split_k, flags=0, activation=0):
     if isinstance(variant, str):
         try:
             v = VARIANTS[variant.lower()]
@@ -122,4 +129,4 @@ def _make_cfg(variant, split_k, flags=0):
             raise ValueError(f"unknown matrix_mul variant {variant!r}; expected one of {sorted(VARIANTS)}")
     else:
         v = int(variant)
-    return MMConfig(v, int(split_k), int(flags))
+    return MMConfig(v, int(split_k), int(flags), int(activation))

@@ -126,6 +126,27 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 3-D tiled load (x innermost, z = batch index); same rules as tma_load_2d.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y,
+                                            int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- epilogue
+// Element-wise epilogue applied where C is written: v + bias (when given), then the
+// activation (TILEC_MM_ACT_*: 0 none, 1 ReLU, 2 GELU with the exact erf form).
+enum : int { kActNone = 0, kActRelu = 1, kActGelu = 2 };
+__device__ __forceinline__ float epilogue(float v, float bias, int act) {
+  v += bias;
+  if (act == kActRelu) return fmaxf(v, 0.f);
+  if (act == kActGelu) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+  return v;
+}
+
 // ---------------------------------------------------------------- cp.async (SIMT path)
 __device__ __forceinline__ void cp_async_16(void* dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)

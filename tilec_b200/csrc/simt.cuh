@@ -95,12 +95,15 @@ __device__ __forceinline__ void simt_load_tile(float* as, float* bs, const float
   }
 }
 
-// out/ldo: C (gridDim.z == 1) or the split-K workspace (slab z at out + z*out_slab).
+// out/ldo: C (one K slice) or the split-K workspace (slab z at out + z*out_slab).
+// blockIdx.z = batch * splits + K slice; batch b reads A + b*stride_a, B + b*stride_b and
+// writes out + b*out_batch.  bias / act: fused epilogue (only when writing C directly).
 template <int BN, bool VEC>
 __global__ void __launch_bounds__(kSimtThreads, 1)
     simt_gemm_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ out,
                      int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldo, int64_t out_slab,
-                     int64_t k_chunk, int vec_out) {
+                     int64_t k_chunk, int vec_out, int splits, int64_t stride_a, int64_t stride_b,
+                     int64_t out_batch, const float* __restrict__ bias, int act) {
   constexpr int TN = BN / 16;  // columns per thread: 8 (two float4 groups 64 apart) or 4
   extern __shared__ __align__(16) float smem[];
   float* As = smem;
@@ -114,10 +117,14 @@ __global__ void __launch_bounds__(kSimtThreads, 1)
   const int tid = threadIdx.x;
   const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kSimtBM;
   const int64_t n0 = static_cast<int64_t>(blockIdx.y) * BN;
-  const int64_t k_begin = static_cast<int64_t>(blockIdx.z) * k_chunk;
+  const int64_t batch = static_cast<int64_t>(blockIdx.z) / splits;
+  const int64_t kslice = static_cast<int64_t>(blockIdx.z) % splits;
+  A += batch * stride_a;
+  B += batch * stride_b;
+  const int64_t k_begin = kslice * k_chunk;
   const int64_t k_end = (k_begin + k_chunk < K) ? k_begin + k_chunk : K;
   const int64_t nkt = (k_end > k_begin) ? (k_end - k_begin + kSimtBK - 1) / kSimtBK : 0;
-  out += static_cast<int64_t>(blockIdx.z) * out_slab;
+  out += kslice * out_slab + batch * out_batch;
 
   const int tm = tid >> 4;
   const int tn = tid & 15;
@@ -181,6 +188,17 @@ __global__ void __launch_bounds__(kSimtThreads, 1)
   pdl_launch_dependents();
 
   // Epilogue: masked stores (ext.py:24).  Each warp writes two 256-byte row runs.
+  if (bias != nullptr || act != kActNone) {
+#pragma unroll
+    for (int g = 0; g < TN / 4; ++g)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t gn = n0 + g * 64 + tn * 4 + j;
+        const float bv = (bias != nullptr && gn < N) ? __ldg(bias + gn) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i][g * 4 + j] = epilogue(acc[i][g * 4 + j], bv, act);
+      }
+  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int64_t gm = m0 + tm + 16 * i;
@@ -209,15 +227,22 @@ __global__ void __launch_bounds__(kSimtThreads, 1)
 // bitwise reproducible.  P and U are chosen so that one pass of resident blocks covers
 // the output with every load in flight at once (up to eight per thread at a time):
 // separate grid-stride rounds would each pay the full L2 latency again.
+//
+// Batched: blockIdx.y is the batch; its slabs are W + blockIdx.y*S*slab and its result
+// goes to C + blockIdx.y*stride_c.  bias / act: the fused epilogue, applied to the
+// finished sum.
 template <int P, int U>
-__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ W, float* __restrict__ C,
+__global__ void __launch_bounds__(256, 2) splitk_reduce_kernel(const float* __restrict__ W, float* __restrict__ C,
                                                             int64_t M, int64_t N, int64_t ldw, int64_t ldc,
-                                                            int64_t slab, int S, int vec_out) {
+                                                            int64_t slab, int S, int vec_out, int64_t stride_c,
+                                                            const float* __restrict__ bias, int act) {
   static_assert(8 % U == 0, "U divides the load batch");
   constexpr int G = 256 / P;
   __shared__ float4 part[P > 1 ? P - 1 : 1][P > 1 ? U * G : 1];
   pdl_wait();
   pdl_launch_dependents();
+  W += static_cast<int64_t>(blockIdx.y) * S * slab;
+  C += static_cast<int64_t>(blockIdx.y) * stride_c;
   const int p = static_cast<int>(threadIdx.x) / G;
   const int gi = static_cast<int>(threadIdx.x) % G;
   const int z0 = (S * p) / P, nz = (S * (p + 1)) / P - z0;
@@ -271,6 +296,15 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
           const float4 v = part[q - 1][u * G + gi];
           s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
         }
+        if (bias != nullptr || act != kActNone) {
+          float bv[4] = {0.f, 0.f, 0.f, 0.f};
+          if (bias != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bv[j] = nn[u] + j < N ? __ldg(bias + nn[u] + j) : 0.f;
+          }
+          s = make_float4(epilogue(s.x, bv[0], act), epilogue(s.y, bv[1], act), epilogue(s.z, bv[2], act),
+                          epilogue(s.w, bv[3], act));
+        }
         float* c = C + mm[u] * ldc + nn[u];
         if (vec_out && nn[u] + 3 < N) {
           *reinterpret_cast<float4*>(c) = s;
@@ -284,14 +318,20 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
   }
 }
 
-// K == 0: the reference's accumulator stays 0 and is stored (ext.py:18,24).
-__global__ void __launch_bounds__(256) fill_zero_kernel(float* __restrict__ C, int64_t M, int64_t N, int64_t ldc) {
+// K == 0: the reference's accumulator stays 0 and is stored (ext.py:18,24); with a fused
+// epilogue C = act(bias) per column.  All batches (C + b*stride_c) in one pass.
+__global__ void __launch_bounds__(256) fill_zero_kernel(float* __restrict__ C, int64_t M, int64_t N, int64_t ldc,
+                                                        int64_t batches, int64_t stride_c,
+                                                        const float* __restrict__ bias, int act) {
   pdl_wait();
   pdl_launch_dependents();
-  const int64_t total = M * N;
+  const int64_t total = batches * M * N;
   for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    C[(e / N) * ldc + (e % N)] = 0.f;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = e / N, n = e % N, b = row / M, m = row - b * M;
+    C[b * stride_c + m * ldc + n] =
+        (bias != nullptr || act != kActNone) ? epilogue(0.f, bias != nullptr ? bias[n] : 0.f, act) : 0.f;
+  }
 }
 
 }  // namespace tilec

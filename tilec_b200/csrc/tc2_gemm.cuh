@@ -66,7 +66,8 @@ template <int BN, int STAGES, bool HI_EXPLICIT>
 __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
     tc2_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     float* __restrict__ out, int M, int N, int64_t ldo, int64_t out_slab, int K, int k_chunk,
-                    int mp_tiles, int n_tiles, int group_m, int vec_out, int layout) {
+                    int mp_tiles, int n_tiles, int group_m, int vec_out, int layout, int64_t out_batch,
+                    const float* __restrict__ bias, int act, int shared) {
   using Cfg = Tc2Cfg<BN, STAGES>;
   constexpr int BK = Cfg::BK;
   constexpr int KC = Cfg::kChunkBlocks;
@@ -114,7 +115,9 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
   const int k_end = min(K, k_begin + k_chunk);
   const int nkb = k_end > k_begin ? (k_end - k_begin + BK - 1) / BK : 0;
   const int n_chunks = (nkb + KC - 1) / KC;
-  out += static_cast<int64_t>(blockIdx.z) * out_slab;
+  const int batch = static_cast<int>(blockIdx.y);
+  const int a_batch = (shared & 1) ? 0 : batch, b_batch = (shared & 2) ? 0 : batch;
+  out += static_cast<int64_t>(blockIdx.z) * out_slab + static_cast<int64_t>(batch) * out_batch;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -161,16 +164,17 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
         const int k0 = k_begin + kb * BK;
         if (layout & kOpAMN) {
 #pragma unroll
-          for (int j = 0; j < 128 / 32; ++j) tma_load_2d(a_raw(s) + j * BK * 128, &tmA, &full[s], m0 + 32 * j, k0);
+          for (int j = 0; j < 128 / 32; ++j)
+            tma_load_3d(a_raw(s) + j * BK * 128, &tmA, &full[s], m0 + 32 * j, k0, a_batch);
         } else {
-          tma_load_2d(a_raw(s), &tmA, &full[s], k0, m0);
+          tma_load_3d(a_raw(s), &tmA, &full[s], k0, m0, a_batch);
         }
         if (layout & kOpBK) {
-          tma_load_2d(b_raw(s), &tmB, &full[s], k0, nb0);
+          tma_load_3d(b_raw(s), &tmB, &full[s], k0, nb0, b_batch);
         } else {
 #pragma unroll
           for (int j = 0; j < Cfg::kBNHalf / 32; ++j)
-            tma_load_2d(b_raw(s) + j * BK * 128, &tmB, &full[s], nb0 + 32 * j, k0);
+            tma_load_3d(b_raw(s) + j * BK * 128, &tmB, &full[s], nb0 + 32 * j, k0, b_batch);
         }
         ++issued;
       }
@@ -326,7 +330,7 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
     pdl_launch_dependents();
     if (ok) {
       float* stage = reinterpret_cast<float*>(smem) + e * 32 * (COLS + 4);
-      store_rows_coalesced<COLS>(stage, tot, out, ldo, m0 + 32 * q, n0 + h * COLS, M, N, vec_out, lane);
+      store_rows_coalesced<COLS>(stage, tot, out, ldo, m0 + 32 * q, n0 + h * COLS, M, N, vec_out, lane, bias, act);
     }
   }
 

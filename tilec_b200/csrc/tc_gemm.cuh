@@ -89,21 +89,30 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
 // staging buffer `stage` (32 x (NC + 4) floats; the pitch of NC + 4 keeps both passes
 // free of bank conflicts) so that consecutive lanes store consecutive 16-byte pieces of
 // one row: the warp writes whole row runs instead of 32 rows 16 bytes at a time.
-template <int NC>
-__device__ __forceinline__ void store_rows_coalesced(float* stage, const float (&v)[NC], float* out, int64_t ldo,
-                                                     int row0, int col0, int M, int N, int vec_out, int lane) {
+//
+// `bias` (per column, or nullptr) and `act` (kAct*) apply the fused epilogue on the way;
+// the test is made once, outside the store loop (EPI instantiates the loop with it).
+template <int NC, bool EPI>
+__device__ __forceinline__ void store_rows_pass(const float* stage, float* out, int64_t ldo, int row0, int col0,
+                                                int M, int N, int vec_out, int lane, const float* __restrict__ bias,
+                                                int act) {
   constexpr int kPitch = NC + 4;
   constexpr int kChunks = NC / 4;  // 16-byte pieces per row
-#pragma unroll
-  for (int j = 0; j < NC; j += 4)
-    *reinterpret_cast<float4*>(stage + lane * kPitch + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-  __syncwarp();
 #pragma unroll 4
   for (int c = lane; c < 32 * kChunks; c += 32) {
     const int r = c / kChunks, piece = c % kChunks;
     const int grow = row0 + r, gcol = col0 + 4 * piece;
     if (grow < M) {
-      const float4 x = *reinterpret_cast<const float4*>(stage + r * kPitch + 4 * piece);
+      float4 x = *reinterpret_cast<const float4*>(stage + r * kPitch + 4 * piece);
+      if constexpr (EPI) {
+        float bv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (bias != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) bv[j] = gcol + j < N ? __ldg(bias + gcol + j) : 0.f;
+        }
+        x = make_float4(epilogue(x.x, bv[0], act), epilogue(x.y, bv[1], act), epilogue(x.z, bv[2], act),
+                        epilogue(x.w, bv[3], act));
+      }
       float* dst = out + static_cast<int64_t>(grow) * ldo + gcol;
       if (vec_out && gcol + 3 < N) {
         *reinterpret_cast<float4*>(dst) = x;
@@ -115,15 +124,34 @@ __device__ __forceinline__ void store_rows_coalesced(float* stage, const float (
       }
     }
   }
+}
+
+template <int NC>
+__device__ __forceinline__ void store_rows_coalesced(float* stage, const float (&v)[NC], float* out, int64_t ldo,
+                                                     int row0, int col0, int M, int N, int vec_out, int lane,
+                                                     const float* __restrict__ bias = nullptr, int act = kActNone) {
+  constexpr int kPitch = NC + 4;
+#pragma unroll
+  for (int j = 0; j < NC; j += 4)
+    *reinterpret_cast<float4*>(stage + lane * kPitch + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  __syncwarp();
+  if (bias != nullptr || act != kActNone)
+    store_rows_pass<NC, true>(stage, out, ldo, row0, col0, M, N, vec_out, lane, bias, act);
+  else
+    store_rows_pass<NC, false>(stage, out, ldo, row0, col0, M, N, vec_out, lane, nullptr, kActNone);
   __syncwarp();
 }
 
-// Grid: x = tile index (grouped raster), z = K split (slabs of `out`).
+// Grid: x = tile index (grouped raster), y = batch index, z = K split (slabs of `out`).
+// Operand tensor maps are 3-D (x inner, y outer, z batch); an operand's batch coordinate
+// is 0 when it is shared by all batches (`shared` bit 0 = A, bit 1 = B).  `out` advances by out_batch per batch and out_slab per K slice; bias / act
+// are the fused epilogue (only when C is written directly, i.e. without a K split).
 template <int BN, int BK, int STAGES, bool SPLIT3, bool HI_EXPLICIT>
 __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    float* __restrict__ out, int M, int N, int64_t ldo, int64_t out_slab, int K, int k_chunk,
-                   int m_tiles, int n_tiles, int group_m, int vec_out, int layout) {
+                   int m_tiles, int n_tiles, int group_m, int vec_out, int layout, int64_t out_batch,
+                   const float* __restrict__ bias, int act, int shared) {
   using Cfg = TcCfg<BN, BK, STAGES, SPLIT3>;
   constexpr int KC = Cfg::kChunkBlocks;
   extern __shared__ uint8_t smem_raw[];
@@ -162,7 +190,9 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
   const int tile_m = first_m + in_band % band_rows;
   const int tile_n = in_band / band_rows;
   const int kslice = static_cast<int>(blockIdx.z);
-  out += static_cast<int64_t>(blockIdx.z) * out_slab;
+  const int batch = static_cast<int>(blockIdx.y);
+  const int a_batch = (shared & 1) ? 0 : batch, b_batch = (shared & 2) ? 0 : batch;
+  out += static_cast<int64_t>(blockIdx.z) * out_slab + static_cast<int64_t>(batch) * out_batch;
   const int m0 = tile_m * kTcBM;
   const int n0 = tile_n * BN;
 
@@ -214,15 +244,17 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
         const int k0 = k_begin + kb * BK;
         if (layout & kOpAMN) {
 #pragma unroll
-          for (int j = 0; j < kTcBM / 32; ++j) tma_load_2d(a_raw(s) + j * BK * 128, &tmA, &full[s], m0 + 32 * j, k0);
+          for (int j = 0; j < kTcBM / 32; ++j)
+            tma_load_3d(a_raw(s) + j * BK * 128, &tmA, &full[s], m0 + 32 * j, k0, a_batch);
         } else {
-          tma_load_2d(a_raw(s), &tmA, &full[s], k0, m0);
+          tma_load_3d(a_raw(s), &tmA, &full[s], k0, m0, a_batch);
         }
         if (layout & kOpBK) {
-          tma_load_2d(b_raw(s), &tmB, &full[s], k0, n0);
+          tma_load_3d(b_raw(s), &tmB, &full[s], k0, n0, b_batch);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 32; ++j) tma_load_2d(b_raw(s) + j * BK * 128, &tmB, &full[s], n0 + 32 * j, k0);
+          for (int j = 0; j < BN / 32; ++j)
+            tma_load_3d(b_raw(s) + j * BK * 128, &tmB, &full[s], n0 + 32 * j, k0, b_batch);
         }
         ++issued;
       }
@@ -365,7 +397,8 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
       pdl_launch_dependents();
       if (ok) {
         float* stage = reinterpret_cast<float*>(smem) + e * Cfg::kStageFloatsPerWarp;
-        store_rows_coalesced<COLS>(stage, tot, out, ldo, m0 + 32 * q, n0 + h * COLS, M, N, vec_out, lane);
+        store_rows_coalesced<COLS>(stage, tot, out, ldo, m0 + 32 * q, n0 + h * COLS, M, N, vec_out, lane, bias,
+                                   act);
       }
     } else {
       if (nkb > 0) ok = mbar_wait(acc_bar, 0, abort_flag);
@@ -386,7 +419,7 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          store_rows_coalesced<32>(stage, v, out, ldo, m0 + 32 * q, n0 + c * 32, M, N, vec_out, lane);
+          store_rows_coalesced<32>(stage, v, out, ldo, m0 + 32 * q, n0 + c * 32, M, N, vec_out, lane, bias, act);
         }
       }
     }

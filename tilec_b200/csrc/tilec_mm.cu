@@ -157,8 +157,20 @@ inline int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
 
 // Workspace layout (each region 256-byte aligned):
 //   [packed A: M x round_up(K,4)] [packed B: K x round_up(N,4)] [split-K slabs: split x M x round_up(N,4)]
-// Packed copies exist only for operands whose rows are not 16-byte aligned and only on
-// the tensor-core path (TMA needs 16-byte aligned bases and row strides).
+// One call's arguments: a single product is batch 1 (batch strides unused).  Batch b reads
+// A + b*stride_a and B + b*stride_b (a zero stride shares that operand) and writes
+// C + b*stride_c; bias (per column, or nullptr) and act form the fused epilogue.
+struct Problem {
+  const float* A = nullptr;
+  const float* B = nullptr;
+  float* C = nullptr;
+  const float* bias = nullptr;
+  int64_t M = 0, N = 0, K = 0, lda = 0, ldb = 0, ldc = 0;
+  int64_t batch = 1, stride_a = 0, stride_b = 0, stride_c = 0;
+};
+
+// Packed copies exist only for operands whose rows (or batch strides) are not 16-byte
+// aligned and only on the tensor-core path (TMA needs 16-byte aligned bases and strides).
 struct Plan {
   int variant = TILEC_MM_SIMT;
   int split = 1;
@@ -170,6 +182,8 @@ struct Plan {
   bool pack_a = false, pack_b = false;    // tensor variants: aligned copy, same storage order
   bool tpose_a = false, tpose_b = false;  // SIMT variants: transposed operand -> row-major copy
   bool pair = false;  // 3XTF32 on a CTA pair (tc2_gemm_kernel, 256 x 256 tiles)
+  bool a_shared = false, b_shared = false;  // batch > 1 with a zero batch stride
+  int act = 0;                              // TILEC_MM_ACT_*
   size_t off_a = 0, off_b = 0, off_slabs = 0;
 };
 
@@ -194,7 +208,7 @@ int ilog2_floor(int64_t v) {
 
 // Built-in AUTO rules (a table installed with tilec_mm_set_table overrides them).
 void choose_auto(const DeviceInfo& d, const float* A, const float* B, int64_t M, int64_t N, int64_t K,
-                 int64_t lda, int64_t ldb, int* variant, int* split) {
+                 int64_t lda, int64_t ldb, int64_t batch, int* variant, int* split) {
   {
     std::lock_guard<std::mutex> lk(g_table_mu);
     if (!g_table.empty()) {
@@ -214,7 +228,7 @@ void choose_auto(const DeviceInfo& d, const float* A, const float* B, int64_t M,
   }
   (void)d;
   *split = 0;
-  const double flops = 2.0 * double(M) * double(N) * double(K);
+  const double flops = 2.0 * double(M) * double(N) * double(K) * double(batch);
   const bool aligned = tensor_path_ok(A, B, M, N, K, lda, ldb);
   // Misaligned operands are packed first (2 x (MK + KN) x 4 bytes of traffic): worth it
   // once the product is large enough for the tensor cores to win by a wide margin.
@@ -222,7 +236,7 @@ void choose_auto(const DeviceInfo& d, const float* A, const float* B, int64_t M,
     *variant = TILEC_MM_3XTF32;
     return;
   }
-  const int64_t tiles = cdiv(M, kSimtBM) * cdiv(N, N <= 64 ? 64 : 128);
+  const int64_t tiles = cdiv(M, kSimtBM) * cdiv(N, N <= 64 ? 64 : 128) * batch;
   *variant = (tiles < d.sms && K >= 1024) ? TILEC_MM_SPLITK : TILEC_MM_SIMT;
 }
 
@@ -271,27 +285,31 @@ double cta_seconds(int64_t rows, int64_t cols, int64_t b_cols, int64_t K, double
 // FMA ~0.31; HBM share ~38 GB/s per SM with every SM streaming.
 constexpr double kRate3x = 1.7e12, kRateTf32 = 4.3e12, kRateSimt = 0.31e12, kBwPerSm = 38.0e9;
 
-int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K,
-              int64_t lda, int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg, Plan* p) {
-  (void)C;
-  (void)ldc;
+int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Plan* p) {
+  const int64_t M = q.M, N = q.N, K = q.K, nb = q.batch;
   int variant = cfg ? cfg->variant : TILEC_MM_AUTO;
   int requested_split = cfg ? cfg->split_k : 0;
   const int flags = cfg ? cfg->flags : 0;
+  const int act = cfg ? cfg->activation : 0;
   if (flags & ~(TILEC_MM_TRANS_A | TILEC_MM_TRANS_B)) return TILEC_ERR_BAD_ARG;
+  if (act < TILEC_MM_ACT_NONE || act > TILEC_MM_ACT_GELU) return TILEC_ERR_BAD_ARG;
   if (cfg) {
-    for (int i = 0; i < 5; ++i)
+    for (int i = 0; i < 4; ++i)
       if (cfg->reserved[i] != 0) return TILEC_ERR_BAD_ARG;
   }
   p->flags = flags;
+  p->act = act;
+  p->a_shared = nb > 1 && q.stride_a == 0;
+  p->b_shared = nb > 1 && q.stride_b == 0;
   if (requested_split < 0) return TILEC_ERR_BAD_ARG;
-  if (variant == TILEC_MM_AUTO) choose_auto(d, A, B, M, N, K, lda, ldb, &variant, &requested_split);
+  if (variant == TILEC_MM_AUTO) choose_auto(d, q.A, q.B, M, N, K, q.lda, q.ldb, nb, &variant, &requested_split);
   if (variant < TILEC_MM_SIMT || variant > TILEC_MM_3XTF32_MASKED) return TILEC_ERR_BAD_ARG;
   const bool tensor = variant == TILEC_MM_TF32 || variant == TILEC_MM_3XTF32 || variant == TILEC_MM_3XTF32_MASKED;
   if (tensor && !tensor_dims_ok(M, N, K)) return TILEC_ERR_UNSUPPORTED;
   if (tensor) {
-    p->pack_a = !rows_aligned(A, lda);
-    p->pack_b = !rows_aligned(B, ldb);
+    // TMA also needs each batch's base 16-byte aligned: batch strides a multiple of 4.
+    p->pack_a = !rows_aligned(q.A, q.lda) || (nb > 1 && q.stride_a % 4 != 0);
+    p->pack_b = !rows_aligned(q.B, q.ldb) || (nb > 1 && q.stride_b % 4 != 0);
   } else {
     p->tpose_a = (flags & TILEC_MM_TRANS_A) != 0;
     p->tpose_b = (flags & TILEC_MM_TRANS_B) != 0;
@@ -305,22 +323,22 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
     const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
     // The CTA pair launches two CTAs per 256-row x 256-column tile; each computes 128 rows
     // and loads half of the B columns.
-    const int64_t ctas = p->pair ? 2 * cdiv(M, 256) * cdiv(N, 256) : tiles;
+    const int64_t ctas = (p->pair ? 2 * cdiv(M, 256) * cdiv(N, 256) : tiles) * nb;
     const double cta_s = cta_seconds(kTcBM, p->bn, p->pair ? p->bn / 2 : p->bn, K,
                                      variant == TILEC_MM_TF32 ? kRateTf32 : kRate3x, kBwPerSm);
-    p->split = choose_split(ctas, d.sms, cta_s, double(M) * double(round_up(N, 4)) * 4.0, K / (int64_t(bk) * 4),
-                            requested_split, /*one_wave=*/true);
+    p->split = choose_split(ctas, d.sms, cta_s, double(M) * double(round_up(N, 4)) * 4.0 * double(nb),
+                            K / (int64_t(bk) * 4), requested_split, /*one_wave=*/true);
     p->k_chunk = round_up(cdiv(K, p->split), bk);
     p->split = static_cast<int>(cdiv(K, p->k_chunk > 0 ? p->k_chunk : 1));
     if (p->split < 1) p->split = 1;
   } else {
     p->bn = N <= 64 ? 64 : 128;
-    const int64_t tiles = cdiv(M, kSimtBM) * cdiv(N, p->bn);
+    const int64_t tiles = cdiv(M, kSimtBM) * cdiv(N, p->bn) * nb;
     int split = 1;
     if (variant == TILEC_MM_SPLITK) {
       const double cta_s = cta_seconds(kSimtBM, p->bn, p->bn, K, kRateSimt, kBwPerSm);
-      split = choose_split(tiles, d.sms, cta_s, double(M) * double(round_up(N, 4)) * 4.0, K / (int64_t(kSimtBK) * 4),
-                           requested_split, /*one_wave=*/false);
+      split = choose_split(tiles, d.sms, cta_s, double(M) * double(round_up(N, 4)) * 4.0 * double(nb),
+                           K / (int64_t(kSimtBK) * 4), requested_split, /*one_wave=*/false);
     }
     p->k_chunk = round_up(cdiv(K, split), kSimtBK);
     split = static_cast<int>(cdiv(K, p->k_chunk > 0 ? p->k_chunk : 1));
@@ -329,21 +347,22 @@ int make_plan(const DeviceInfo& d, const float* A, const float* B, const float* 
   if (p->k_chunk <= 0) p->k_chunk = 16;
   p->ldw = round_up(N, 4);
   // An aligned copy keeps the stored order (K x M for a transposed A); a SIMT transpose
-  // writes the row-major M x K (K x N) operand.
+  // writes the row-major M x K (K x N) operand.  One copy per batch (one when shared).
   const bool ta = (flags & TILEC_MM_TRANS_A) != 0, tb = (flags & TILEC_MM_TRANS_B) != 0;
+  const size_t na = p->a_shared ? 1 : size_t(nb), nbb = p->b_shared ? 1 : size_t(nb);
   size_t off = 0;
   if (p->pack_a || p->tpose_a) {
     p->off_a = off;
     const size_t elems = (p->pack_a && ta) ? size_t(K) * size_t(round_up(M, 4)) : size_t(M) * size_t(round_up(K, 4));
-    off += align256(elems * sizeof(float));
+    off += align256(na * elems * sizeof(float));
   }
   if (p->pack_b || p->tpose_b) {
     p->off_b = off;
     const size_t elems = (p->pack_b && tb) ? size_t(N) * size_t(round_up(K, 4)) : size_t(K) * size_t(round_up(N, 4));
-    off += align256(elems * sizeof(float));
+    off += align256(nbb * elems * sizeof(float));
   }
   p->off_slabs = off;
-  if (p->split > 1) off += size_t(p->split) * size_t(M) * size_t(p->ldw) * sizeof(float);
+  if (p->split > 1) off += size_t(nb) * size_t(p->split) * size_t(M) * size_t(p->ldw) * sizeof(float);
   p->ws_bytes = off;
   return TILEC_OK;
 }
@@ -360,34 +379,49 @@ int check_args(const float* A, const float* B, const float* C, int64_t M, int64_
   return TILEC_OK;
 }
 
+// check_args for every product of a batch, plus: non-negative batch and strides, and
+// batches of C that do not overlap (they are written concurrently).
+int check_problem(const Problem& q, bool need_c, int flags) {
+  const int rc = check_args(q.A, q.B, q.C, q.M, q.N, q.K, q.lda, q.ldb, q.ldc, need_c, flags);
+  if (rc) return rc;
+  if (q.batch < 0 || q.stride_a < 0 || q.stride_b < 0 || q.stride_c < 0) return TILEC_ERR_BAD_ARG;
+  if (q.batch > 1 && q.M > 0 && q.N > 0 && q.stride_c < (q.M - 1) * q.ldc + q.N) return TILEC_ERR_BAD_ARG;
+  return TILEC_OK;
+}
+
 int launch_status() {
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TILEC_OK : TILEC_ERR_LAUNCH;
 }
 
-// Tensor maps for the operand tiles (`layout`: kOpAMN / kOpBK, see common.cuh).  A K-major:
-// box {bk, 128} with a bk*4-byte swizzle; A MN-major (stored K x M): boxes {32, bk} with
-// the 128-byte / 32-byte-granule swizzle.  B MN-major: boxes {32, bk}, same swizzle; B
-// K-major (stored N x K): box {bk, b_rows}, bk*4-byte swizzle.
+// Tensor maps for the operand tiles (`layout`: kOpAMN / kOpBK, see common.cuh), 3-D with
+// the batch outermost (extent 1 for a single or shared operand).  A K-major: box {bk, 128}
+// with a bk*4-byte swizzle; A MN-major (stored K x M): boxes {32, bk} with the 128-byte /
+// 32-byte-granule swizzle.  B MN-major: boxes {32, bk}, same swizzle; B K-major (stored
+// N x K): box {bk, b_rows}, bk*4-byte swizzle.
 int encode_maps(const float* A, const float* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
-                int bk, int layout, int b_rows, CUtensorMap* ma, CUtensorMap* mb) {
+                int64_t stride_a, int64_t nba, int64_t stride_b, int64_t nbb, int bk, int layout, int b_rows,
+                CUtensorMap* ma, CUtensorMap* mb) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode();
   if (!enc) return TILEC_ERR_NO_DEVICE;
   const CUtensorMapSwizzle k_sw = bk * 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  auto encode = [&](CUtensorMap* m, const float* base, int64_t inner, int64_t outer, int64_t ld, int box_in,
-                    int box_out, CUtensorMapSwizzle sw) {
-    cuuint64_t dims[2] = {cuuint64_t(inner), cuuint64_t(outer)};
-    cuuint64_t strides[1] = {cuuint64_t(ld) * 4};
-    cuuint32_t box[2] = {cuuint32_t(box_in), cuuint32_t(box_out)};
-    cuuint32_t estr[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+  auto encode = [&](CUtensorMap* m, const float* base, int64_t inner, int64_t outer, int64_t ld, int64_t bstride,
+                    int64_t nbatch, int box_in, int box_out, CUtensorMapSwizzle sw) {
+    cuuint64_t dims[3] = {cuuint64_t(inner), cuuint64_t(outer), cuuint64_t(nbatch)};
+    const int64_t bs = nbatch > 1 ? bstride : round_up(outer * ld, 4);
+    cuuint64_t strides[2] = {cuuint64_t(ld) * 4, cuuint64_t(bs) * 4};
+    cuuint32_t box[3] = {cuuint32_t(box_in), cuuint32_t(box_out), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
   };
-  const bool ok_a = (layout & kOpAMN) ? encode(ma, A, M, K, lda, 32, bk, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
-                                      : encode(ma, A, K, M, lda, bk, kTcBM, k_sw);
-  const bool ok_b = (layout & kOpBK) ? encode(mb, B, K, N, ldb, bk, b_rows, k_sw)
-                                     : encode(mb, B, N, K, ldb, 32, bk, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  const bool ok_a = (layout & kOpAMN)
+                        ? encode(ma, A, M, K, lda, stride_a, nba, 32, bk, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
+                        : encode(ma, A, K, M, lda, stride_a, nba, bk, kTcBM, k_sw);
+  const bool ok_b = (layout & kOpBK) ? encode(mb, B, K, N, ldb, stride_b, nbb, bk, b_rows, k_sw)
+                                     : encode(mb, B, N, K, ldb, stride_b, nbb, 32, bk,
+                                              CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
   return ok_a && ok_b ? TILEC_OK : TILEC_ERR_BAD_ARG;
 }
 
@@ -441,59 +475,76 @@ int launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStr
   return launch_kx(true, kern, grid, block, smem, s, cluster_x, args...);
 }
 
+// Per-launch arguments of the GEMM kernels: where the output goes (C, or the split-K
+// slabs: slab z of batch b at out + z*out_slab + b*out_batch), the fused epilogue (only
+// when writing C), the batch count (grid y) and the shared-operand bits.
+struct Launch {
+  float* out = nullptr;
+  int64_t ldo = 0, out_slab = 0, out_batch = 0, k_chunk = 0;
+  int split = 1, vec_out = 0, layout = 0, batch = 1, shared = 0, act = 0;
+  const float* bias = nullptr;
+};
+
 template <int BN, int BK, int STAGES, bool SPLIT3, bool HI>
-int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N, int64_t ldo,
-              int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, int layout, cudaStream_t s) {
+int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
+              cudaStream_t s) {
   using Cfg = TcCfg<BN, BK, STAGES, SPLIT3>;
   const int m_tiles = static_cast<int>(cdiv(M, kTcBM));
   const int n_tiles = static_cast<int>(cdiv(N, BN));
   const int group_m = 16;
-  dim3 grid(static_cast<unsigned>(int64_t(m_tiles) * n_tiles), 1, static_cast<unsigned>(split));
+  const dim3 grid(static_cast<unsigned>(int64_t(m_tiles) * n_tiles), static_cast<unsigned>(L.batch),
+                  static_cast<unsigned>(L.split));
   return launch_k(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 1, ma,
-                  mb, out, static_cast<int>(M), static_cast<int>(N), ldo, slab, static_cast<int>(K),
-                  static_cast<int>(k_chunk), m_tiles, n_tiles, group_m, vec_out, layout);
+                  mb, L.out, static_cast<int>(M), static_cast<int>(N), L.ldo, L.out_slab, static_cast<int>(K),
+                  static_cast<int>(L.k_chunk), m_tiles, n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias,
+                  L.act, L.shared);
 }
 
 template <int BN, bool SPLIT3, bool HI>
-int launch_tc_mode(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N, int64_t ldo,
-                   int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, int layout, cudaStream_t s) {
+int launch_tc_mode(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
+                   cudaStream_t s) {
   if constexpr (SPLIT3)
-    return launch_tc<BN, k3xBK, TcShape<BN>::k3xStages, true, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split,
-                                                                  vec_out, layout, s);
+    return launch_tc<BN, k3xBK, TcShape<BN>::k3xStages, true, HI>(ma, mb, M, N, K, L, s);
   else
-    return launch_tc<BN, 32, TcShape<BN>::kTf32Stages, false, false>(ma, mb, out, M, N, ldo, slab, K, k_chunk,
-                                                                     split, vec_out, layout, s);
+    return launch_tc<BN, 32, TcShape<BN>::kTf32Stages, false, false>(ma, mb, M, N, K, L, s);
 }
 
 template <bool HI>
-int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N, int64_t ldo,
-               int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, int layout, cudaStream_t s) {
+int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
+               cudaStream_t s) {
   using Cfg = Tc2Cfg<256, kPairStages>;
   const int mp_tiles = static_cast<int>(cdiv(M, 256));
   const int n_tiles = static_cast<int>(cdiv(N, 256));
   const int group_m = 8;
-  const dim3 grid(static_cast<unsigned>(2 * int64_t(mp_tiles) * n_tiles), 1, static_cast<unsigned>(split));
+  const dim3 grid(static_cast<unsigned>(2 * int64_t(mp_tiles) * n_tiles), static_cast<unsigned>(L.batch),
+                  static_cast<unsigned>(L.split));
   return launch_k(tc2_gemm_kernel<256, kPairStages, HI>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 2, ma, mb,
-                  out, static_cast<int>(M), static_cast<int>(N), ldo, slab, static_cast<int>(K),
-                  static_cast<int>(k_chunk), mp_tiles, n_tiles, group_m, vec_out, layout);
+                  L.out, static_cast<int>(M), static_cast<int>(N), L.ldo, L.out_slab, static_cast<int>(K),
+                  static_cast<int>(L.k_chunk), mp_tiles, n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias,
+                  L.act, L.shared);
 }
 
 template <bool SPLIT3, bool HI>
-int dispatch_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, float* out, int64_t M, int64_t N,
-                   int64_t ldo, int64_t slab, int64_t K, int64_t k_chunk, int split, int vec_out, int layout, cudaStream_t s) {
+int dispatch_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K,
+                   const Launch& L, cudaStream_t s) {
   switch (bn) {
-    case 64: return launch_tc_mode<64, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, layout, s);
-    case 128: return launch_tc_mode<128, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, layout, s);
-    default: return launch_tc_mode<256, SPLIT3, HI>(ma, mb, out, M, N, ldo, slab, K, k_chunk, split, vec_out, layout, s);
+    case 64: return launch_tc_mode<64, SPLIT3, HI>(ma, mb, M, N, K, L, s);
+    case 128: return launch_tc_mode<128, SPLIT3, HI>(ma, mb, M, N, K, L, s);
+    default: return launch_tc_mode<256, SPLIT3, HI>(ma, mb, M, N, K, L, s);
   }
 }
 
-// dst[r, 0:cols] = src[r, 0:cols] with row strides lds / ldd (one CTA per row, grid-stride).
-__global__ void __launch_bounds__(256) pack_rows_kernel(const float* __restrict__ src, int64_t lds,
+// dst[b][r, 0:cols] = src[b][r, 0:cols] for batch b = blockIdx.y (src batch stride
+// sstride, dst dense: batch stride rows*ldd), row strides lds / ldd; one CTA per row,
+// grid-stride.
+__global__ void __launch_bounds__(256) pack_rows_kernel(const float* __restrict__ src, int64_t lds, int64_t sstride,
                                                         float* __restrict__ dst, int64_t ldd, int64_t rows,
-                                                        int64_t cols) {
+                                                        int64_t cols, int64_t batches) {
   pdl_wait();
   pdl_launch_dependents();
+  (void)batches;
+  src += static_cast<int64_t>(blockIdx.y) * sstride;
+  dst += static_cast<int64_t>(blockIdx.y) * rows * ldd;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* s = src + r * lds;
     float* d = dst + r * ldd;
@@ -501,76 +552,94 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const float* __restrict_
   }
 }
 
-// dst[c, r] = src[r, c] for r < rows, c < cols: 32 x 32 tiles through shared memory (the
+// dst[b][c, r] = src[b][r, c] for r < rows, c < cols, batch b = blockIdx.y (src batch
+// stride sstride, dst dense: batch stride cols*ldd): 32 x 32 tiles through shared memory (the
 // +1 column keeps the transposed reads free of bank conflicts), coalesced on both sides.
-__global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict__ src, int64_t lds,
+__global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict__ src, int64_t lds, int64_t sstride,
                                                         float* __restrict__ dst, int64_t ldd, int64_t rows,
-                                                        int64_t cols) {
+                                                        int64_t cols, int64_t batches) {
   __shared__ float t[32][33];
   pdl_wait();
   pdl_launch_dependents();
   const int64_t tr = (rows + 31) / 32, tc = (cols + 31) / 32;
   const int tx = static_cast<int>(threadIdx.x) & 31, ty = static_cast<int>(threadIdx.x) >> 5;  // 32 x 8
+  (void)batches;
+  const float* sb = src + static_cast<int64_t>(blockIdx.y) * sstride;
+  float* db = dst + static_cast<int64_t>(blockIdx.y) * cols * ldd;
   for (int64_t tile = blockIdx.x; tile < tr * tc; tile += gridDim.x) {
     const int64_t r0 = (tile / tc) * 32, c0 = (tile % tc) * 32;
     for (int i = ty; i < 32; i += 8) {
       const int64_t r = r0 + i, c = c0 + tx;
-      if (r < rows && c < cols) t[i][tx] = src[r * lds + c];
+      if (r < rows && c < cols) t[i][tx] = sb[r * lds + c];
     }
     __syncthreads();
     for (int i = ty; i < 32; i += 8) {
       const int64_t c = c0 + i, r = r0 + tx;
-      if (r < rows && c < cols) dst[c * ldd + r] = t[tx][i];
+      if (r < rows && c < cols) db[c * ldd + r] = t[tx][i];
     }
     __syncthreads();
   }
 }
 
-int launch_transpose(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows, int64_t cols,
-                     const DeviceInfo& d, cudaStream_t s) {
+int launch_transpose(const float* src, int64_t lds, int64_t sstride, float* dst, int64_t ldd, int64_t rows,
+                     int64_t cols, int64_t batches, const DeviceInfo& d, cudaStream_t s) {
   int64_t blocks = cdiv(rows, 32) * cdiv(cols, 32);
-  if (blocks > int64_t(d.sms) * 8) blocks = int64_t(d.sms) * 8;
+  const int64_t cap = int64_t(d.sms) * 8 / batches + 1;
+  if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  return launch_k(transpose_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, 1, src, lds, dst, ldd, rows,
-                  cols);
+  return launch_k(transpose_kernel, dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(batches)), dim3(256), 0,
+                  s, 1, src, lds, sstride, dst, ldd, rows, cols, batches);
 }
 
-int launch_pack(const float* src, int64_t lds, float* dst, int64_t ldd, int64_t rows, int64_t cols,
-                const DeviceInfo& d, cudaStream_t s) {
-  int64_t blocks = rows < int64_t(d.sms) * 16 ? rows : int64_t(d.sms) * 16;
+int launch_pack(const float* src, int64_t lds, int64_t sstride, float* dst, int64_t ldd, int64_t rows, int64_t cols,
+                int64_t batches, const DeviceInfo& d, cudaStream_t s) {
+  const int64_t cap = int64_t(d.sms) * 16 / batches + 1;
+  int64_t blocks = rows < cap ? rows : cap;
   if (blocks < 1) blocks = 1;
-  return launch_k(pack_rows_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, 1, src, lds, dst, ldd, rows,
-                  cols);
+  return launch_k(pack_rows_kernel, dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(batches)), dim3(256), 0,
+                  s, 1, src, lds, sstride, dst, ldd, rows, cols, batches);
 }
+
+// The split-K reduction of all batches (slabs of batch b at ws + b*split*M*ldw) into C,
+// with the fused epilogue.
+struct Reduce {
+  const float* ws = nullptr;
+  float* C = nullptr;
+  int64_t M = 0, N = 0, ldw = 0, ldc = 0, batches = 1, stride_c = 0;
+  int split = 1, act = 0;
+  const float* bias = nullptr;
+};
 
 template <int P>
-int launch_reduce_p(int U, dim3 grid, const float* ws, float* C, int64_t M, int64_t N, int64_t ldw, int64_t ldc,
-                    int64_t slab, int split, int vec_out, cudaStream_t s) {
+int launch_reduce_p(int U, dim3 grid, const Reduce& r, int vec_out, cudaStream_t s) {
+  const int64_t slab = r.M * r.ldw;
+  auto go = [&](auto kern) {
+    return launch_k(kern, grid, dim3(256), 0, s, 1, r.ws, r.C, r.M, r.N, r.ldw, r.ldc, slab, r.split, vec_out,
+                    r.stride_c, r.bias, r.act);
+  };
   switch (U) {
-    case 4: return launch_k(splitk_reduce_kernel<P, 4>, grid, dim3(256), 0, s, 1, ws, C, M, N, ldw, ldc, slab, split, vec_out);
-    case 2: return launch_k(splitk_reduce_kernel<P, 2>, grid, dim3(256), 0, s, 1, ws, C, M, N, ldw, ldc, slab, split, vec_out);
-    default: return launch_k(splitk_reduce_kernel<P, 1>, grid, dim3(256), 0, s, 1, ws, C, M, N, ldw, ldc, slab, split, vec_out);
+    case 4: return go(splitk_reduce_kernel<P, 4>);
+    case 2: return go(splitk_reduce_kernel<P, 2>);
+    default: return go(splitk_reduce_kernel<P, 1>);
   }
 }
 
-int launch_reduce(const float* ws, float* C, int64_t M, int64_t N, int64_t ldw, int64_t ldc, int split,
-                  const DeviceInfo& d, cudaStream_t s) {
-  const int P = split >= 8 ? 8 : (split >= 4 ? 4 : (split >= 2 ? 2 : 1));
+int launch_reduce(const Reduce& r, const DeviceInfo& d, cudaStream_t s) {
+  const int P = r.split >= 8 ? 8 : (r.split >= 4 ? 4 : (r.split >= 2 ? 2 : 1));
   const int64_t G = 256 / P;
-  const int64_t groups = M * cdiv(N, 4);
-  const int64_t resident = int64_t(d.sms) * 8;  // 256-thread blocks resident at once
+  const int64_t groups = r.M * cdiv(r.N, 4);                       // per batch
+  const int64_t resident = int64_t(d.sms) * 8 / r.batches + 1;       // 256-thread blocks per batch at once
   const int U = groups <= resident * G ? 1 : (groups <= 2 * resident * G ? 2 : 4);
   int64_t blocks = cdiv(groups, G * U);
   if (blocks > resident) blocks = resident;
   if (blocks < 1) blocks = 1;
-  const int vec_out = aligned16(C) && (ldc % 4 == 0);
-  const dim3 grid(static_cast<unsigned>(blocks));
-  const int64_t slab = M * ldw;
+  const int vec_out = aligned16(r.C) && (r.ldc % 4 == 0) && (r.batches == 1 || r.stride_c % 4 == 0);
+  const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(r.batches));
   switch (P) {
-    case 8: return launch_reduce_p<8>(U, grid, ws, C, M, N, ldw, ldc, slab, split, vec_out, s);
-    case 4: return launch_reduce_p<4>(U, grid, ws, C, M, N, ldw, ldc, slab, split, vec_out, s);
-    case 2: return launch_reduce_p<2>(U, grid, ws, C, M, N, ldw, ldc, slab, split, vec_out, s);
-    default: return launch_reduce_p<1>(U, grid, ws, C, M, N, ldw, ldc, slab, split, vec_out, s);
+    case 8: return launch_reduce_p<8>(U, grid, r, vec_out, s);
+    case 4: return launch_reduce_p<4>(U, grid, r, vec_out, s);
+    case 2: return launch_reduce_p<2>(U, grid, r, vec_out, s);
+    default: return launch_reduce_p<1>(U, grid, r, vec_out, s);
   }
 }
 
@@ -590,28 +659,218 @@ __global__ void __launch_bounds__(32) selftest_wait_kernel(unsigned long long li
   __syncwarp();
 }
 
-int launch_fill_zero(float* C, int64_t M, int64_t N, int64_t ldc, const DeviceInfo& d, cudaStream_t s) {
-  int64_t blocks = cdiv(M * N, 256);
+int launch_fill_zero(float* C, int64_t M, int64_t N, int64_t ldc, int64_t batches, int64_t stride_c,
+                     const float* bias, int act, const DeviceInfo& d, cudaStream_t s) {
+  int64_t blocks = cdiv(M * N * batches, 256);
   if (blocks > int64_t(d.sms) * 8) blocks = int64_t(d.sms) * 8;
-  return launch_k(fill_zero_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, 1, C, M, N, ldc);
+  if (blocks < 1) blocks = 1;
+  return launch_k(fill_zero_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, 1, C, M, N, ldc, batches,
+                  stride_c, bias, act);
 }
 
-int launch_simt(int bn, bool vec, dim3 grid, const float* A, const float* B, float* out, int64_t M, int64_t N,
-                int64_t K, int64_t lda, int64_t ldb, int64_t ldo, int64_t slab, int64_t k_chunk, int vec_out,
-                cudaStream_t s) {
+// grid: (M tiles, N tiles, batches * L.split).  A / B advance by stride_a / stride_b per
+// batch (0 = shared).
+int launch_simt(int bn, bool vec, dim3 grid, const float* A, const float* B, int64_t M, int64_t N, int64_t K,
+                int64_t lda, int64_t ldb, int64_t stride_a, int64_t stride_b, const Launch& L, cudaStream_t s) {
   // Launched without programmatic serialisation: a SIMT CTA fits twice on an SM, and CTAs
   // placed while the previous kernel still occupies the GPU were measured to double up on
   // some SMs (a 128-CTA grid ran 40% slower).
   const dim3 block(kSimtThreads);
   auto go = [&](auto kern, size_t smem) {
-    return launch_kx(false, kern, grid, block, smem, s, 1, A, B, out, M, N, K, lda, ldb, ldo, slab, k_chunk,
-                     vec_out);
+    return launch_kx(false, kern, grid, block, smem, s, 1, A, B, L.out, M, N, K, lda, ldb, L.ldo, L.out_slab,
+                     L.k_chunk, L.vec_out, L.split, stride_a, stride_b, L.out_batch, L.bias, L.act);
   };
   if (bn == 64)
     return vec ? go(simt_gemm_kernel<64, true>, simt_smem_bytes<64>())
                : go(simt_gemm_kernel<64, false>, simt_smem_bytes<64>());
   return vec ? go(simt_gemm_kernel<128, true>, simt_smem_bytes<128>())
              : go(simt_gemm_kernel<128, false>, simt_smem_bytes<128>());
+}
+
+constexpr int64_t kMaxBatch = 65535;  // grid y / z limit; larger batches run in chunks
+
+// One launch sequence for a batch chunk (batch <= kMaxBatch): packing / transposition
+// into the workspace when needed, the GEMM, and the split-K reduction.
+int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, void* workspace, size_t ws_bytes,
+              cudaStream_t s) {
+  Plan p;
+  int rc = make_plan(d, q, cfg, &p);
+  if (rc) return rc;
+  if (p.ws_bytes > 0) {
+    if (!workspace || ws_bytes < p.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+      return TILEC_ERR_WORKSPACE;
+  }
+  uint8_t* wsb = static_cast<uint8_t*>(workspace);
+  const int64_t M = q.M, N = q.N, K = q.K, nb = q.batch;
+  const float* A = q.A;
+  const float* B = q.B;
+  int64_t lda = q.lda, ldb = q.ldb, sa = p.a_shared ? 0 : q.stride_a, sb = p.b_shared ? 0 : q.stride_b;
+  const bool ta = (p.flags & TILEC_MM_TRANS_A) != 0, tb = (p.flags & TILEC_MM_TRANS_B) != 0;
+  // Stored shapes: A is M x K (K x M when transposed), B is K x N (N x K when transposed).
+  const int64_t a_rows = ta ? K : M, a_cols = ta ? M : K;
+  const int64_t b_rows = tb ? N : K, b_cols = tb ? K : N;
+  const int64_t na = p.a_shared ? 1 : nb, nbb = p.b_shared ? 1 : nb;
+  if (p.pack_a || p.tpose_a) {
+    float* pa = reinterpret_cast<float*>(wsb + p.off_a);
+    if (p.pack_a) {
+      const int64_t ld = round_up(a_cols, 4);
+      rc = launch_pack(A, lda, sa, pa, ld, a_rows, a_cols, na, d, s);
+      lda = ld;
+      sa = p.a_shared ? 0 : a_rows * ld;
+    } else {
+      const int64_t ld = round_up(K, 4);
+      rc = launch_transpose(A, lda, sa, pa, ld, K, M, na, d, s);
+      lda = ld;
+      sa = p.a_shared ? 0 : M * ld;
+    }
+    if (rc) return rc;
+    A = pa;
+  }
+  if (p.pack_b || p.tpose_b) {
+    float* pb = reinterpret_cast<float*>(wsb + p.off_b);
+    if (p.pack_b) {
+      const int64_t ld = round_up(b_cols, 4);
+      rc = launch_pack(B, ldb, sb, pb, ld, b_rows, b_cols, nbb, d, s);
+      ldb = ld;
+      sb = p.b_shared ? 0 : b_rows * ld;
+    } else {
+      const int64_t ld = round_up(N, 4);
+      rc = launch_transpose(B, ldb, sb, pb, ld, N, K, nbb, d, s);
+      ldb = ld;
+      sb = p.b_shared ? 0 : K * ld;
+    }
+    if (rc) return rc;
+    B = pb;
+  }
+  // The tensor-core kernels read either storage order in place; SIMT operands are now
+  // row-major.
+  const bool simt = p.variant == TILEC_MM_SIMT || p.variant == TILEC_MM_SPLITK;
+  float* slabs = reinterpret_cast<float*>(wsb + p.off_slabs);
+  Launch L;
+  L.layout = simt ? 0 : p.flags;
+  L.batch = static_cast<int>(nb);
+  L.shared = (p.a_shared ? 1 : 0) | (p.b_shared ? 2 : 0);
+  L.split = p.split;
+  L.k_chunk = p.k_chunk;
+  if (p.split > 1) {  // partial sums to the slabs; the reduction applies the epilogue
+    L.out = slabs;
+    L.ldo = p.ldw;
+    L.out_slab = M * p.ldw;
+    L.out_batch = int64_t(p.split) * M * p.ldw;
+    L.vec_out = 1;
+  } else {
+    L.out = q.C;
+    L.ldo = q.ldc;
+    L.out_batch = q.stride_c;
+    L.vec_out = aligned16(q.C) && (q.ldc % 4 == 0) && (nb == 1 || q.stride_c % 4 == 0) ? 1 : 0;
+    L.bias = q.bias;
+    L.act = p.act;
+  }
+
+  if (simt) {
+    const bool vec = aligned16(A) && aligned16(B) && (lda % 4 == 0) && (ldb % 4 == 0) && (sa % 4 == 0) &&
+                     (sb % 4 == 0);
+    const int64_t mt = cdiv(M, kSimtBM), nt = cdiv(N, p.bn);
+    if (nt > 65535 || nb * p.split > 65535) return TILEC_ERR_UNSUPPORTED;
+    const dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(nb * p.split));
+    rc = launch_simt(p.bn, vec, grid, A, B, M, N, K, lda, ldb, sa, sb, L, s);
+  } else {
+    CUtensorMap ma, mb;
+    const int bk = p.variant == TILEC_MM_TF32 ? 32 : (p.pair ? 16 : k3xBK);
+    rc = encode_maps(A, B, M, N, K, lda, ldb, sa, na, sb, nbb, bk, L.layout, p.pair ? 128 : p.bn, &ma, &mb);
+    if (rc) return rc;
+    if (p.pair)
+      rc = p.variant == TILEC_MM_3XTF32 ? launch_tc2<false>(ma, mb, M, N, K, L, s)
+                                        : launch_tc2<true>(ma, mb, M, N, K, L, s);
+    else if (p.variant == TILEC_MM_TF32)
+      rc = dispatch_tc_bn<false, false>(p.bn, ma, mb, M, N, K, L, s);
+    else if (p.variant == TILEC_MM_3XTF32)
+      rc = dispatch_tc_bn<true, false>(p.bn, ma, mb, M, N, K, L, s);
+    else
+      rc = dispatch_tc_bn<true, true>(p.bn, ma, mb, M, N, K, L, s);
+  }
+  if (rc) return rc;
+  if (p.split > 1) {
+    Reduce r;
+    r.ws = slabs;
+    r.C = q.C;
+    r.M = M;
+    r.N = N;
+    r.ldw = p.ldw;
+    r.ldc = q.ldc;
+    r.batches = nb;
+    r.stride_c = q.stride_c;
+    r.split = p.split;
+    r.act = p.act;
+    r.bias = q.bias;
+    rc = launch_reduce(r, d, s);
+  }
+  return rc;
+}
+
+int run_problem(const Problem& q, const tilec_mm_cfg* cfg, void* workspace, size_t ws_bytes, void* stream) {
+  int rc = check_problem(q, true, cfg ? cfg->flags : 0);
+  if (rc) return rc;
+  if (q.M == 0 || q.N == 0 || q.batch == 0) return TILEC_OK;
+  DeviceInfo* d = nullptr;
+  rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (q.K == 0) {
+    const int act = cfg ? cfg->activation : 0;
+    if (act < TILEC_MM_ACT_NONE || act > TILEC_MM_ACT_GELU) return TILEC_ERR_BAD_ARG;
+    return launch_fill_zero(q.C, q.M, q.N, q.ldc, q.batch, q.stride_c, q.bias, act, *d, s);
+  }
+  for (int64_t b0 = 0; b0 < q.batch; b0 += kMaxBatch) {
+    Problem c = q;
+    c.batch = q.batch - b0 < kMaxBatch ? q.batch - b0 : kMaxBatch;
+    c.A = q.A + b0 * q.stride_a;
+    c.B = q.B + b0 * q.stride_b;
+    c.C = q.C + b0 * q.stride_c;
+    rc = run_chunk(*d, c, cfg, workspace, ws_bytes, s);
+    if (rc) return rc;
+  }
+  return TILEC_OK;
+}
+
+size_t workspace_for(Problem q, const tilec_mm_cfg* cfg) {
+  if (q.M <= 0 || q.N <= 0 || q.K <= 0 || q.batch <= 0) return 0;
+  DeviceInfo* d = nullptr;
+  if (current_device(&d)) return 0;
+  // NULL operands: assume 16-byte aligned pointers (documented in the header).
+  if (!q.A) q.A = reinterpret_cast<const float*>(uintptr_t(256));
+  if (!q.B) q.B = reinterpret_cast<const float*>(uintptr_t(256));
+  if (q.batch > kMaxBatch) q.batch = kMaxBatch;  // batches run in chunks of this size
+  Plan p;
+  if (make_plan(*d, q, cfg, &p)) return 0;
+  return p.ws_bytes;
+}
+
+Problem single(const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+               int64_t ldb, int64_t ldc) {
+  Problem q;
+  q.A = A;
+  q.B = B;
+  q.C = const_cast<float*>(C);
+  q.M = M;
+  q.N = N;
+  q.K = K;
+  q.lda = lda;
+  q.ldb = ldb;
+  q.ldc = ldc;
+  return q;
+}
+
+Problem batched(const float* A, const float* B, const float* C, const float* bias, int64_t M, int64_t N, int64_t K,
+                int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t stride_a, int64_t stride_b,
+                int64_t stride_c) {
+  Problem q = single(A, B, C, M, N, K, lda, ldb, ldc);
+  q.bias = bias;
+  q.batch = batch;
+  q.stride_a = stride_a;
+  q.stride_b = stride_b;
+  q.stride_c = stride_c;
+  return q;
 }
 
 }  // namespace
@@ -624,120 +883,45 @@ extern "C" {
 int tilec_mm_plan(const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                   int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg, tilec_mm_cfg* out) {
   if (!out) return TILEC_ERR_BAD_ARG;
-  int rc = check_args(A, B, C, M, N, K, lda, ldb, ldc, /*need_c=*/false, cfg ? cfg->flags : 0);
+  const Problem q = single(A, B, C, M, N, K, lda, ldb, ldc);
+  int rc = check_problem(q, /*need_c=*/false, cfg ? cfg->flags : 0);
   if (rc) return rc;
   DeviceInfo* d = nullptr;
   rc = current_device(&d);
   if (rc) return rc;
   Plan p;
-  rc = make_plan(*d, A, B, C, M, N, K, lda, ldb, ldc, cfg, &p);
+  rc = make_plan(*d, q, cfg, &p);
   if (rc) return rc;
   std::memset(out, 0, sizeof(*out));
   out->variant = p.variant;
   out->split_k = p.split;
   out->flags = p.flags;
+  out->activation = p.act;
   return TILEC_OK;
 }
 
 size_t tilec_mm_workspace_bytes(const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K,
                                 int64_t lda, int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg) {
-  if (M <= 0 || N <= 0 || K <= 0) return 0;
-  DeviceInfo* d = nullptr;
-  if (current_device(&d)) return 0;
-  // NULL operands: assume 16-byte aligned pointers (documented in the header).
-  const float* a = A ? A : reinterpret_cast<const float*>(uintptr_t(256));
-  const float* b = B ? B : reinterpret_cast<const float*>(uintptr_t(256));
-  Plan p;
-  if (make_plan(*d, a, b, C, M, N, K, lda, ldb, ldc, cfg, &p)) return 0;
-  return p.ws_bytes;
+  return workspace_for(single(A, B, C, M, N, K, lda, ldb, ldc), cfg);
+}
+
+size_t tilec_mm_workspace_bytes_ex(const float* A, const float* B, const float* C, int64_t M, int64_t N, int64_t K,
+                                   int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t stride_a,
+                                   int64_t stride_b, int64_t stride_c, const tilec_mm_cfg* cfg) {
+  return workspace_for(batched(A, B, C, nullptr, M, N, K, lda, ldb, ldc, batch, stride_a, stride_b, stride_c), cfg);
 }
 
 int tilec_mm_f32(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                  int64_t ldb, int64_t ldc, const tilec_mm_cfg* cfg, void* workspace, size_t ws_bytes,
                  void* stream) {
-  int rc = check_args(A, B, C, M, N, K, lda, ldb, ldc, true, cfg ? cfg->flags : 0);
-  if (rc) return rc;
-  if (M == 0 || N == 0) return TILEC_OK;
-  DeviceInfo* d = nullptr;
-  rc = current_device(&d);
-  if (rc) return rc;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return run_problem(single(A, B, C, M, N, K, lda, ldb, ldc), cfg, workspace, ws_bytes, stream);
+}
 
-  if (K == 0) return launch_fill_zero(C, M, N, ldc, *d, s);
-
-  Plan p;
-  rc = make_plan(*d, A, B, C, M, N, K, lda, ldb, ldc, cfg, &p);
-  if (rc) return rc;
-  if (p.ws_bytes > 0) {
-    if (!workspace || ws_bytes < p.ws_bytes || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
-      return TILEC_ERR_WORKSPACE;
-  }
-  uint8_t* wsb = static_cast<uint8_t*>(workspace);
-  const bool ta = (p.flags & TILEC_MM_TRANS_A) != 0, tb = (p.flags & TILEC_MM_TRANS_B) != 0;
-  // Stored shapes: A is M x K (K x M when transposed), B is K x N (N x K when transposed).
-  const int64_t a_rows = ta ? K : M, a_cols = ta ? M : K;
-  const int64_t b_rows = tb ? N : K, b_cols = tb ? K : N;
-  if (p.pack_a || p.tpose_a) {
-    float* pa = reinterpret_cast<float*>(wsb + p.off_a);
-    if (p.pack_a) {
-      rc = launch_pack(A, lda, pa, round_up(a_cols, 4), a_rows, a_cols, *d, s);
-      lda = round_up(a_cols, 4);
-    } else {
-      rc = launch_transpose(A, lda, pa, round_up(K, 4), K, M, *d, s);
-      lda = round_up(K, 4);
-    }
-    if (rc) return rc;
-    A = pa;
-  }
-  if (p.pack_b || p.tpose_b) {
-    float* pb = reinterpret_cast<float*>(wsb + p.off_b);
-    if (p.pack_b) {
-      rc = launch_pack(B, ldb, pb, round_up(b_cols, 4), b_rows, b_cols, *d, s);
-      ldb = round_up(b_cols, 4);
-    } else {
-      rc = launch_transpose(B, ldb, pb, round_up(N, 4), N, K, *d, s);
-      ldb = round_up(N, 4);
-    }
-    if (rc) return rc;
-    B = pb;
-  }
-  // The tensor-core kernels read either storage order in place; SIMT operands are now
-  // row-major.
-  const bool simt = p.variant == TILEC_MM_SIMT || p.variant == TILEC_MM_SPLITK;
-  const int layout = simt ? 0 : p.flags;
-  float* slabs = reinterpret_cast<float*>(wsb + p.off_slabs);
-  float* out = p.split > 1 ? slabs : C;
-  const int64_t ldo = p.split > 1 ? p.ldw : ldc;
-  const int64_t slab = p.split > 1 ? M * p.ldw : 0;
-  const int vec_out = p.split > 1 ? 1 : (aligned16(C) && (ldc % 4 == 0) ? 1 : 0);
-
-  if (simt) {
-    const bool vec = aligned16(A) && aligned16(B) && (lda % 4 == 0) && (ldb % 4 == 0);
-    const int64_t mt = cdiv(M, kSimtBM), nt = cdiv(N, p.bn);
-    if (nt > 65535) return TILEC_ERR_UNSUPPORTED;
-    dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(p.split));
-    rc = launch_simt(p.bn, vec, grid, A, B, out, M, N, K, lda, ldb, ldo, slab, p.k_chunk, vec_out, s);
-  } else {
-    CUtensorMap ma, mb;
-    const int bk = p.variant == TILEC_MM_TF32 ? 32 : (p.pair ? 16 : k3xBK);
-    rc = encode_maps(A, B, M, N, K, lda, ldb, bk, layout, p.pair ? 128 : p.bn, &ma, &mb);
-    if (rc) return rc;
-    if (p.pair)
-      rc = p.variant == TILEC_MM_3XTF32
-               ? launch_tc2<false>(ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, layout, s)
-               : launch_tc2<true>(ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, layout, s);
-    else if (p.variant == TILEC_MM_TF32)
-      rc = dispatch_tc_bn<false, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, layout,
-                                        s);
-    else if (p.variant == TILEC_MM_3XTF32)
-      rc = dispatch_tc_bn<true, false>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, layout,
-                                       s);
-    else
-      rc = dispatch_tc_bn<true, true>(p.bn, ma, mb, out, M, N, ldo, slab, K, p.k_chunk, p.split, vec_out, layout, s);
-  }
-  if (rc) return rc;
-  if (p.split > 1) rc = launch_reduce(slabs, C, M, N, p.ldw, ldc, p.split, *d, s);
-  return rc;
+int tilec_mm_f32_ex(const float* A, const float* B, float* C, const float* bias, int64_t M, int64_t N, int64_t K,
+                    int64_t lda, int64_t ldb, int64_t ldc, int64_t batch, int64_t stride_a, int64_t stride_b,
+                    int64_t stride_c, const tilec_mm_cfg* cfg, void* workspace, size_t ws_bytes, void* stream) {
+  return run_problem(batched(A, B, C, bias, M, N, K, lda, ldb, ldc, batch, stride_a, stride_b, stride_c), cfg,
+                     workspace, ws_bytes, stream);
 }
 
 int tilec_mm_set_table(const int32_t* rows, int32_t nrows) {
@@ -840,7 +1024,7 @@ extern "C" int tilec_mm_f32_splitk_noalloc(const float* A, const float* B, float
   rc = current_device(&d);
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (K == 0) return launch_fill_zero(C, M, N, ldc, *d, s);
+  if (K == 0) return launch_fill_zero(C, M, N, ldc, 1, 0, nullptr, TILEC_MM_ACT_NONE, *d, s);
   float* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;
@@ -864,13 +1048,24 @@ extern "C" int tilec_mm_f32_splitk_noalloc(const float* A, const float* B, float
   const int64_t k_chunk = round_up(cdiv(K, split), kSimtBK);
   split = cdiv(K, k_chunk);
 
-  float* out = split > 1 ? scratch : C;
-  const int64_t ldo = split > 1 ? ldw : ldc;
-  const int64_t out_slab = split > 1 ? slab : 0;
-  const int vec_out = split > 1 ? 1 : (aligned16(C) && (ldc % 4 == 0) ? 1 : 0);
+  Launch L;
+  L.out = split > 1 ? scratch : C;
+  L.ldo = split > 1 ? ldw : ldc;
+  L.out_slab = split > 1 ? slab : 0;
+  L.vec_out = split > 1 ? 1 : (aligned16(C) && (ldc % 4 == 0) ? 1 : 0);
+  L.split = static_cast<int>(split);
+  L.k_chunk = k_chunk;
   const bool vec = aligned16(A) && aligned16(B) && (lda % 4 == 0) && (ldb % 4 == 0);
   dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(split));
-  rc = launch_simt(bn, vec, grid, A, B, out, M, N, K, lda, ldb, ldo, out_slab, k_chunk, vec_out, s);
+  rc = launch_simt(bn, vec, grid, A, B, M, N, K, lda, ldb, 0, 0, L, s);
   if (rc || split == 1) return rc;
-  return launch_reduce(scratch, C, M, N, ldw, ldc, static_cast<int>(split), *d, s);
+  Reduce r;
+  r.ws = scratch;
+  r.C = C;
+  r.M = M;
+  r.N = N;
+  r.ldw = ldw;
+  r.ldc = ldc;
+  r.split = static_cast<int>(split);
+  return launch_reduce(r, *d, s);
 }

@@ -151,6 +151,85 @@ def matrix_mul(x1, x2):
     return _matrix_mul(x1, x2)
 
 
+def _batched_operand(x):
+    """(tensor, leading stride, transposed, batch stride, batch count or None) for a 2-D
+    operand or a 3-D batch of them whose slices are all row views or all column views
+    (copied to contiguous otherwise)."""
+    if x.dim() == 2:
+        t, ld, trans = _operand(x)
+        return t, ld, trans, 0, None
+    if x.dim() != 3:
+        raise ValueError(f"matrix_mul_ex: operands must be 2-D or 3-D, got shape {tuple(x.shape)}")
+    nb, r, c = x.shape
+    sb, sr, sc = x.stride()
+    if (c <= 1 or sc == 1) and (r <= 1 or sr >= max(c, 1)):
+        return x, (sr if r > 1 else max(c, 1)), False, sb, nb
+    if sr == 1 and sc >= r:
+        return x, sc, True, sb, nb
+    x = x.contiguous()
+    return x, max(c, 1), False, r * c, nb
+
+
+def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, split_k=0):
+    """act(x1 @ x2 + bias), batched: the fused, batched form of matrix_mul.
+
+    x1 [M, K] or [B, M, K]; x2 [K, N] or [B, K, N] (a 2-D operand is shared by every
+    product of the batch); bias: None or a float32 [N] tensor added per column;
+    activation: None, "relu" or "gelu" (exact erf form).  Returns (or writes into `out`)
+    [M, N] or [B, M, N].  One library call (tilec_mm_f32_ex): the batch is a grid dimension
+    of the kernels and the epilogue runs where C is stored.  Row views and column views
+    (.t() / .transpose(-1, -2)) of each slice are read in place, as in matrix_mul.
+    """
+    _check_operand(x1)
+    _check_operand(x2)
+    if x1.device.type != "cuda" or x2.device.type != "cuda" or x1.device != x2.device:
+        raise ValueError(f"matrix_mul_ex: inputs must be CUDA tensors on one device (got {x1.device} and {x2.device})")
+    M, K = x1.shape[-2:]
+    K2, N = x2.shape[-2:]
+    if K != K2:
+        raise ValueError(f"matrix_mul: shapes {tuple(x1.shape)} and {tuple(x2.shape)} don't match")
+    a, lda, ta, sa, na = _batched_operand(x1)
+    b, ldb, tb, sb, nbb = _batched_operand(x2)
+    if na is not None and nbb is not None and na != nbb:
+        raise ValueError(f"matrix_mul_ex: batch sizes {na} and {nbb} don't match")
+    nb = na if na is not None else nbb
+    if activation not in _native.ACTIVATIONS:
+        raise ValueError(f"matrix_mul_ex: unknown activation {activation!r}; expected None, 'relu' or 'gelu'")
+    if bias is not None:
+        if bias.dtype != torch.float32 or bias.dim() != 1 or bias.shape[0] != N or bias.device != x1.device:
+            raise ValueError(f"matrix_mul_ex: bias must be a float32 [{N}] tensor on {x1.device}")
+        bias = bias.contiguous()
+    shape = (M, N) if nb is None else (nb, M, N)
+    if out is None:
+        out = x1.new_empty(shape)
+    elif tuple(out.shape) != shape or out.dtype != torch.float32 or out.device != x1.device:
+        raise ValueError(f"matrix_mul_ex: out must be a float32 {shape} tensor on {x1.device}")
+    c2 = out if nb is None else out[0]
+    ldc = _check_out(c2, M, N, x1.device) if M * N else max(N, 1)
+    sc = 0 if nb is None else out.stride(0)
+    if M == 0 or N == 0 or nb == 0:
+        return out
+    nbatch = 1 if nb is None else nb
+    if nbatch > 1 and sc < (M - 1) * ldc + N:
+        raise ValueError("matrix_mul_ex: the batches of out overlap")
+    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0)
+    lib = _native.load()
+    from . import select
+    select.ensure_installed()
+    cfg = _native.make_cfg(variant or _default_variant(), split_k, flags, _native.ACTIVATIONS[activation])
+    pa, pb, pc = a.data_ptr(), b.data_ptr(), out.data_ptr()
+    dev = out.device
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        ws_bytes = lib.tilec_mm_workspace_bytes_ex(pa, pb, pc, M, N, K, lda, ldb, ldc, nbatch, sa, sb, sc,
+                                                   ctypes.byref(cfg))
+        ws_ptr = _workspace(dev, stream, ws_bytes).data_ptr() if ws_bytes else None
+        rc = lib.tilec_mm_f32_ex(pa, pb, pc, bias.data_ptr() if bias is not None else None, M, N, K, lda, ldb, ldc,
+                                 nbatch, sa, sb, sc, ctypes.byref(cfg), ws_ptr, ws_bytes, stream)
+    _native.check(rc, "tilec_mm_f32_ex")
+    return out
+
+
 def plan(x1, x2, variant=None, split_k=0):
     """The (variant name, split_k) that matrix_mul would launch for these operands."""
     M, K = x1.shape
