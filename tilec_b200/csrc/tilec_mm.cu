@@ -230,14 +230,16 @@ void choose_auto(const DeviceInfo& d, const float* A, const float* B, int64_t M,
   *split = 0;
   const double flops = 2.0 * double(M) * double(N) * double(K) * double(batch);
   const bool aligned = tensor_path_ok(A, B, M, N, K, lda, ldb);
-  // Misaligned operands are packed first (2 x (MK + KN) x 4 bytes of traffic): worth it
-  // once the product is large enough for the tensor cores to win by a wide margin.
-  if (tensor_dims_ok(M, N, K) && flops >= (aligned ? 1.0e8 : 5.0e8)) {
+  // Thresholds from a 64-shape B200 sweep (log-uniform over [1, 8192]^3): below about
+  // 1e7 FLOPs every variant sits at the launch floor; misaligned operands are packed
+  // first, which pays from about 3e7.  Smaller products go to the SIMT kernel, split
+  // over K when their tiles leave SMs idle (the split rule picks 1 when it would not pay).
+  if (tensor_dims_ok(M, N, K) && flops >= (aligned ? 1.0e7 : 3.0e7)) {
     *variant = TILEC_MM_3XTF32;
     return;
   }
   const int64_t tiles = cdiv(M, kSimtBM) * cdiv(N, N <= 64 ? 64 : 128) * batch;
-  *variant = (tiles < d.sms && K >= 1024) ? TILEC_MM_SPLITK : TILEC_MM_SIMT;
+  *variant = tiles < d.sms ? TILEC_MM_SPLITK : TILEC_MM_SIMT;
 }
 
 // K slices for a grid of `tiles` output tiles: minimise (waves of CTAs) / slices, i.e. the

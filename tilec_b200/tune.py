@@ -105,7 +105,9 @@ def bench(n=64, path=DEFAULT_CSV, seed=4):
             w.writerow([dev, m, k, nn, "builtin", 0, f"{ms:.6f}"])
             cands = [("simt", 0), ("splitk", 0), ("3xtf32", 0), ("tf32", 0)] + ext.mm_configs(m, k, nn)
             for v, s in cands:
-                ms = time_ms(lambda: ext._matrix_mul(a, b, variant=v, split_k=s, out=c), best)
+                # Family rows (the library's own split) feed the fit, so they are always
+                # measured in full; explicit splits may stop early when far behind.
+                ms = time_ms(lambda: ext._matrix_mul(a, b, variant=v, split_k=s, out=c), None if s == 0 else best)
                 best = ms if best is None else min(best, ms)
                 w.writerow([dev, m, k, nn, v, s, f"{ms:.6f}"])
             f.flush()
@@ -131,16 +133,22 @@ def _best_family(rs):
     return min(rs, key=lambda r: r["ms"])["variant"]
 
 
-def fit(rows, k_nn=3):
-    """Selection table over a coarse log2 grid: each cell gets the variant family that is
-    fastest for most of the k_nn measured shapes nearest to the cell centre (log2 space);
-    the split count is left to the library (split_k = 0)."""
+def fit(rows, k_nn=3, margin=1.10):
+    """Selection rows over a coarse log2 grid, only where the measurements beat the
+    library's built-in rule: a cell gets the variant family that is fastest for the
+    majority of the k_nn measured shapes nearest to its centre (log2 space), provided
+    that family is at least `margin` times faster than the built-in choice on those
+    shapes (geometric mean).  Other cells get no row, so AUTO keeps its built-in rule
+    there.  The split count is left to the library (split_k = 0)."""
     by_shape = {}
-    for r in _family_rows(rows):
+    for r in rows:
         by_shape.setdefault((r["M"], r["K"], r["N"]), []).append(r)
     pts = []
     for (m, k, n), rs in by_shape.items():
-        pts.append(((math.log2(max(m, 1)), math.log2(max(n, 1)), math.log2(max(k, 1))), _best_family(rs)))
+        fam = {r["variant"]: r["ms"] for r in rs if r["variant"] in FP32_CLASS and r["split_k"] == 0}
+        builtin = next((r["ms"] for r in rs if r["variant"] == "builtin"), None)
+        if fam and builtin is not None:
+            pts.append(((math.log2(max(m, 1)), math.log2(max(n, 1)), math.log2(max(k, 1))), fam, builtin))
     if not pts:
         return []
     table = []
@@ -151,10 +159,15 @@ def fit(rows, k_nn=3):
                 c = tuple(min(e[x] + 1.0, 13.0) for x in (i, j, l))
                 near = sorted(pts, key=lambda p: sum((p[0][d] - c[d]) ** 2 for d in range(3)))[:k_nn]
                 votes = {}
-                for _, v in near:
-                    votes[v] = votes.get(v, 0) + 1
-                v = max(votes.items(), key=lambda kv: (kv[1], kv[0] == "3xtf32"))[0]
-                table.append([e[i], e[i + 1], e[j], e[j + 1], e[l], e[l + 1], v, 0])
+                for _, fam, _ in near:
+                    best = min(fam, key=fam.get)
+                    votes[best] = votes.get(best, 0) + 1
+                v, count = max(votes.items(), key=lambda kv: (kv[1], kv[0] == "3xtf32"))
+                if count <= len(near) // 2 or any(v not in fam for _, fam, _ in near):
+                    continue
+                gain = math.exp(sum(math.log(b / fam[v]) for _, fam, b in near) / len(near))
+                if gain >= margin:
+                    table.append([e[i], e[i + 1], e[j], e[j + 1], e[l], e[l + 1], v, 0])
     return table
 
 
@@ -174,11 +187,15 @@ def train(path=DEFAULT_CSV, out=None, test_frac=0.2, seed=0):
         rs = by_shape[key]
         best = min(r["ms"] for r in rs if r["variant"] in FP32_CLASS)
         pick = select.lookup([t[:6] + [_variant_code(t[6]), t[7]] for t in table], *_mnk(key))
-        chosen = next(r for r in rs if r["variant"] == pick[0] and r["split_k"] == 0)
         default = next(r for r in rs if r["variant"] == "builtin")
+        chosen = default if pick is None else next(r for r in rs if r["variant"] == pick[0] and r["split_k"] == 0)
         ratio_sel.append(chosen["ms"] / best)
         ratio_default.append(default["ms"] / best)
     gm = lambda v: math.exp(sum(math.log(a) for a in v) / max(len(v), 1))  # noqa: E731
+    cv = cross_validate(rows)
+    print(f"5-fold cross-validation over all {len(keys)} shapes: selector {cv['selector_x_of_best']:.3f}x of best "
+          f"(worst {cv['selector_worst']:.2f}x), built-in rules {cv['builtin_x_of_best']:.3f}x "
+          f"(worst {cv['builtin_worst']:.2f}x)")
     print(f"held-out shapes: {len(test)}")
     print(f"selector: {gm(ratio_sel):.3f}x of best (geo mean), worst {max(ratio_sel, default=1):.2f}x")
     print(f"default : {gm(ratio_default):.3f}x of best (geo mean), worst {max(ratio_default, default=1):.2f}x")
@@ -188,12 +205,50 @@ def train(path=DEFAULT_CSV, out=None, test_frac=0.2, seed=0):
            "heldout": {"shapes": len(test), "selector_x_of_best": round(gm(ratio_sel), 4),
                        "builtin_x_of_best": round(gm(ratio_default), 4),
                        "selector_worst": round(max(ratio_sel, default=1), 3),
-                       "builtin_worst": round(max(ratio_default, default=1), 3)}}
+                       "builtin_worst": round(max(ratio_default, default=1), 3)},
+           "cross_validation": cv}
     out = out or select.TABLE_PATH
     with open(out, "w") as f:
         json.dump(doc, f, indent=1)
     print("wrote", out)
     return doc
+
+
+def _choice_ms(rs, table):
+    """Time of what AUTO runs for one measured shape under `table` (the built-in rule's
+    time when no row matches)."""
+    from . import select
+    m, k, n = rs[0]["M"], rs[0]["K"], rs[0]["N"]
+    pick = select.lookup([t[:6] + [_variant_code(t[6]), t[7]] for t in table], m, n, k)
+    default = next(r for r in rs if r["variant"] == "builtin")
+    if pick is None:
+        return default["ms"]
+    return next(r for r in rs if r["variant"] == pick[0] and r["split_k"] == 0)["ms"]
+
+
+def cross_validate(rows, folds=5, seeds=(0, 1, 2)):
+    """k-fold estimate (averaged over shuffles) of the fitted selector and of the built-in
+    rules, as geometric-mean and worst "x of best" over every measured shape."""
+    by_shape = {}
+    for r in rows:
+        by_shape.setdefault((r["M"], r["K"], r["N"]), []).append(r)
+    keys0 = sorted(k for k, rs in by_shape.items() if any(r["variant"] == "builtin" for r in rs))
+    sel, dft = [], []
+    for seed in seeds:
+        keys = list(keys0)
+        random.Random(seed).shuffle(keys)
+        for f in range(folds):
+            test = set(keys[f::folds])
+            table = fit([r for r in rows if (r["M"], r["K"], r["N"]) not in test])
+            for key in test:
+                rs = by_shape[key]
+                best = min(r["ms"] for r in rs if r["variant"] in FP32_CLASS)
+                sel.append(_choice_ms(rs, table) / best)
+                dft.append(next(r for r in rs if r["variant"] == "builtin")["ms"] / best)
+    gm = lambda v: math.exp(sum(math.log(a) for a in v) / max(len(v), 1))  # noqa: E731
+    return {"folds": folds, "shuffles": len(seeds), "selector_x_of_best": round(gm(sel), 4),
+            "builtin_x_of_best": round(gm(dft), 4), "selector_worst": round(max(sel, default=1), 3),
+            "builtin_worst": round(max(dft, default=1), 3)}
 
 
 def _variant_code(v):
