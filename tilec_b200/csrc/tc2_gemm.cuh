@@ -62,12 +62,14 @@ struct Tc2Cfg {
 
 // M = 256 (pair), N = BN, kind::tf32; A K-major and B MN-major unless `layout` flips
 // them (kOpAMN / kOpBK, operands stored transposed).
-template <int BN, int STAGES, bool HI_EXPLICIT>
+// ANY_LAYOUT as in tc_gemm_kernel.
+template <int BN, int STAGES, bool HI_EXPLICIT, bool ANY_LAYOUT>
 __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
     tc2_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     float* __restrict__ out, int M, int N, int64_t ldo, int64_t out_slab, int K, int k_chunk,
-                    int mp_tiles, int n_tiles, int group_m, int vec_out, int layout, int64_t out_batch,
+                    int mp_tiles, int n_tiles, int group_m, int vec_out, int layout_arg, int64_t out_batch,
                     const float* __restrict__ bias, int act, int shared) {
+  const int layout = ANY_LAYOUT ? layout_arg : 0;
   using Cfg = Tc2Cfg<BN, STAGES>;
   constexpr int BK = Cfg::BK;
   constexpr int KC = Cfg::kChunkBlocks;

@@ -58,7 +58,10 @@ std::vector<int32_t> g_table;  // rows of 8 int32
 template <int BN, int BK, int STAGES, bool SPLIT3, bool HI>
 cudaError_t set_tc_attr() {
   using Cfg = TcCfg<BN, BK, STAGES, SPLIT3>;
-  return cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI>,
+  const cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, false>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, true>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
 }
 
@@ -108,10 +111,14 @@ cudaError_t init_device_attrs() {
   acc(set_tc_attr<256, k3xBK, TcShape<256>::k3xStages, true, false>());
   acc(set_tc_attr<128, k3xBK, TcShape<128>::k3xStages, true, false>());
   acc(set_tc_attr<64, k3xBK, TcShape<64>::k3xStages, true, false>());
-  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           Tc2Cfg<256, kPairStages>::kSmemBytes));
-  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           Tc2Cfg<256, kPairStages>::kSmemBytes));
+  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, false, false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, Tc2Cfg<256, kPairStages>::kSmemBytes));
+  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, true, false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, Tc2Cfg<256, kPairStages>::kSmemBytes));
+  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, false, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, Tc2Cfg<256, kPairStages>::kSmemBytes));
+  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, true, true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, Tc2Cfg<256, kPairStages>::kSmemBytes));
   return e;
 }
 
@@ -496,10 +503,13 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N
   const int group_m = 16;
   const dim3 grid(static_cast<unsigned>(int64_t(m_tiles) * n_tiles), static_cast<unsigned>(L.batch),
                   static_cast<unsigned>(L.split));
-  return launch_k(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 1, ma,
-                  mb, L.out, static_cast<int>(M), static_cast<int>(N), L.ldo, L.out_slab, static_cast<int>(K),
-                  static_cast<int>(L.k_chunk), m_tiles, n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias,
-                  L.act, L.shared);
+  auto go = [&](auto kern) {
+    return launch_k(kern, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 1, ma, mb, L.out, static_cast<int>(M),
+                    static_cast<int>(N), L.ldo, L.out_slab, static_cast<int>(K), static_cast<int>(L.k_chunk), m_tiles,
+                    n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias, L.act, L.shared);
+  };
+  return L.layout ? go(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, true>)
+                  : go(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, false>);
 }
 
 template <int BN, bool SPLIT3, bool HI>
@@ -520,10 +530,12 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t 
   const int group_m = 8;
   const dim3 grid(static_cast<unsigned>(2 * int64_t(mp_tiles) * n_tiles), static_cast<unsigned>(L.batch),
                   static_cast<unsigned>(L.split));
-  return launch_k(tc2_gemm_kernel<256, kPairStages, HI>, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 2, ma, mb,
-                  L.out, static_cast<int>(M), static_cast<int>(N), L.ldo, L.out_slab, static_cast<int>(K),
-                  static_cast<int>(L.k_chunk), mp_tiles, n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias,
-                  L.act, L.shared);
+  auto go = [&](auto kern) {
+    return launch_k(kern, grid, dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 2, ma, mb, L.out, static_cast<int>(M),
+                    static_cast<int>(N), L.ldo, L.out_slab, static_cast<int>(K), static_cast<int>(L.k_chunk),
+                    mp_tiles, n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias, L.act, L.shared);
+  };
+  return L.layout ? go(tc2_gemm_kernel<256, kPairStages, HI, true>) : go(tc2_gemm_kernel<256, kPairStages, HI, false>);
 }
 
 template <bool SPLIT3, bool HI>
