@@ -225,11 +225,8 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
   return out;
 }
-// Arrive on an mbarrier given by a shared::cluster address (own or peer CTA), release at cluster scope.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-// Same, release at CTA scope (orders this thread's prior operations for its own CTA only).
+// Arrive on an mbarrier given by a shared::cluster address (own or peer CTA), release at
+// CTA scope (orders this thread's prior operations for its own CTA only).
 __device__ __forceinline__ void mbar_arrive_remote_cta(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }

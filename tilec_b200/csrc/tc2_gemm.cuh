@@ -25,16 +25,13 @@
 #include "common.cuh"
 #include "tc_gemm.cuh"
 
-// How the split warps and the epilogue warps signal the leader CTA:
-//   1 (default) remote mbarrier arrive with release at CTA scope, after
-//     fence.proxy.async.shared::cta has made the warp's shared-memory writes visible to the
-//     async proxy (the tensor core reads them only after the leader observes the arrive);
-//   0 the same arrive with release at cluster scope (a cluster memory barrier per warp and
-//     stage: measured 147 vs 245 TFLOP/s at 8192^3);
-//   2 eight local arrives, then one cluster-scope release per stage (139 TFLOP/s).
-#ifndef TILEC_PAIR_SIGNAL
-#define TILEC_PAIR_SIGNAL 1
-#endif
+// The split warps and the epilogue warps signal the leader CTA with a remote mbarrier
+// arrive whose release is at CTA scope, after fence.proxy.async.shared::cta has made the
+// warp's shared-memory writes visible to the async proxy (the tensor core reads them only
+// after the leader observes the arrive).  Measured alternatives, slower on B200: the same
+// arrive with a cluster-scope release (a cluster memory barrier per warp and stage: 147
+// vs 245 TFLOP/s at 8192^3), and eight local arrives followed by one cluster-scope release
+// per stage (139 TFLOP/s).
 
 namespace tilec {
 
@@ -88,8 +85,7 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
   uint64_t* chunk_full = split + STAGES;
   uint64_t* chunk_empty = chunk_full + 2;
   uint64_t* drain_bar = chunk_empty + 2;
-  uint64_t* split_local = drain_bar + 1;   // [STAGES] split warps of this CTA -> publishing warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(split_local + STAGES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -125,14 +121,13 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&split[s], TILEC_PAIR_SIGNAL == 2 ? 2 : 2 * Cfg::kEpiWarps);
+      mbar_init(&split[s], 2 * Cfg::kEpiWarps);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&chunk_full[b], 1);
       mbar_init(&chunk_empty[b], 2 * Cfg::kEpiWarps);
     }
     mbar_init(drain_bar, 1);
-    for (int st = 0; st < STAGES; ++st) mbar_init(&split_local[st], Cfg::kEpiWarps);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -268,11 +263,7 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-#if TILEC_PAIR_SIGNAL == 0
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&chunk_empty[buf]), 0));
-#else
       if (lane == 0) mbar_arrive_remote_cta(mapa_shared(smem_u32(&chunk_empty[buf]), 0));
-#endif
       return true;
     };
 
@@ -301,22 +292,8 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
         if constexpr (HI_EXPLICIT) src_b[i] = hv;
       }
       fence_proxy_async_smem();
-#if TILEC_PAIR_SIGNAL == 2
-      // Each split warp reports to a local barrier; one of them (rotating with the stage)
-      // waits for all eight and publishes the stage to the leader with one cluster release.
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&split_local[s]);
-      if (e == (kb % Cfg::kEpiWarps)) {
-        if (!mbar_wait(&split_local[s], ph, abort_flag)) { ok = false; break; }
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&split[s]), 0));
-      }
-#elif TILEC_PAIR_SIGNAL == 1
       __syncwarp();
       if (lane == 0) mbar_arrive_remote_cta(mapa_shared(smem_u32(&split[s]), 0));
-#else
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&split[s]), 0));
-#endif
       if (kb % KC == (kLag < KC ? kLag : KC - 1) && kb / KC >= 1 && drained < kb / KC) {
         if (!drain(drained)) { ok = false; break; }
         ++drained;

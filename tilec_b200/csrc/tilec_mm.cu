@@ -66,11 +66,9 @@ cudaError_t set_tc_attr() {
 }
 
 // Stages per mode (a 3XTF32 stage holds raw + lo tiles): BN 256: 4 x 48 KB; 128: 6 x 32 KB;
-// 64: 8 x 24 KB; 32: 8 x 20 KB.
-#ifndef TILEC_3X_BK
-#define TILEC_3X_BK 16
-#endif
-constexpr int k3xBK = TILEC_3X_BK;  // K per stage of the 1-CTA 3XTF32 kernel
+// 64: 8 x 24 KB.  K per stage of the 1-CTA 3XTF32 kernel: 16 (32 was measured: no faster,
+// and twice the error, since fewer promotions per K).
+constexpr int k3xBK = 16;
 template <int BN>
 struct TcShape {
   static constexpr int kTf32Stages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
@@ -79,15 +77,11 @@ struct TcShape {
 
 
 
-// CTA-pair 3XTF32 kernel (tc2_gemm_kernel): 256 x 256 tiles, stages of 32 KB, used for
-// M >= TILEC_PAIR_MIN_M and N > 128 (B200: 245 vs 210 TFLOP/s for the 1-CTA kernel at 8192^3).
-#ifndef TILEC_PAIR_STAGES
-#define TILEC_PAIR_STAGES 6
-#endif
-#ifndef TILEC_PAIR_MIN_M
-#define TILEC_PAIR_MIN_M 256
-#endif
-constexpr int kPairStages = TILEC_PAIR_STAGES;
+// CTA-pair 3XTF32 kernel (tc2_gemm_kernel): 256 x 256 tiles, 6 stages of 32 KB (4 were
+// measured slower), used for M >= kPairMinM and N > 128 (B200: 245 vs 210 TFLOP/s for the
+// 1-CTA kernel at 8192^3).
+constexpr int kPairStages = 6;
+constexpr int64_t kPairMinM = 256;
 
 cudaError_t init_device_attrs() {
   cudaError_t e = cudaSuccess;
@@ -327,7 +321,7 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
   p->variant = variant;
   if (tensor) {
     p->bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
-    p->pair = variant != TILEC_MM_TF32 && p->bn == 256 && M > 128 && M >= TILEC_PAIR_MIN_M;
+    p->pair = variant != TILEC_MM_TF32 && p->bn == 256 && M >= kPairMinM;
     const int bk = variant == TILEC_MM_TF32 ? 32 : (p->pair ? 16 : k3xBK);
     const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
     // The CTA pair launches two CTAs per 256-row x 256-column tile; each computes 128 rows
