@@ -513,3 +513,22 @@ def test_fused_argument_errors():
         ext.matrix_mul_ex(x1, torch.randn(3, 16, 4, device=DEV))
     with pytest.raises(ValueError, match="overlap"):
         ext.matrix_mul_ex(x1, x2, out=torch.empty(8, 4, device=DEV).expand(2, 8, 4))
+
+
+@pytest.mark.parametrize("shape", [(512, 2048, 512), (1000, 3001, 777), (300, 520, 700)])
+@pytest.mark.parametrize("split_k", (1, 3))
+def test_tf32_pair_kernel_matches_single_cta(shape, split_k):
+    """TF32 on 256-row CTA pairs (M >= 256, N > 128) equals, row block by row block, the
+    1-CTA TF32 kernel that a 128-row slice runs on (same K order per element), and keeps
+    the TF32 error gate."""
+    m, k, n = shape
+    g = torch.Generator(device=DEV).manual_seed(m + k + n + 7 * split_k)
+    a = torch.randn(m, k, device=DEV, generator=g)
+    b = torch.randn(k, n, device=DEV, generator=g)
+    got = ext._matrix_mul(a, b, variant="tf32", split_k=split_k)
+    for r0 in range(0, m, 128):
+        part = ext._matrix_mul(a[r0:r0 + 128], b, variant="tf32", split_k=split_k)
+        assert torch.equal(got[r0:r0 + 128], part), r0
+    ref = a.double() @ b.double()
+    assert ((got.double() - ref).norm() / ref.norm()).item() <= 5e-3
+    assert _status_clean()

@@ -35,23 +35,27 @@
 
 namespace tilec {
 
-template <int BN, int STAGES>
+// SPLIT3: 3XTF32 (BK 16, raw + lo tiles per stage, K-chunk promotion through two TMEM
+// buffers); otherwise TF32 (BK 32, raw tiles only, one accumulator over all of K, the
+// split warps only relay "stage full" to the leader).
+template <int BN, int STAGES, bool SPLIT3 = true>
 struct Tc2Cfg {
-  static constexpr int BK = 16;
+  static constexpr int BK = SPLIT3 ? 16 : 32;
   static constexpr int kBNHalf = BN / 2;
   static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kABytes = 128 * BK * 4;          // own A rows
   static constexpr int kBBytes = BK * kBNHalf * 4;      // own half of B
-  static constexpr int kStageBytes = 2 * (kABytes + kBBytes);  // raw + lo
+  static constexpr int kStageBytes = (SPLIT3 ? 2 : 1) * (kABytes + kBBytes);  // raw (+ lo)
   static constexpr int kTxBytes = kABytes + kBBytes;
   static constexpr int kSmemBytes = STAGES * kStageBytes + 1024 + 1024;
-  static constexpr uint32_t kASbo = 512u;               // 8 rows x 64 B (64B swizzle)
+  static constexpr uint32_t kASbo = 8u * BK * 4u;       // 8 rows x BK*4 bytes (K-major)
+  static constexpr uint32_t kALayout = SPLIT3 ? kLayoutSw64 : kLayoutSw128;
   static constexpr uint32_t kBLbo = BK * 128u;          // stride between 32-column slabs
   static constexpr uint32_t kBSbo = 512u;               // stride between 4-row K groups
-  static constexpr uint32_t kTmemCols = 2 * BN;         // two chunk buffers of BN columns
+  static constexpr uint32_t kTmemCols = SPLIT3 ? 2 * BN : BN;  // chunk buffers of BN columns
   static constexpr int kColsPerThread = BN / 2;
-  static constexpr int kChunkBlocks = 8;
+  static constexpr int kChunkBlocks = SPLIT3 ? 8 : (1 << 30);  // TF32: one chunk
   static_assert(BN == 256 || BN == 128, "BN");
   static_assert(kSmemBytes <= 232448, "shared memory");
   static_assert(kEpiWarps * 32 * (kColsPerThread + 4) * 4 <= STAGES * kStageBytes, "output staging");
@@ -60,14 +64,14 @@ struct Tc2Cfg {
 // M = 256 (pair), N = BN, kind::tf32; A K-major and B MN-major unless `layout` flips
 // them (kOpAMN / kOpBK, operands stored transposed).
 // ANY_LAYOUT as in tc_gemm_kernel.
-template <int BN, int STAGES, bool HI_EXPLICIT, bool ANY_LAYOUT>
-__global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
+template <int BN, int STAGES, bool SPLIT3, bool HI_EXPLICIT, bool ANY_LAYOUT>
+__global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3>::kThreads, 1)
     tc2_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     float* __restrict__ out, int M, int N, int64_t ldo, int64_t out_slab, int K, int k_chunk,
                     int mp_tiles, int n_tiles, int group_m, int vec_out, int layout_arg, int64_t out_batch,
                     const float* __restrict__ bias, int act, int shared) {
   const int layout = ANY_LAYOUT ? layout_arg : 0;
-  using Cfg = Tc2Cfg<BN, STAGES>;
+  using Cfg = Tc2Cfg<BN, STAGES, SPLIT3>;
   constexpr int BK = Cfg::BK;
   constexpr int KC = Cfg::kChunkBlocks;
   extern __shared__ uint8_t smem_raw[];
@@ -192,10 +196,10 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
       const uint32_t idesc = make_idesc_tf32(256, BN, a_mn, !b_k);
       auto desc_a = [&](uint32_t base, int kk) {
         return a_mn ? make_smem_desc(base + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32)
-                    : make_smem_desc(base + kk * 32, 16, Cfg::kASbo, kLayoutSw64);
+                    : make_smem_desc(base + kk * 32, 16, Cfg::kASbo, Cfg::kALayout);
       };
       auto desc_b = [&](uint32_t base, int kk) {
-        return b_k ? make_smem_desc(base + kk * 32, 16, Cfg::kASbo, kLayoutSw64)
+        return b_k ? make_smem_desc(base + kk * 32, 16, Cfg::kASbo, Cfg::kALayout)
                    : make_smem_desc(base + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
       };
       const uint32_t peer = 1u;
@@ -212,15 +216,18 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
         if (!mbar_wait_cluster(&split[s], ph, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t a_hi = smem_u32(a_raw(s)), b_hi = smem_u32(b_raw(s));
-        const uint32_t a_l = smem_u32(a_lo(s)), b_l = smem_u32(b_lo(s));
 #pragma unroll
         for (int kk = 0; kk < BK / 8; ++kk) {
           const uint64_t ad = desc_a(a_hi, kk), bd = desc_b(b_hi, kk);
-          const uint64_t adl = desc_a(a_l, kk), bdl = desc_b(b_l, kk);
           const uint32_t accum = (chunk_start && kk == 0) ? 0u : 1u;
-          umma_tf32_pair(tmem + dcol, adl, bd, idesc, accum);  // small terms first
-          umma_tf32_pair(tmem + dcol, ad, bdl, idesc, 1u);
-          umma_tf32_pair(tmem + dcol, ad, bd, idesc, 1u);
+          if constexpr (SPLIT3) {
+            const uint64_t adl = desc_a(smem_u32(a_lo(s)), kk), bdl = desc_b(smem_u32(b_lo(s)), kk);
+            umma_tf32_pair(tmem + dcol, adl, bd, idesc, accum);  // small terms first
+            umma_tf32_pair(tmem + dcol, ad, bdl, idesc, 1u);
+            umma_tf32_pair(tmem + dcol, ad, bd, idesc, 1u);
+          } else {
+            umma_tf32_pair(tmem + dcol, ad, bd, idesc, accum);
+          }
         }
         const uint32_t e_local = smem_u32(&empty[s]);
         umma_commit_pair(e_local);
@@ -273,25 +280,27 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES>::kThreads, 1)
       const int s = kb % STAGES;
       const uint32_t ph = (kb / STAGES) & 1;
       if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
-      float4* src_a = reinterpret_cast<float4*>(a_raw(s));
-      float4* dst_a = reinterpret_cast<float4*>(a_lo(s));
+      if constexpr (SPLIT3) {
+        float4* src_a = reinterpret_cast<float4*>(a_raw(s));
+        float4* dst_a = reinterpret_cast<float4*>(a_lo(s));
 #pragma unroll
-      for (int i = et; i < Cfg::kABytes / 16; i += 32 * Cfg::kEpiWarps) {
-        const float4 x = src_a[i];
-        const float4 hv = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-        dst_a[i] = make_float4(x.x - hv.x, x.y - hv.y, x.z - hv.z, x.w - hv.w);
-        if constexpr (HI_EXPLICIT) src_a[i] = hv;
-      }
-      float4* src_b = reinterpret_cast<float4*>(b_raw(s));
-      float4* dst_b = reinterpret_cast<float4*>(b_lo(s));
+        for (int i = et; i < Cfg::kABytes / 16; i += 32 * Cfg::kEpiWarps) {
+          const float4 x = src_a[i];
+          const float4 hv = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+          dst_a[i] = make_float4(x.x - hv.x, x.y - hv.y, x.z - hv.z, x.w - hv.w);
+          if constexpr (HI_EXPLICIT) src_a[i] = hv;
+        }
+        float4* src_b = reinterpret_cast<float4*>(b_raw(s));
+        float4* dst_b = reinterpret_cast<float4*>(b_lo(s));
 #pragma unroll
-      for (int i = et; i < Cfg::kBBytes / 16; i += 32 * Cfg::kEpiWarps) {
-        const float4 x = src_b[i];
-        const float4 hv = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
-        dst_b[i] = make_float4(x.x - hv.x, x.y - hv.y, x.z - hv.z, x.w - hv.w);
-        if constexpr (HI_EXPLICIT) src_b[i] = hv;
+        for (int i = et; i < Cfg::kBBytes / 16; i += 32 * Cfg::kEpiWarps) {
+          const float4 x = src_b[i];
+          const float4 hv = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+          dst_b[i] = make_float4(x.x - hv.x, x.y - hv.y, x.z - hv.z, x.w - hv.w);
+          if constexpr (HI_EXPLICIT) src_b[i] = hv;
+        }
+        fence_proxy_async_smem();
       }
-      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote_cta(mapa_shared(smem_u32(&split[s]), 0));
       if (kb % KC == (kLag < KC ? kLag : KC - 1) && kb / KC >= 1 && drained < kb / KC) {

@@ -105,14 +105,16 @@ cudaError_t init_device_attrs() {
   acc(set_tc_attr<256, k3xBK, TcShape<256>::k3xStages, true, false>());
   acc(set_tc_attr<128, k3xBK, TcShape<128>::k3xStages, true, false>());
   acc(set_tc_attr<64, k3xBK, TcShape<64>::k3xStages, true, false>());
-  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, false, false>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, Tc2Cfg<256, kPairStages>::kSmemBytes));
-  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, true, false>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, Tc2Cfg<256, kPairStages>::kSmemBytes));
-  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, false, true>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, Tc2Cfg<256, kPairStages>::kSmemBytes));
-  acc(cudaFuncSetAttribute(tc2_gemm_kernel<256, kPairStages, true, true>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, Tc2Cfg<256, kPairStages>::kSmemBytes));
+  auto pair_attr = [&](auto kern, int smem) {
+    acc(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  };
+  constexpr int k3x = Tc2Cfg<256, kPairStages, true>::kSmemBytes, kTf = Tc2Cfg<256, kPairStages, false>::kSmemBytes;
+  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, false>, k3x);
+  pair_attr(tc2_gemm_kernel<256, kPairStages, true, true, false>, k3x);
+  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, true>, k3x);
+  pair_attr(tc2_gemm_kernel<256, kPairStages, true, true, true>, k3x);
+  pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, false>, kTf);
+  pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, true>, kTf);
   return e;
 }
 
@@ -321,8 +323,8 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
   p->variant = variant;
   if (tensor) {
     p->bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
-    p->pair = variant != TILEC_MM_TF32 && p->bn == 256 && M >= kPairMinM;
-    const int bk = variant == TILEC_MM_TF32 ? 32 : (p->pair ? 16 : k3xBK);
+    p->pair = p->bn == 256 && M >= kPairMinM;
+    const int bk = variant == TILEC_MM_TF32 ? 32 : k3xBK;
     const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
     // The CTA pair launches two CTAs per 256-row x 256-column tile; each computes 128 rows
     // and loads half of the B columns.
@@ -515,10 +517,10 @@ int launch_tc_mode(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int6
     return launch_tc<BN, 32, TcShape<BN>::kTf32Stages, false, false>(ma, mb, M, N, K, L, s);
 }
 
-template <bool HI>
+template <bool SPLIT3, bool HI>
 int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
                cudaStream_t s) {
-  using Cfg = Tc2Cfg<256, kPairStages>;
+  using Cfg = Tc2Cfg<256, kPairStages, SPLIT3>;
   const int mp_tiles = static_cast<int>(cdiv(M, 256));
   const int n_tiles = static_cast<int>(cdiv(N, 256));
   const int group_m = 8;
@@ -529,7 +531,8 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t 
                     static_cast<int>(N), L.ldo, L.out_slab, static_cast<int>(K), static_cast<int>(L.k_chunk),
                     mp_tiles, n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias, L.act, L.shared);
   };
-  return L.layout ? go(tc2_gemm_kernel<256, kPairStages, HI, true>) : go(tc2_gemm_kernel<256, kPairStages, HI, false>);
+  return L.layout ? go(tc2_gemm_kernel<256, kPairStages, SPLIT3, HI, true>)
+                  : go(tc2_gemm_kernel<256, kPairStages, SPLIT3, HI, false>);
 }
 
 template <bool SPLIT3, bool HI>
@@ -784,12 +787,13 @@ int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, vo
     rc = launch_simt(p.bn, vec, grid, A, B, M, N, K, lda, ldb, sa, sb, L, s);
   } else {
     CUtensorMap ma, mb;
-    const int bk = p.variant == TILEC_MM_TF32 ? 32 : (p.pair ? 16 : k3xBK);
+    const int bk = p.variant == TILEC_MM_TF32 ? 32 : k3xBK;
     rc = encode_maps(A, B, M, N, K, lda, ldb, sa, na, sb, nbb, bk, L.layout, p.pair ? 128 : p.bn, &ma, &mb);
     if (rc) return rc;
     if (p.pair)
-      rc = p.variant == TILEC_MM_3XTF32 ? launch_tc2<false>(ma, mb, M, N, K, L, s)
-                                        : launch_tc2<true>(ma, mb, M, N, K, L, s);
+      rc = p.variant == TILEC_MM_TF32     ? launch_tc2<false, false>(ma, mb, M, N, K, L, s)
+           : p.variant == TILEC_MM_3XTF32 ? launch_tc2<true, false>(ma, mb, M, N, K, L, s)
+                                          : launch_tc2<true, true>(ma, mb, M, N, K, L, s);
     else if (p.variant == TILEC_MM_TF32)
       rc = dispatch_tc_bn<false, false>(p.bn, ma, mb, M, N, K, L, s);
     else if (p.variant == TILEC_MM_3XTF32)
