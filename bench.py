@@ -1,7 +1,7 @@
 """Benchmark of tilec_b200.ext.matrix_mul on B200 (one JSON line on rank 0).
 
-Workload (the config the headline metric is quoted on at 1/2/4/8
-GPUs): C = x1 @ x2 with M = 65536, K = 8192, N = 8192, fp32.  x1 ~ N(0,1) is split into
+Workload (benchmark config 5, the one the headline metric is quoted on at 1/2/4/8 GPUs):
+C = x1 @ x2 with M = 65536, K = 8192, N = 8192, fp32.  x1 ~ N(0,1) is split into
 M/world row blocks (rank r owns its block), x2 ~ N(0, 1/K) lives on rank 0 and is
 NCCL-broadcast each step; C stays row-sharded.  One step = broadcast of x2 (world > 1)
 + the local GEMM of every rank.  Total work is fixed as the GPU count grows (strong
@@ -263,7 +263,8 @@ def time_launches(fn, reps, warm=10):
 
 
 def extra_configs(pk):
-    """Single-GPU figures for BASELINE configs 1-3 (inputs rotated over a pool larger than L2)."""
+    """Single-GPU figures for benchmark configs 1-3 (512x4096x64, 2048^3, 1000x3001x777;
+    inputs rotated over a pool larger than L2)."""
     from tilec_b200 import ext
     out = {}
     l2_bytes = 126 * 2 ** 20

@@ -42,7 +42,7 @@ def digest(*arrays):
 
 
 def config4_shapes(n=64, seed=4):
-    """seeded log-uniform (M, K, N) triples over [1, 8192]^3.
+    """Benchmark config 4: seeded log-uniform (M, K, N) triples over [1, 8192]^3.
 
     Modelled on the reference tuner's shape sampler (tilec/tune.py:54-65) but spanning
     [1, 8192] per dimension; the first triple is forced to M = 1 (GEMV-like) and the
@@ -65,7 +65,7 @@ def config4_shapes(n=64, seed=4):
     return out
 
 
-# BASELINE configs 1-3 and 5 as (M, K, N, distribution).
+# Benchmark configs 1-3 and 5 as (M, K, N, distribution).
 CONFIG1 = (512, 4096, 64, "normal")
 CONFIG2 = (2048, 2048, 2048, "normal")
 CONFIG3 = (1000, 3001, 777, "uniform")

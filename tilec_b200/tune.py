@@ -9,7 +9,7 @@
 CUDA events around back-to-back launches after warm-up (tilec/tune.py:35-51 used
 perf_counter + synchronize and a median of 5), with the same early abort for configs far
 slower than the best so far.  The shape sampler follows tilec/tune.py:54-65 but spans
-[1, 8192] per dimension and includes M = 1 and N <= 64 cases.
+[1, 8192] per dimension (benchmark config 4) and includes M = 1 and N <= 64 cases.
 
 ``train`` mirrors tilec/tune.py:99-132: a held-out 20% of shapes measures the geo-mean
 "x of best" of the fitted selector against the library's built-in rules
