@@ -546,8 +546,13 @@ int dispatch_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, int64_t
 }
 
 // dst[b][r, 0:cols] = src[b][r, 0:cols] for batch b = blockIdx.y (src batch stride
-// sstride, dst dense: batch stride rows*ldd), row strides lds / ldd; one CTA per row,
-// grid-stride.
+// sstride, dst dense: batch stride rows*ldd), row strides lds / ldd, dst 16-byte aligned
+// with ldd a multiple of 4.  Source rows are only 4-byte aligned, so each thread reads the
+// two 16-byte-aligned float4s that hold its output chunk and shifts them into place: 16-byte
+// loads and stores throughout.  An aligned float4 never crosses a page, so reading one that
+// holds at least one element of the row cannot fault; the padding columns of the copy
+// (cols .. ldd) receive whatever the last chunk held and are never read by the GEMM.
+// Short rows share a block: a warp per row when cols <= 128.
 __global__ void __launch_bounds__(256) pack_rows_kernel(const float* __restrict__ src, int64_t lds, int64_t sstride,
                                                         float* __restrict__ dst, int64_t ldd, int64_t rows,
                                                         int64_t cols, int64_t batches) {
@@ -556,10 +561,41 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const float* __restrict_
   (void)batches;
   src += static_cast<int64_t>(blockIdx.y) * sstride;
   dst += static_cast<int64_t>(blockIdx.y) * rows * ldd;
-  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+  const int64_t lanes = cols <= 128 ? 32 : blockDim.x;
+  const int64_t rows_per_block = blockDim.x / lanes;
+  const int64_t sub = threadIdx.x / lanes, t = threadIdx.x % lanes;
+  const int64_t chunks = (cols + 3) / 4;
+  for (int64_t r = blockIdx.x * rows_per_block + sub; r < rows; r += gridDim.x * rows_per_block) {
     const float* s = src + r * lds;
-    float* d = dst + r * ldd;
-    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) d[c] = s[c];
+    const int shift = static_cast<int>((reinterpret_cast<uintptr_t>(s) >> 2) & 3);
+    const float4* base = reinterpret_cast<const float4*>(s - shift);
+    const int64_t last = (shift + cols - 1) / 4;  // last aligned float4 holding row data
+    float4* d = reinterpret_cast<float4*>(dst + r * ldd);
+    for (int64_t q0 = t; q0 < chunks; q0 += 2 * lanes) {
+      float4 lo[2], hi[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int64_t q = q0 + j * lanes;
+        if (q < chunks) {
+          lo[j] = __ldg(base + q);
+          hi[j] = q + 1 <= last ? __ldg(base + q + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int64_t q = q0 + j * lanes;
+        if (q >= chunks) continue;
+        const float w[8] = {lo[j].x, lo[j].y, lo[j].z, lo[j].w, hi[j].x, hi[j].y, hi[j].z, hi[j].w};
+        float4 o;
+        switch (shift) {
+          case 0: o = lo[j]; break;
+          case 1: o = make_float4(w[1], w[2], w[3], w[4]); break;
+          case 2: o = make_float4(w[2], w[3], w[4], w[5]); break;
+          default: o = make_float4(w[3], w[4], w[5], w[6]); break;
+        }
+        d[q] = o;
+      }
+    }
   }
 }
 
@@ -604,8 +640,9 @@ int launch_transpose(const float* src, int64_t lds, int64_t sstride, float* dst,
 
 int launch_pack(const float* src, int64_t lds, int64_t sstride, float* dst, int64_t ldd, int64_t rows, int64_t cols,
                 int64_t batches, const DeviceInfo& d, cudaStream_t s) {
-  const int64_t cap = int64_t(d.sms) * 16 / batches + 1;
-  int64_t blocks = rows < cap ? rows : cap;
+  const int64_t cap = int64_t(d.sms) * 8 / batches + 1;
+  const int64_t per_block = cols <= 128 ? 8 : 1;  // rows per 256-thread block
+  int64_t blocks = cdiv(rows, per_block) < cap ? cdiv(rows, per_block) : cap;
   if (blocks < 1) blocks = 1;
   return launch_k(pack_rows_kernel, dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(batches)), dim3(256), 0,
                   s, 1, src, lds, sstride, dst, ldd, rows, cols, batches);
