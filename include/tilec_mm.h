@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define TILEC_MM_ABI_VERSION 3
+#define TILEC_MM_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define TILEC_API __attribute__((visibility("default")))
@@ -92,6 +92,18 @@ typedef struct tilec_mm_cfg {
  * they were reserved[0..1] and had to be zero, so version-1 callers keep their meaning.) */
 #define TILEC_MM_TRANS_A 1
 #define TILEC_MM_TRANS_B 2
+
+/* cfg->flags (ABI version 4): stream-K for the CTA-pair tensor-core kernel (256 x 256
+ * tiles; M >= 256, N > 128).  The GEMM then runs as one wave of CTA pairs that share out
+ * the K blocks of the tiles beyond the last complete wave, instead of one pair per tile,
+ * and the pairs add each tile's partial sums in a fixed order (results are deterministic
+ * and independent of timing, but differ in rounding from the one-pair-per-tile form).
+ * AUTO with split_k == 0 uses it where it pays (81 tiles on 74 pair slots: 1.47x on B200);
+ * setting the flag asks for it whenever the pair kernel runs and split_k <= 1; split_k >= 2
+ * (K slices) never uses it.  tilec_mm_plan sets the flag in its output when the plan is
+ * stream-K, so feeding that output back reproduces the plan.  Needs workspace (partial
+ * tiles, 256 KiB per pair): ask tilec_mm_workspace_bytes. */
+#define TILEC_MM_STREAM_K 4
 
 /* C = A . B  (see the semantics block above).
  * cfg may be NULL (= AUTO).  workspace/ws_bytes: scratch for split-K partial sums;

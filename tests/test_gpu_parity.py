@@ -246,13 +246,18 @@ def test_matrix_mul_host_pipelined(chunks):
 @pytest.mark.parametrize("shape", [(4096, 1024, 1024), (4096, 2048, 64), (4096, 999, 333)])
 def test_matrix_mul_host_equals_device_bitwise(shape, chunks):
     """Chunked host-buffer product (tapered or explicit spans, chunks below one 256-row
-    CTA-pair tile included) = the unchunked device product, bit for bit: every chunk runs
-    the kernel and K split planned for the full product."""
+    CTA-pair tile included) = the unchunked device product under the same plan, bit for
+    bit: every chunk runs the kernel and K split planned for the full product (a stream-K
+    plan runs as one pair per tile, since stream-K groups each tile's sums by the tile
+    count of the whole product)."""
     m, k, n = shape
     g = torch.Generator().manual_seed(m + k + n)
     x1 = torch.randn(m, k, generator=g).pin_memory()
     x2 = torch.randn(k, n, generator=g).pin_memory()
-    want = ext.matrix_mul(x1.to(DEV), x2.to(DEV)).cpu()
+    d1, d2 = x1.to(DEV), x2.to(DEV)
+    v, s = ext.plan(d1, d2)
+    want = ext._matrix_mul(d1, d2, variant=v, split_k=s).cpu()
+    assert oracle.rel_frob(want.numpy(), ext.matrix_mul(d1, d2).cpu().numpy()) <= 1e-5
     got = ext.matrix_mul_host(x1, x2, chunks=chunks)
     assert torch.equal(got, want)
 
@@ -291,13 +296,16 @@ def test_skinny_split_k(shape):
     assert _status_clean()
 
 
-@pytest.mark.parametrize("variant,split_k", [("3xtf32", 0), ("3xtf32", 29), ("splitk", 8), ("tf32", 5),
-                                             ("3xtf32", 1), ("simt", 0)])
-def test_back_to_back_launches_in_a_graph(variant, split_k):
+@pytest.mark.parametrize("variant,split_k,stream_k", [("3xtf32", 0, False), ("3xtf32", 29, False),
+                                                      ("splitk", 8, False), ("tf32", 5, False),
+                                                      ("3xtf32", 1, False), ("simt", 0, False),
+                                                      ("3xtf32", 0, True), ("tf32", 0, True)])
+def test_back_to_back_launches_in_a_graph(variant, split_k, stream_k):
     """Kernels start while the previous one drains (programmatic dependent launch): a
     CUDA graph of consecutive products that share one workspace and chain through their
     outputs (each next input is the previous output) must equal the same calls run one
-    at a time with a device sync between them."""
+    at a time with a device sync between them.  With stream_k the [512 x 64] x [64 x 2048]
+    products run in stream-K form, whose ready flags are cleared inside the graph."""
     g = torch.Generator(device=DEV).manual_seed(17)
     m, k, n = 512, 2048, 64
     a = torch.randn(m, k, device=DEV, generator=g)
@@ -309,8 +317,8 @@ def test_back_to_back_launches_in_a_graph(variant, split_k):
     def chain():
         x = a
         for i in range(3):
-            ext._matrix_mul(x, bs[i], variant=variant, split_k=split_k, out=outs[i])
-            ext._matrix_mul(outs[i], w, variant=variant, split_k=split_k, out=mids[i])
+            ext._matrix_mul(x, bs[i], variant=variant, split_k=split_k, out=outs[i], stream_k=stream_k)
+            ext._matrix_mul(outs[i], w, variant=variant, split_k=split_k, out=mids[i], stream_k=stream_k)
             x = mids[i]
 
     side = torch.cuda.Stream(device=DEV)
@@ -330,9 +338,9 @@ def test_back_to_back_launches_in_a_graph(variant, split_k):
     # Reference: the same chain with a full device sync after every call.
     x = a
     for i in range(3):
-        ext._matrix_mul(x, bs[i], variant=variant, split_k=split_k, out=outs[i])
+        ext._matrix_mul(x, bs[i], variant=variant, split_k=split_k, out=outs[i], stream_k=stream_k)
         torch.cuda.synchronize()
-        ext._matrix_mul(outs[i], w, variant=variant, split_k=split_k, out=mids[i])
+        ext._matrix_mul(outs[i], w, variant=variant, split_k=split_k, out=mids[i], stream_k=stream_k)
         torch.cuda.synchronize()
         x = mids[i]
     for g_, r in zip(got, outs + mids):
@@ -531,4 +539,91 @@ def test_tf32_pair_kernel_matches_single_cta(shape, split_k):
         assert torch.equal(got[r0:r0 + 128], part), r0
     ref = a.double() @ b.double()
     assert ((got.double() - ref).norm() / ref.norm()).item() <= 5e-3
+    assert _status_clean()
+
+
+# ---------------------------------------------------------------- stream-K form of the CTA-pair kernel
+
+def _rel(got, ref):
+    got, ref = got.double().cpu(), ref.double().cpu()
+    return ((got - ref).norm() / ref.norm()).item()
+
+
+SK_SHAPES = [
+    (2048, 2048, 2048),  # 64 tiles, one wave of pairs
+    (2304, 2048, 2304),  # 81 tiles: two waves as one pair per tile (AUTO takes stream-K)
+    (1000, 3001, 777),   # 16 ragged tiles, about five pairs per tile
+    (300, 200, 520),     # 6 tiles of 13 k-blocks: 78 units, one or two per pair
+    (257, 64, 300),      # 2 tiles of 4 k-blocks: 8 pairs of one unit
+    (4096, 1024, 4608),  # 288 tiles: two whole waves, then stream-K over the rest
+]
+
+
+@pytest.mark.parametrize("variant", TENSOR)
+@pytest.mark.parametrize("shape", SK_SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_stream_k_matches_oracle_and_one_pair_per_tile(shape, variant):
+    """Stream-K (pairs share out the k-blocks of the tiles and add each tile's partial
+    sums in pair order) keeps the variant's error gate against the fp64 product, agrees
+    with the one-pair-per-tile form up to fp32 regrouping, and is deterministic."""
+    m, k, n = shape
+    g = torch.Generator().manual_seed(m + 3 * k + 7 * n)
+    x1 = torch.randn(m, k, generator=g)
+    x2 = torch.randn(k, n, generator=g)
+    a, b = x1.to(DEV), x2.to(DEV)
+    info = ext.plan(a, b, variant=variant, stream_k=True, detail=True)
+    assert info["stream_k"] and info["split_k"] == 1, info
+    sk = ext._matrix_mul(a, b, variant=variant, stream_k=True)
+    dp = ext._matrix_mul(a, b, variant=variant, split_k=1)
+    assert _rel(sk, x1.double() @ x2.double()) <= TOL[variant]
+    assert _rel(sk, dp) <= 1e-5
+    assert torch.equal(sk, ext._matrix_mul(a, b, variant=variant, stream_k=True))
+    assert _status_clean()
+
+
+def test_stream_k_is_auto_choice_where_tiles_leave_pairs_idle():
+    """AUTO takes stream-K where one pair per tile would leave most of a wave idle (81
+    tiles: two waves on 74 pair slots), not where the last wave is nearly full (2048^3:
+    64 tiles in one wave, which stream-K's slower k-blocks would not win back)."""
+    x = torch.empty(2304, 2048, device=DEV)
+    assert ext.plan(x, x.t(), detail=True) == {"variant": "3xtf32", "split_k": 1, "stream_k": True}
+    a = torch.empty(2048, 2048, device=DEV)
+    assert not ext.plan(a, a, detail=True)["stream_k"]
+    # Whole waves (or K slices asked for) keep one pair per tile.
+    big = torch.empty(65536, 8192, device=DEV)
+    assert not ext.plan(big, torch.empty(8192, 8192, device=DEV), detail=True)["stream_k"]
+    assert not ext.plan(a, a, variant="3xtf32", split_k=2, stream_k=True, detail=True)["stream_k"]
+    assert not ext.plan(a, a, variant="3xtf32", split_k=1, detail=True)["stream_k"]
+    assert ext.plan(a, a, variant="3xtf32", split_k=1, stream_k=True, detail=True)["stream_k"]
+    # Kernels without a CTA pair ignore the flag.
+    assert not ext.plan(a[:, :64], a[:64, :64], stream_k=True, detail=True)["stream_k"]
+
+
+@pytest.mark.parametrize("ta,tb", [(False, True), (True, False), (True, True)])
+def test_stream_k_transposed_views(ta, tb):
+    m, k, n = 1000, 3001, 777
+    g = torch.Generator(device=DEV).manual_seed(31 + 2 * ta + tb)
+    a = torch.randn(k, m, device=DEV, generator=g).t() if ta else torch.randn(m, k, device=DEV, generator=g)
+    b = torch.randn(n, k, device=DEV, generator=g).t() if tb else torch.randn(k, n, device=DEV, generator=g)
+    for v in ("3xtf32", "tf32"):
+        sk = ext._matrix_mul(a, b, variant=v, stream_k=True)
+        assert _rel(sk, ext._matrix_mul(a, b, variant=v, split_k=1)) <= 1e-5
+        assert _rel(sk, a.double() @ b.double()) <= TOL[v]
+    assert _status_clean()
+
+
+@pytest.mark.parametrize("act", (None, "relu", "gelu"))
+def test_stream_k_batched_fused(act):
+    """Stream-K over the tiles of a whole batch (units run across batch boundaries), with
+    the bias / activation epilogue applied where each tile is stored, and a shared B."""
+    g = torch.Generator(device=DEV).manual_seed(5)
+    a = torch.randn(3, 600, 1024, device=DEV, generator=g)
+    b = torch.randn(3, 1024, 520, device=DEV, generator=g) / 32
+    bias = torch.randn(520, device=DEV, generator=g)
+    got = ext.matrix_mul_ex(a, b, bias=bias, activation=act, stream_k=True)
+    for i in range(3):
+        want = ext.matrix_mul_ex(a[i], b[i], bias=bias, activation=act, split_k=1)
+        assert _rel(got[i], want) <= 1e-5, i
+        assert _rel(got[i], _ref64(a[i], b[i], bias, act)) <= 1e-5, i
+    shared = ext.matrix_mul_ex(a, b[0], bias=bias, activation=act, stream_k=True)
+    assert _rel(shared[2], _ref64(a[2], b[0], bias, act)) <= 1e-5
     assert _status_clean()

@@ -35,6 +35,7 @@ class MMConfig(ctypes.Structure):
 
 TRANS_A = 1   # TILEC_MM_TRANS_A: A stored K x M (x1 is a column view, e.g. y.t())
 TRANS_B = 2   # TILEC_MM_TRANS_B: B stored N x K
+STREAM_K = 4  # TILEC_MM_STREAM_K: CTA-pair kernel as one wave of pairs sharing out K blocks
 ACTIVATIONS = {None: 0, "none": 0, "relu": 1, "gelu": 2}   # TILEC_MM_ACT_*
 
 

@@ -105,6 +105,36 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// ---------------------------------------------------------------- flags between CTAs in global memory
+// A producer CTA publishes data with plain stores, then one thread raises a flag with a
+// release at GPU scope; the consumer polls the flag with acquire loads.
+__device__ __forceinline__ void flag_release(int* f, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+__device__ __forceinline__ int flag_acquire(const int* f) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+// Bounded wait for a nonzero flag, with the same limit, abort flag and status bit as mbar_wait.
+__device__ __forceinline__ bool flag_wait(const int* f, volatile int* abort_flag,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
+  if (flag_acquire(f)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(64);
+    if (flag_acquire(f)) return true;
+    if ((it & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > limit_ns) {
+        *abort_flag = 1;
+        record_status(TILEC_DEV_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- proxies / fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -38,7 +38,11 @@ namespace tilec {
 // SPLIT3: 3XTF32 (BK 16, raw + lo tiles per stage, K-chunk promotion through two TMEM
 // buffers); otherwise TF32 (BK 32, raw tiles only, one accumulator over all of K, the
 // split warps only relay "stage full" to the leader).
-template <int BN, int STAGES, bool SPLIT3 = true>
+// SK: the stream-K kernel (tc2_sk.cuh) on the same stages: two TMEM buffers in both modes
+// (a segment's sums are read out while the next segment's MMAs run), a smaller barrier
+// area and a 32 x 33 float block per epilogue warp for stores made while the stages
+// still stream.  SK = false is the one-pair-per-tile kernel below.
+template <int BN, int STAGES, bool SPLIT3 = true, bool SK = false>
 struct Tc2Cfg {
   static constexpr int BK = SPLIT3 ? 16 : 32;
   static constexpr int kBNHalf = BN / 2;
@@ -48,17 +52,22 @@ struct Tc2Cfg {
   static constexpr int kBBytes = BK * kBNHalf * 4;      // own half of B
   static constexpr int kStageBytes = (SPLIT3 ? 2 : 1) * (kABytes + kBBytes);  // raw (+ lo)
   static constexpr int kTxBytes = kABytes + kBBytes;
-  static constexpr int kSmemBytes = STAGES * kStageBytes + 1024 + 1024;
+  static constexpr int kBarBytes = SK ? 256 : 1024;
+  static constexpr int kBlockPitch = 33;                // 32 x 33 floats: conflict-free both ways
+  static constexpr int kBlockBytes = SK ? kEpiWarps * 32 * kBlockPitch * 4 : 0;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + 1024 + kBarBytes + kBlockBytes;
   static constexpr uint32_t kASbo = 8u * BK * 4u;       // 8 rows x BK*4 bytes (K-major)
   static constexpr uint32_t kALayout = SPLIT3 ? kLayoutSw64 : kLayoutSw128;
   static constexpr uint32_t kBLbo = BK * 128u;          // stride between 32-column slabs
   static constexpr uint32_t kBSbo = 512u;               // stride between 4-row K groups
-  static constexpr uint32_t kTmemCols = SPLIT3 ? 2 * BN : BN;  // chunk buffers of BN columns
+  static constexpr uint32_t kTmemCols = (SPLIT3 || SK) ? 2 * BN : BN;  // chunk buffers of BN columns
   static constexpr int kColsPerThread = BN / 2;
-  static constexpr int kChunkBlocks = SPLIT3 ? 8 : (1 << 30);  // TF32: one chunk
+  static constexpr int kChunkBlocks = SPLIT3 ? 8 : (1 << 30);  // TF32: one chunk (per segment)
+  static constexpr int kPartialFloats = 2 * kEpiWarps * 32 * kColsPerThread;  // one pair's tile
   static_assert(BN == 256 || BN == 128, "BN");
   static_assert(kSmemBytes <= 232448, "shared memory");
   static_assert(kEpiWarps * 32 * (kColsPerThread + 4) * 4 <= STAGES * kStageBytes, "output staging");
+  static_assert((3 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");  // mbarriers + TMEM slot + abort flag
 };
 
 // M = 256 (pair), N = BN, kind::tf32; A K-major and B MN-major unless `layout` flips

@@ -24,6 +24,7 @@
 #include "simt.cuh"
 #include "tc_gemm.cuh"
 #include "tc2_gemm.cuh"
+#include "tc2_sk.cuh"
 
 static_assert(TILEC_DEV_STATUS_TIMEOUT == tilec::TILEC_DEV_TIMEOUT && TILEC_DEV_STATUS_TMEM == tilec::TILEC_DEV_TMEM &&
                   TILEC_DEV_STATUS_BAD_LAUNCH == tilec::TILEC_DEV_BAD_LAUNCH,
@@ -43,6 +44,7 @@ struct DeviceInfo {
   int cc_major = 0;
   int cc_minor = 0;
   int max_smem_optin = 0;
+  int pair_slots = 0;  // CTA pairs of the stream-K pair kernel resident at once (0: stream-K off)
   cudaError_t init_err = cudaSuccess;
 };
 
@@ -108,6 +110,7 @@ cudaError_t init_device_attrs() {
   auto pair_attr = [&](auto kern, int smem) {
     acc(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   };
+  // Every (mode, layout) instantiation of both pair kernels that the launch paths use.
   constexpr int k3x = Tc2Cfg<256, kPairStages, true>::kSmemBytes, kTf = Tc2Cfg<256, kPairStages, false>::kSmemBytes;
   pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, false>, k3x);
   pair_attr(tc2_gemm_kernel<256, kPairStages, true, true, false>, k3x);
@@ -115,7 +118,40 @@ cudaError_t init_device_attrs() {
   pair_attr(tc2_gemm_kernel<256, kPairStages, true, true, true>, k3x);
   pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, false>, kTf);
   pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, true>, kTf);
+  constexpr int s3x = Tc2Cfg<256, kPairStages, true, true>::kSmemBytes;
+  constexpr int sTf = Tc2Cfg<256, kPairStages, false, true>::kSmemBytes;
+  pair_attr(tc2_sk_kernel<256, kPairStages, true, false, false>, s3x);
+  pair_attr(tc2_sk_kernel<256, kPairStages, true, true, false>, s3x);
+  pair_attr(tc2_sk_kernel<256, kPairStages, true, false, true>, s3x);
+  pair_attr(tc2_sk_kernel<256, kPairStages, true, true, true>, s3x);
+  pair_attr(tc2_sk_kernel<256, kPairStages, false, false, false>, sTf);
+  pair_attr(tc2_sk_kernel<256, kPairStages, false, false, true>, sTf);
   return e;
+}
+
+// CTA pairs of the stream-K kernel that fit on the device at once (clusters must sit within
+// one GPC, so this can be below SMs / 2).  A stream-K launch never asks for more: its pairs
+// wait on one another's partial tiles.  0 disables stream-K.
+int query_pair_slots() {
+  using Cfg = Tc2Cfg<256, kPairStages, true, true>;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(2, 1, 1);
+  lc.blockDim = dim3(Cfg::kThreads);
+  lc.dynamicSmemBytes = Cfg::kSmemBytes;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  lc.attrs = &attr;
+  lc.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, tc2_sk_kernel<256, kPairStages, true, false, false>, &lc) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
 }
 
 int current_device(DeviceInfo** out) {
@@ -134,6 +170,7 @@ int current_device(DeviceInfo** out) {
       e = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e == cudaSuccess && d.cc_major != 10) e = cudaErrorNoKernelImageForDevice;
     if (e == cudaSuccess) e = init_device_attrs();
+    if (e == cudaSuccess) d.pair_slots = query_pair_slots();
     d.init_err = e;
     cudaGetLastError();
   });
@@ -160,6 +197,7 @@ inline int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
 
 // Workspace layout (each region 256-byte aligned):
 //   [packed A: M x round_up(K,4)] [packed B: K x round_up(N,4)] [split-K slabs: split x M x round_up(N,4)]
+//   [stream-K: pairs x 256 x 256 fp32 partial tiles][pairs x 16 int ready flags]
 // One call's arguments: a single product is batch 1 (batch strides unused).  Batch b reads
 // A + b*stride_a and B + b*stride_b (a zero stride shares that operand) and writes
 // C + b*stride_c; bias (per column, or nullptr) and act form the fused epilogue.
@@ -185,6 +223,9 @@ struct Plan {
   bool pack_a = false, pack_b = false;    // tensor variants: aligned copy, same storage order
   bool tpose_a = false, tpose_b = false;  // SIMT variants: transposed operand -> row-major copy
   bool pair = false;  // 3XTF32 on a CTA pair (tc2_gemm_kernel, 256 x 256 tiles)
+  bool sk = false;    // pair kernel in its stream-K form (split == 1)
+  int sk_pairs = 0, sk_dp_tiles = 0, sk_tiles = 0, sk_tiles_per_batch = 0;
+  size_t off_sk = 0;  // [sk_pairs partial tiles][sk_pairs x 16 ready flags]
   bool a_shared = false, b_shared = false;  // batch > 1 with a zero batch stride
   int act = 0;                              // TILEC_MM_ACT_*
   size_t off_a = 0, off_b = 0, off_slabs = 0;
@@ -290,19 +331,57 @@ double cta_seconds(int64_t rows, int64_t cols, int64_t b_cols, int64_t K, double
 // FMA ~0.31; HBM share ~38 GB/s per SM with every SM streaming.
 constexpr double kRate3x = 1.7e12, kRateTf32 = 4.3e12, kRateSimt = 0.31e12, kBwPerSm = 38.0e9;
 
+// Stream-K form of the pair kernel (Plan::sk).  T tiles on P pair slots take ceil(T / P)
+// waves of tile-times as one pair per tile, and T / P tile-times as stream-K, times a
+// per-k-block penalty measured on B200 at 2048^3 (all 148 SMs streaming their own k
+// offsets run 6 % slower per k-block in 3XTF32 than 128 SMs in lockstep, 17 % in the
+// L2-bound TF32), plus ~5 us for the partial tiles' round trip and the flag reset.  Chosen,
+// unless `forced`, when that is at least 3 % faster, every tile has at most three pairs
+// (T >= P / 2) and K has at least 8 blocks.  The tiles of all waves but the last complete
+// one stay one per pair (sk_dp_tiles); the rest, P to 2P - 1 tiles, are shared out.
+constexpr size_t kPartialBytes = size_t(Tc2Cfg<256, kPairStages, true, true>::kPartialFloats) * sizeof(float);
+constexpr int kSkFlagsPerPair = 2 * Tc2Cfg<256, kPairStages, true, true>::kEpiWarps;
+
+void plan_stream_k(const DeviceInfo& d, int64_t M, int64_t N, int64_t K, int64_t nb, int bk, double cta_s,
+                   bool forced, Plan* p) {
+  const int64_t P = d.pair_slots;
+  if (P <= 0) return;
+  const int64_t per_batch = cdiv(M, 256) * cdiv(N, 256);
+  const int64_t T = per_batch * nb, nkb = cdiv(K, bk);
+  if (T >= (int64_t(1) << 30)) return;
+  if (!forced) {
+    if (nkb < 8 || 2 * T < P) return;
+    const double penalty = bk == 32 ? 1.17 : 1.08;
+    const double dp = double(cdiv(T, P)) * cta_s;
+    const double sk = double(T) / double(P) * cta_s * penalty + 5.0e-6;
+    if (!(sk < 0.97 * dp)) return;
+  }
+  const int64_t dp_tiles = T >= 2 * P ? (T / P - 1) * P : 0;
+  const int64_t units = (T - dp_tiles) * nkb;  // >= P whenever dp_tiles > 0
+  if (units * P >= (int64_t(1) << 31)) return;  // the kernel's share arithmetic is 32-bit
+  p->sk = true;
+  p->split = 1;
+  p->k_chunk = round_up(K, bk);
+  p->sk_pairs = static_cast<int>(units < P ? units : P);
+  p->sk_dp_tiles = static_cast<int>(dp_tiles);
+  p->sk_tiles = static_cast<int>(T);
+  p->sk_tiles_per_batch = static_cast<int>(per_batch);
+}
+
 int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Plan* p) {
   const int64_t M = q.M, N = q.N, K = q.K, nb = q.batch;
   int variant = cfg ? cfg->variant : TILEC_MM_AUTO;
   int requested_split = cfg ? cfg->split_k : 0;
   const int flags = cfg ? cfg->flags : 0;
   const int act = cfg ? cfg->activation : 0;
-  if (flags & ~(TILEC_MM_TRANS_A | TILEC_MM_TRANS_B)) return TILEC_ERR_BAD_ARG;
+  if (flags & ~(TILEC_MM_TRANS_A | TILEC_MM_TRANS_B | TILEC_MM_STREAM_K)) return TILEC_ERR_BAD_ARG;
+  const bool want_sk = (flags & TILEC_MM_STREAM_K) != 0;
   if (act < TILEC_MM_ACT_NONE || act > TILEC_MM_ACT_GELU) return TILEC_ERR_BAD_ARG;
   if (cfg) {
     for (int i = 0; i < 4; ++i)
       if (cfg->reserved[i] != 0) return TILEC_ERR_BAD_ARG;
   }
-  p->flags = flags;
+  p->flags = flags & (TILEC_MM_TRANS_A | TILEC_MM_TRANS_B);
   p->act = act;
   p->a_shared = nb > 1 && q.stride_a == 0;
   p->b_shared = nb > 1 && q.stride_b == 0;
@@ -336,6 +415,8 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
     p->k_chunk = round_up(cdiv(K, p->split), bk);
     p->split = static_cast<int>(cdiv(K, p->k_chunk > 0 ? p->k_chunk : 1));
     if (p->split < 1) p->split = 1;
+    if (p->pair && K > 0 && requested_split <= 1 && (want_sk || (requested_split == 0 && p->split == 1)))
+      plan_stream_k(d, M, N, K, nb, bk, cta_s, want_sk, p);
   } else {
     p->bn = N <= 64 ? 64 : 128;
     const int64_t tiles = cdiv(M, kSimtBM) * cdiv(N, p->bn) * nb;
@@ -368,6 +449,11 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
   }
   p->off_slabs = off;
   if (p->split > 1) off += size_t(nb) * size_t(p->split) * size_t(M) * size_t(p->ldw) * sizeof(float);
+  if (p->sk) {
+    off = align256(off);
+    p->off_sk = off;
+    off += size_t(p->sk_pairs) * (kPartialBytes + kSkFlagsPerPair * sizeof(int));
+  }
   p->ws_bytes = off;
   return TILEC_OK;
 }
@@ -533,6 +619,26 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t 
   };
   return L.layout ? go(tc2_gemm_kernel<256, kPairStages, SPLIT3, HI, true>)
                   : go(tc2_gemm_kernel<256, kPairStages, SPLIT3, HI, false>);
+}
+
+// Stream-K form: the flag reset (programmatic serialisation on both sides, so the GEMM's
+// set-up still overlaps the previous kernel) and a grid of `pairs` pairs.
+template <bool SPLIT3, bool HI>
+int launch_tc2_sk(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
+                  const Tc2StreamK& sk, int pairs, cudaStream_t s) {
+  int rc = launch_k(sk_flags_reset_kernel, dim3(1), dim3(256), 0, s, 1, sk.flags, pairs * kSkFlagsPerPair);
+  if (rc) return rc;
+  using Cfg = Tc2Cfg<256, kPairStages, SPLIT3, true>;
+  const int mp_tiles = static_cast<int>(cdiv(M, 256));
+  const int n_tiles = static_cast<int>(cdiv(N, 256));
+  const int group_m = 8;
+  auto go = [&](auto kern) {
+    return launch_k(kern, dim3(static_cast<unsigned>(2 * pairs)), dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 2, ma,
+                    mb, L.out, static_cast<int>(M), static_cast<int>(N), L.ldo, static_cast<int>(K), mp_tiles,
+                    n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias, L.act, L.shared, sk);
+  };
+  return L.layout ? go(tc2_sk_kernel<256, kPairStages, SPLIT3, HI, true>)
+                  : go(tc2_sk_kernel<256, kPairStages, SPLIT3, HI, false>);
 }
 
 template <bool SPLIT3, bool HI>
@@ -827,7 +933,17 @@ int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, vo
     const int bk = p.variant == TILEC_MM_TF32 ? 32 : k3xBK;
     rc = encode_maps(A, B, M, N, K, lda, ldb, sa, na, sb, nbb, bk, L.layout, p.pair ? 128 : p.bn, &ma, &mb);
     if (rc) return rc;
-    if (p.pair)
+    if (p.sk) {
+      Tc2StreamK sk{};
+      sk.partial = reinterpret_cast<float*>(wsb + p.off_sk);
+      sk.flags = reinterpret_cast<int*>(wsb + p.off_sk + size_t(p.sk_pairs) * kPartialBytes);
+      sk.dp_tiles = p.sk_dp_tiles;
+      sk.tiles = p.sk_tiles;
+      sk.tiles_per_batch = p.sk_tiles_per_batch;
+      rc = p.variant == TILEC_MM_TF32     ? launch_tc2_sk<false, false>(ma, mb, M, N, K, L, sk, p.sk_pairs, s)
+           : p.variant == TILEC_MM_3XTF32 ? launch_tc2_sk<true, false>(ma, mb, M, N, K, L, sk, p.sk_pairs, s)
+                                          : launch_tc2_sk<true, true>(ma, mb, M, N, K, L, sk, p.sk_pairs, s);
+    } else if (p.pair)
       rc = p.variant == TILEC_MM_TF32     ? launch_tc2<false, false>(ma, mb, M, N, K, L, s)
            : p.variant == TILEC_MM_3XTF32 ? launch_tc2<true, false>(ma, mb, M, N, K, L, s)
                                           : launch_tc2<true, true>(ma, mb, M, N, K, L, s);
@@ -944,7 +1060,7 @@ int tilec_mm_plan(const float* A, const float* B, const float* C, int64_t M, int
   std::memset(out, 0, sizeof(*out));
   out->variant = p.variant;
   out->split_k = p.split;
-  out->flags = p.flags;
+  out->flags = p.flags | (p.sk ? TILEC_MM_STREAM_K : 0);
   out->activation = p.act;
   return TILEC_OK;
 }

@@ -115,12 +115,14 @@ def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k, flags=0):
     return out
 
 
-def _matrix_mul(x1, x2, variant=None, split_k=0, out=None):
+def _matrix_mul(x1, x2, variant=None, split_k=0, out=None, stream_k=False):
     """matrix_mul with explicit kernel choice.
 
     variant: None (= $TILEC_MM_VARIANT or "auto"), "simt", "splitk", "tf32", "3xtf32",
-    "3xtf32_masked".  split_k: K slices for split variants (0 = library choice).
-    out: optional preallocated [M, N] float32 result (unit column stride).
+    "3xtf32_masked".  split_k: K slices for split variants (0 = library choice; 1 = none,
+    which also rules out stream-K).  stream_k: run the CTA-pair kernel in its stream-K form
+    whenever it is the kernel and split_k <= 1 (the library picks it by itself where it
+    pays).  out: optional preallocated [M, N] float32 result (unit column stride).
     """
     M, K = x1.shape
     K2, N = x2.shape
@@ -142,7 +144,7 @@ def _matrix_mul(x1, x2, variant=None, split_k=0, out=None):
         ldc = _check_out(out, M, N, x1.device)
     if M == 0 or N == 0:
         return out
-    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0)
+    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0) | (_native.STREAM_K if stream_k else 0)
     return _launch(a, lda, b, ldb, out, ldc, M, N, K, variant or _default_variant(), split_k, flags)
 
 
@@ -170,7 +172,7 @@ def _batched_operand(x):
     return x, max(c, 1), False, r * c, nb
 
 
-def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, split_k=0):
+def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, split_k=0, stream_k=False):
     """act(x1 @ x2 + bias), batched: the fused, batched form of matrix_mul.
 
     x1 [M, K] or [B, M, K]; x2 [K, N] or [B, K, N] (a 2-D operand is shared by every
@@ -179,6 +181,8 @@ def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, sp
     [M, N] or [B, M, N].  One library call (tilec_mm_f32_ex): the batch is a grid dimension
     of the kernels and the epilogue runs where C is stored.  Row views and column views
     (.t() / .transpose(-1, -2)) of each slice are read in place, as in matrix_mul.
+    variant / split_k / stream_k as in _matrix_mul (stream-K shares out the tiles of the
+    whole batch).
     """
     _check_operand(x1)
     _check_operand(x2)
@@ -212,7 +216,7 @@ def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, sp
     nbatch = 1 if nb is None else nb
     if nbatch > 1 and sc < (M - 1) * ldc + N:
         raise ValueError("matrix_mul_ex: the batches of out overlap")
-    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0)
+    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0) | (_native.STREAM_K if stream_k else 0)
     lib = _native.load()
     from . import select
     select.ensure_installed()
@@ -230,8 +234,9 @@ def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, sp
     return out
 
 
-def plan(x1, x2, variant=None, split_k=0):
-    """The (variant name, split_k) that matrix_mul would launch for these operands."""
+def plan(x1, x2, variant=None, split_k=0, stream_k=False, detail=False):
+    """The (variant name, split_k) that matrix_mul would launch for these operands; with
+    detail=True a dict that also says whether the pair kernel runs in its stream-K form."""
     M, K = x1.shape
     _, N = x2.shape
     a, lda, ta = _operand(x1)
@@ -239,14 +244,17 @@ def plan(x1, x2, variant=None, split_k=0):
     lib = _native.load()
     from . import select
     select.ensure_installed()
-    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0)
+    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0) | (_native.STREAM_K if stream_k else 0)
     cfg = _native.make_cfg(variant or _default_variant(), split_k, flags)
     res = _native.MMConfig()
     with torch.cuda.device(x1.device):
         rc = lib.tilec_mm_plan(a.data_ptr(), b.data_ptr(), None, M, N, K, lda, ldb, max(N, 1),
                                ctypes.byref(cfg), ctypes.byref(res))
     _native.check(rc, "tilec_mm_plan")
-    return _native.VARIANT_NAMES.get(res.variant, res.variant), res.split_k
+    name = _native.VARIANT_NAMES.get(res.variant, res.variant)
+    if detail:
+        return {"variant": name, "split_k": res.split_k, "stream_k": bool(res.flags & _native.STREAM_K)}
+    return name, res.split_k
 
 
 def mm_configs(M, K, N):
