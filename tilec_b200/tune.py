@@ -270,7 +270,8 @@ def pick(M, K, N):
     return ext.plan(a, b)
 
 
-def run(shape, variant="auto", split=0, reps=3, seed=0):
+def run(shape, variant="auto", split=0, reps=3, seed=0, stream_k=False):
+    """`reps` launches of one product (for profilers); prints the plan that ran."""
     import torch
     from . import ext
     m, k, n = shape
@@ -279,9 +280,10 @@ def run(shape, variant="auto", split=0, reps=3, seed=0):
     b = torch.randn(k, n, device="cuda", generator=g)
     c = torch.empty(m, n, device="cuda")
     for _ in range(reps):
-        ext._matrix_mul(a, b, variant=variant, split_k=split, out=c)
+        ext._matrix_mul(a, b, variant=variant, split_k=split, out=c, stream_k=stream_k)
     torch.cuda.synchronize()
-    print(json.dumps({"shape": [m, k, n], "plan": ext.plan(a, b, variant=variant, split_k=split), "reps": reps}))
+    plan = ext.plan(a, b, variant=variant, split_k=split, stream_k=stream_k, detail=True)
+    print(json.dumps({"shape": [m, k, n], "plan": plan, "reps": reps}))
 
 
 def main(argv=None):
@@ -299,13 +301,15 @@ def main(argv=None):
     pr.add_argument("--variant", default="auto")
     pr.add_argument("--split", type=int, default=0)
     pr.add_argument("--reps", type=int, default=3)
+    pr.add_argument("--stream-k", action="store_true", help="ask for the pair kernel's stream-K form")
     args = p.parse_args(argv)
     if args.cmd == "bench":
         bench(args.shapes, args.csv, args.seed)
     elif args.cmd == "train":
         train(args.csv, args.out)
     else:
-        run(tuple(int(x) for x in args.shape.split(",")), args.variant, args.split, args.reps)
+        run(tuple(int(x) for x in args.shape.split(",")), args.variant, args.split, args.reps,
+            stream_k=args.stream_k)
 
 
 if __name__ == "__main__":
