@@ -8,13 +8,16 @@
 //
 // B200 mapping:
 //   * CTA tile 128 x BN x 16 (BN = 128 or 64), 256 threads, each thread an 8 x (BN/16)
-//     register block (2-D register blocking, 64 or 32 FFMA per k).
-//   * 4-stage cp.async pipeline global -> shared.  16-byte copies when rows are 16-byte
-//     aligned (VEC), 4-byte copies otherwise; the tail of a ragged tile is zero-filled
-//     by cp.async's src-size operand, so no out-of-range address is ever read.
-//   * Shared tiles are unpadded: A as [128][16] (k fastest), B as [16][BN].  A thread
-//     owns rows tm + 16*i, so the two row indices a warp touches per A load are
-//     adjacent and land in different banks; B loads are contiguous float4 runs.
+//     register block (2-D register blocking, 64 or 32 FFMA per k), at most 128 registers
+//     so that two CTAs (16 warps) share an SM.
+//   * 4-stage cp.async pipeline global -> shared; the tail of a ragged tile is
+//     zero-filled by cp.async's src-size operand, so no out-of-range address is read.
+//   * Both shared tiles are k-major: A as [16][128 + 4] (transposed on the way in by
+//     4-byte copies; a warp copies 4 rows x 8 k, 32-byte runs of global memory, and the
+//     pitch of 132 puts its 32 stores in 32 banks), B as [16][BN] (16-byte copies when
+//     rows are 16-byte aligned, VEC; 4-byte otherwise).  A thread owns the 8 consecutive
+//     rows tm*8.. and reads them at one k with two 16-byte loads, as it reads its B
+//     columns: 4 shared loads per 64 FFMA and only 16 operand registers live.
 //   * Split-K (gridDim.z = S > 1): CTA z covers K range [z*k_chunk, min(K,(z+1)*k_chunk))
 //     and writes its partial tile to slab z of the workspace; splitk_reduce_kernel
 //     sums the slabs in z order (deterministic).
@@ -28,78 +31,94 @@ constexpr int kSimtBM = 128;
 constexpr int kSimtBK = 16;
 constexpr int kSimtStages = 4;
 constexpr int kSimtThreads = 256;
+constexpr int kSimtAPitch = kSimtBM + 4;  // floats per k row of the k-major A tile
 
 template <int BN>
 constexpr int simt_smem_bytes() {
-  return kSimtStages * (kSimtBM * kSimtBK + kSimtBK * BN) * 4;
+  return kSimtStages * (kSimtBK * kSimtAPitch + kSimtBK * BN) * 4;
 }
+// Dynamic shared memory asked for by grids of at most one CTA per SM: more than half of an
+// SM's 228 KB, so the block scheduler cannot place two such CTAs on one SM.
+constexpr int kSimtSpreadSmem = 120 * 1024;
+static_assert(simt_smem_bytes<128>() <= kSimtSpreadSmem, "spread request covers the tiles");
 
+// Per-thread copy plan of the SIMT tiles, fixed for the CTA, so that a tile costs one
+// pointer step per operand:
+//   A (4-byte copies, transposed to k-major): k = a_k of rows a_row + 16 j, j < 8; in a
+//     warp, lane = 8 * (row % 4) + k % 8 over a block of 4 rows x 8 k (32-byte runs of
+//     global memory; with the 132-float pitch the 32 shared stores hit 32 banks).
+//   B: 16-byte chunk (VEC) or element b_n of rows b_row + kBRowStep * i.
+// Out-of-range elements are zero-filled through cp.async's src-size operand, with the
+// operand's base address as the (unread) source.
 template <int BN, bool VEC>
-__device__ __forceinline__ void simt_load_tile(float* as, float* bs, const float* __restrict__ A,
-                                               const float* __restrict__ B, int64_t M, int64_t N, int64_t lda,
-                                               int64_t ldb, int64_t m0, int64_t n0, int64_t k0, int64_t k_end,
-                                               int tid) {
-  if constexpr (VEC) {
-    // A: 128 rows x 16 k = 512 float4 chunks, 2 per thread.
+struct SimtCopy {
+  static constexpr int kAPerThread = kSimtBM * kSimtBK / kSimtThreads;
+  static constexpr int kBPerRow = VEC ? BN / 4 : BN;  // copies per B row
+  static constexpr int kBPerThread = kSimtBK * kBPerRow / kSimtThreads;
+  static constexpr int kBRowStep = kSimtThreads / kBPerRow;
+  static_assert(kSimtThreads % kBPerRow == 0 && kAPerThread == 8, "copy plan");
+  const float* a_src;  // A + (m0 + a_row) * lda + a_k
+  const float* b_src;  // B + b_row * ldb + n0 + b_n
+  int64_t a_step;      // 16 rows of A
+  int64_t b_step;      // kBRowStep rows of B
+  int64_t ldb;
+  int a_dst, b_dst;    // shared offsets within a stage
+  int a_k, b_row;
+  uint32_t a_rows_ok;  // bit j: row a_row + 16 j is below M
+  uint32_t b_bytes;    // per B copy: 16 or fewer at a ragged N edge (VEC), 4 or 0 (scalar)
+
+  __device__ __forceinline__ SimtCopy(const float* A, const float* B, int64_t M, int64_t N, int64_t lda,
+                                      int64_t ldb_, int64_t m0, int64_t n0, int tid) {
+    const int lane = tid & 31, warp = tid >> 5;
+    const int a_row = 4 * (warp >> 1) + (lane >> 3);
+    a_k = 8 * (warp & 1) + (lane & 7);
+    a_dst = a_k * kSimtAPitch + a_row;
+    a_src = A + (m0 + a_row) * lda + a_k;
+    a_step = 16 * lda;
+    a_rows_ok = 0;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int c = tid + i * kSimtThreads;
-      const int row = c >> 2;
-      const int kq = (c & 3) * 4;
-      const int64_t gm = m0 + row, gk = k0 + kq;
-      uint32_t bytes = 0;
-      const float* src = A;
-      if (gm < M && gk < k_end) {
-        const int64_t rem = k_end - gk;
-        bytes = static_cast<uint32_t>(rem >= 4 ? 16 : rem * 4);
-        src = A + gm * lda + gk;
-      }
-      cp_async_16(as + row * kSimtBK + kq, src, bytes);
+    for (int j = 0; j < kAPerThread; ++j)
+      if (m0 + a_row + 16 * j < M) a_rows_ok |= 1u << j;
+    b_row = tid / kBPerRow;
+    const int b_n = (tid % kBPerRow) * (VEC ? 4 : 1);
+    b_dst = b_row * BN + b_n;
+    b_src = B + b_row * ldb_ + n0 + b_n;
+    b_step = kBRowStep * ldb_;
+    ldb = ldb_;
+    const int64_t rem = N - (n0 + b_n);
+    if constexpr (VEC)
+      b_bytes = rem >= 4 ? 16u : (rem > 0 ? static_cast<uint32_t>(rem) * 4u : 0u);
+    else
+      b_bytes = rem > 0 ? 4u : 0u;
+  }
+
+  // Copies the tile at k0 (rows of A and B beyond k_end read as zero) into as / bs.
+  __device__ __forceinline__ void load(float* as, float* bs, const float* A, const float* B, int64_t k0,
+                                       int64_t k_end) const {
+    const bool ka = k0 + a_k < k_end;
+    const float* pa = a_src + k0;
+#pragma unroll
+    for (int j = 0; j < kAPerThread; ++j) {
+      const bool ok = ka && ((a_rows_ok >> j) & 1u);
+      cp_async_4(as + a_dst + 16 * j, ok ? pa + j * a_step : A, ok ? 4u : 0u);
     }
-    // B: 16 rows x BN cols = 4*BN float4 chunks.
-    constexpr int kChunksPerRow = BN / 4;
+    const float* pb = b_src + k0 * ldb;
 #pragma unroll
-    for (int i = 0; i < (kSimtBK * BN / 4) / kSimtThreads; ++i) {
-      const int c = tid + i * kSimtThreads;
-      const int row = c / kChunksPerRow;
-      const int nq = (c % kChunksPerRow) * 4;
-      const int64_t gk = k0 + row, gn = n0 + nq;
-      uint32_t bytes = 0;
-      const float* src = B;
-      if (gk < k_end && gn < N) {
-        const int64_t rem = N - gn;
-        bytes = static_cast<uint32_t>(rem >= 4 ? 16 : rem * 4);
-        src = B + gk * ldb + gn;
-      }
-      cp_async_16(bs + row * BN + nq, src, bytes);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < (kSimtBM * kSimtBK) / kSimtThreads; ++i) {
-      const int e = tid + i * kSimtThreads;
-      const int row = e >> 4;
-      const int kk = e & 15;
-      const int64_t gm = m0 + row, gk = k0 + kk;
-      const bool ok = gm < M && gk < k_end;
-      cp_async_4(as + row * kSimtBK + kk, ok ? A + gm * lda + gk : A, ok ? 4u : 0u);
-    }
-#pragma unroll
-    for (int i = 0; i < (kSimtBK * BN) / kSimtThreads; ++i) {
-      const int e = tid + i * kSimtThreads;
-      const int row = e / BN;
-      const int nn = e % BN;
-      const int64_t gk = k0 + row, gn = n0 + nn;
-      const bool ok = gk < k_end && gn < N;
-      cp_async_4(bs + row * BN + nn, ok ? B + gk * ldb + gn : B, ok ? 4u : 0u);
+    for (int i = 0; i < kBPerThread; ++i) {
+      const bool ok = b_bytes != 0 && k0 + b_row + kBRowStep * i < k_end;
+      if constexpr (VEC)
+        cp_async_16(bs + b_dst + kBRowStep * i * BN, ok ? pb + i * b_step : B, ok ? b_bytes : 0u);
+      else
+        cp_async_4(bs + b_dst + kBRowStep * i * BN, ok ? pb + i * b_step : B, ok ? 4u : 0u);
     }
   }
-}
+};
 
 // out/ldo: C (one K slice) or the split-K workspace (slab z at out + z*out_slab).
 // blockIdx.z = batch * splits + K slice; batch b reads A + b*stride_a, B + b*stride_b and
 // writes out + b*out_batch.  bias / act: fused epilogue (only when writing C directly).
 template <int BN, bool VEC>
-__global__ void __launch_bounds__(kSimtThreads, 1)
+__global__ void __launch_bounds__(kSimtThreads, 2)
     simt_gemm_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ out,
                      int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldo, int64_t out_slab,
                      int64_t k_chunk, int vec_out, int splits, int64_t stride_a, int64_t stride_b,
@@ -107,7 +126,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1)
   constexpr int TN = BN / 16;  // columns per thread: 8 (two float4 groups 64 apart) or 4
   extern __shared__ __align__(16) float smem[];
   float* As = smem;
-  float* Bs = smem + kSimtStages * kSimtBM * kSimtBK;
+  float* Bs = smem + kSimtStages * kSimtBK * kSimtAPitch;
 
   pdl_wait();
   if (blockDim.x != kSimtThreads) {
@@ -125,6 +144,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1)
   const int64_t k_end = (k_begin + k_chunk < K) ? k_begin + k_chunk : K;
   const int64_t nkt = (k_end > k_begin) ? (k_end - k_begin + kSimtBK - 1) / kSimtBK : 0;
   out += kslice * out_slab + batch * out_batch;
+  const SimtCopy<BN, VEC> copy(A, B, M, N, lda, ldb, m0, n0, tid);
 
   const int tm = tid >> 4;
   const int tn = tid & 15;
@@ -138,8 +158,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1)
 #pragma unroll
   for (int s = 0; s < kSimtStages - 1; ++s) {
     if (s < nkt)
-      simt_load_tile<BN, VEC>(As + s * kSimtBM * kSimtBK, Bs + s * kSimtBK * BN, A, B, M, N, lda, ldb, m0, n0,
-                              k_begin + s * kSimtBK, k_end, tid);
+      copy.load(As + s * kSimtBK * kSimtAPitch, Bs + s * kSimtBK * BN, A, B, k_begin + s * kSimtBK, k_end);
     cp_async_commit();
   }
 
@@ -149,37 +168,29 @@ __global__ void __launch_bounds__(kSimtThreads, 1)
     const int64_t nt = kt + kSimtStages - 1;
     if (nt < nkt) {
       const int ns = static_cast<int>(nt % kSimtStages);
-      simt_load_tile<BN, VEC>(As + ns * kSimtBM * kSimtBK, Bs + ns * kSimtBK * BN, A, B, M, N, lda, ldb, m0,
-                              n0, k_begin + nt * kSimtBK, k_end, tid);
+      copy.load(As + ns * kSimtBK * kSimtAPitch, Bs + ns * kSimtBK * BN, A, B, k_begin + nt * kSimtBK, k_end);
     }
     cp_async_commit();
 
     const int cs = static_cast<int>(kt % kSimtStages);
-    const float* as = As + cs * kSimtBM * kSimtBK;
-    const float* bs = Bs + cs * kSimtBK * BN;
+    const float* as = As + cs * kSimtBK * kSimtAPitch + tm * 8;
+    const float* bs = Bs + cs * kSimtBK * BN + tn * 4;
 #pragma unroll
-    for (int kq = 0; kq < kSimtBK / 4; ++kq) {
-      float4 a4[8];
+    for (int k = 0; k < kSimtBK; ++k) {
+      const float4 a0 = *reinterpret_cast<const float4*>(as + k * kSimtAPitch);
+      const float4 a1 = *reinterpret_cast<const float4*>(as + k * kSimtAPitch + 4);
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      float b[TN];
+      const float4 b0 = *reinterpret_cast<const float4*>(bs + k * BN);
+      b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
+      if constexpr (TN == 8) {
+        const float4 b1 = *reinterpret_cast<const float4*>(bs + k * BN + 64);
+        b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        a4[i] = *reinterpret_cast<const float4*>(as + (tm + 16 * i) * kSimtBK + kq * 4);
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const float* brow = bs + (kq * 4 + kk) * BN;
-        float b[TN];
-        const float4 b0 = *reinterpret_cast<const float4*>(brow + tn * 4);
-        b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
-        if constexpr (TN == 8) {
-          const float4 b1 = *reinterpret_cast<const float4*>(brow + 64 + tn * 4);
-          b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float a = kk == 0 ? a4[i].x : kk == 1 ? a4[i].y : kk == 2 ? a4[i].z : a4[i].w;
-#pragma unroll
-          for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a, b[j], acc[i][j]);
-        }
-      }
+        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
     }
   }
   cp_async_wait<0>();
@@ -201,7 +212,7 @@ __global__ void __launch_bounds__(kSimtThreads, 1)
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int64_t gm = m0 + tm + 16 * i;
+    const int64_t gm = m0 + tm * 8 + i;
     if (gm >= M) continue;
     float* crow = out + gm * ldo;
 #pragma unroll

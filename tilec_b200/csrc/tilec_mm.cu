@@ -90,14 +90,15 @@ cudaError_t init_device_attrs() {
   auto acc = [&](cudaError_t x) {
     if (e == cudaSuccess && x != cudaSuccess) e = x;
   };
+  // Up to kSimtSpreadSmem: small grids ask for that much to keep to one CTA per SM.
   acc(cudaFuncSetAttribute(simt_gemm_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           simt_smem_bytes<128>()));
+                           kSimtSpreadSmem));
   acc(cudaFuncSetAttribute(simt_gemm_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           simt_smem_bytes<128>()));
+                           kSimtSpreadSmem));
   acc(cudaFuncSetAttribute(simt_gemm_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           simt_smem_bytes<64>()));
+                           kSimtSpreadSmem));
   acc(cudaFuncSetAttribute(simt_gemm_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           simt_smem_bytes<64>()));
+                           kSimtSpreadSmem));
   acc(set_tc_attr<256, 32, TcShape<256>::kTf32Stages, false, false>());
   acc(set_tc_attr<128, 32, TcShape<128>::kTf32Stages, false, false>());
   acc(set_tc_attr<64, 32, TcShape<64>::kTf32Stages, false, false>());
@@ -825,14 +826,19 @@ int launch_fill_zero(float* C, int64_t M, int64_t N, int64_t ldc, int64_t batche
 // grid: (M tiles, N tiles, batches * L.split).  A / B advance by stride_a / stride_b per
 // batch (0 = shared).
 int launch_simt(int bn, bool vec, dim3 grid, const float* A, const float* B, int64_t M, int64_t N, int64_t K,
-                int64_t lda, int64_t ldb, int64_t stride_a, int64_t stride_b, const Launch& L, cudaStream_t s) {
-  // Launched without programmatic serialisation: a SIMT CTA fits twice on an SM, and CTAs
+                int64_t lda, int64_t ldb, int64_t stride_a, int64_t stride_b, const Launch& L, int sms,
+                cudaStream_t s) {
+  // Launched without programmatic serialisation: two SIMT CTAs fit on an SM, and CTAs
   // placed while the previous kernel still occupies the GPU were measured to double up on
-  // some SMs (a 128-CTA grid ran 40% slower).
+  // some SMs (a 128-CTA grid ran 40% slower).  For the same reason a grid of at most one
+  // CTA per SM asks for more than half an SM's shared memory, so that no SM takes two
+  // (B200, config 1 as SPLITK, 148 CTAs: 12.2 us with two allowed, 11.6 us spread).
   const dim3 block(kSimtThreads);
+  const bool spread = int64_t(grid.x) * grid.y * grid.z <= sms;
   auto go = [&](auto kern, size_t smem) {
-    return launch_kx(false, kern, grid, block, smem, s, 1, A, B, L.out, M, N, K, lda, ldb, L.ldo, L.out_slab,
-                     L.k_chunk, L.vec_out, L.split, stride_a, stride_b, L.out_batch, L.bias, L.act);
+    return launch_kx(false, kern, grid, block, spread ? size_t(kSimtSpreadSmem) : smem, s, 1, A, B, L.out, M, N,
+                     K, lda, ldb, L.ldo, L.out_slab, L.k_chunk, L.vec_out, L.split, stride_a, stride_b,
+                     L.out_batch, L.bias, L.act);
   };
   if (bn == 64)
     return vec ? go(simt_gemm_kernel<64, true>, simt_smem_bytes<64>())
@@ -927,7 +933,7 @@ int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, vo
     const int64_t mt = cdiv(M, kSimtBM), nt = cdiv(N, p.bn);
     if (nt > 65535 || nb * p.split > 65535) return TILEC_ERR_UNSUPPORTED;
     const dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(nb * p.split));
-    rc = launch_simt(p.bn, vec, grid, A, B, M, N, K, lda, ldb, sa, sb, L, s);
+    rc = launch_simt(p.bn, vec, grid, A, B, M, N, K, lda, ldb, sa, sb, L, d.sms, s);
   } else {
     CUtensorMap ma, mb;
     const int bk = p.variant == TILEC_MM_TF32 ? 32 : k3xBK;
@@ -1222,7 +1228,7 @@ extern "C" int tilec_mm_f32_splitk_noalloc(const float* A, const float* B, float
   L.k_chunk = k_chunk;
   const bool vec = aligned16(A) && aligned16(B) && (lda % 4 == 0) && (ldb % 4 == 0);
   dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(split));
-  rc = launch_simt(bn, vec, grid, A, B, M, N, K, lda, ldb, 0, 0, L, s);
+  rc = launch_simt(bn, vec, grid, A, B, M, N, K, lda, ldb, 0, 0, L, d->sms, s);
   if (rc || split == 1) return rc;
   Reduce r;
   r.ws = scratch;
