@@ -16,9 +16,11 @@
 // lower-numbered pairs sharing the tile, in pair order (a fixed order: results do not
 // depend on timing), then stores the tile with the fused epilogue.  A pair visits its
 // stream-K tiles last one first, so its one partial is its first piece of work: a wait is
-// only ever on a lower-numbered pair, for the work it started with, and every pair is
-// resident (the host launches no more than the resident slots), so waits end.  Every wait
-// is bounded all the same (kWaitLimitNs, then TILEC_DEV_TIMEOUT and an orderly unwind).
+// only ever on a lower-numbered pair, for the work it started with.  The host launches no
+// more pairs than fit at once; and should other kernels hold SMs (another stream), a
+// resident pair still only waits on lower-numbered pairs, which the block scheduler has
+// placed no later than it, so waits end either way.  Every wait is bounded all the same
+// (kWaitLimitNs, then TILEC_DEV_TIMEOUT and an orderly unwind).
 //
 // Roles, barriers, TMEM and the hi/lo split are those of tc2_gemm_kernel (see there).
 #pragma once
