@@ -627,3 +627,29 @@ def test_stream_k_batched_fused(act):
     shared = ext.matrix_mul_ex(a, b[0], bias=bias, activation=act, stream_k=True)
     assert _rel(shared[2], _ref64(a[2], b[0], bias, act)) <= 1e-5
     assert _status_clean()
+
+
+def test_stream_k_concurrent_streams():
+    """Two streams run stream-K products at the same time, so the pairs of one launch
+    compete for SMs with the other's: a pair waits only on lower-numbered pairs, which the
+    block scheduler places first, so every launch completes (no bounded wait runs out) and
+    each result equals the same product run alone, bit for bit."""
+    g = torch.Generator(device=DEV).manual_seed(23)
+    shapes = [(2304, 2048, 2304), (2560, 1024, 2560)]
+    ins = [(torch.randn(m, k, device=DEV, generator=g), torch.randn(k, n, device=DEV, generator=g))
+           for (m, k, n) in shapes]
+    alone = [ext._matrix_mul(a, b, variant="3xtf32", stream_k=True) for a, b in ins]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(device=DEV) for _ in ins]
+    outs = [[torch.empty_like(r) for _ in range(4)] for r in alone]
+    for s in streams:
+        s.wait_stream(torch.cuda.current_stream())
+    for rep in range(4):
+        for i, ((a, b), s) in enumerate(zip(ins, streams)):
+            with torch.cuda.stream(s):
+                ext._matrix_mul(a, b, variant="3xtf32", stream_k=True, out=outs[i][rep])
+    torch.cuda.synchronize()
+    assert _status_clean()
+    for r, os_ in zip(alone, outs):
+        for o in os_:
+            assert torch.equal(o, r)
