@@ -44,41 +44,46 @@ static_assert(simt_smem_bytes<128>() <= kSimtSpreadSmem, "spread request covers 
 
 // Per-thread copy plan of the SIMT tiles, fixed for the CTA, so that a tile costs one
 // pointer step per operand:
-//   A (4-byte copies, transposed to k-major): k = a_k of rows a_row + 16 j, j < 8; in a
-//     warp, lane = 8 * (row % 4) + k % 8 over a block of 4 rows x 8 k (32-byte runs of
-//     global memory; with the 132-float pitch the 32 shared stores hit 32 banks).
+//   A (4-byte copies, transposed to k-major): blocks of 4 rows x 8 k, lane = 8 * (row % 4)
+//     + k % 8 (32-byte runs of global memory; with the 132-float pitch, which is 4 mod 32,
+//     the warp's 32 shared stores hit 32 banks).  Copy j of warp w is block 8 j + w: k
+//     group (8 j + w) % G = w % G of the G = BK / 8, so a thread always copies the same k
+//     a_k, of rows a_row + (32 / G) j.
 //   B: 16-byte chunk (VEC) or element b_n of rows b_row + kBRowStep * i.
 // Out-of-range elements are zero-filled through cp.async's src-size operand, with the
 // operand's base address as the (unread) source.
 template <int BN, bool VEC>
 struct SimtCopy {
   static constexpr int kAPerThread = kSimtBM * kSimtBK / kSimtThreads;
-  static constexpr int kBPerRow = VEC ? BN / 4 : BN;  // copies per B row
+  static constexpr int kKGroups = kSimtBK / 8;            // G
+  static constexpr int kARowStep = 4 * (8 / kKGroups);    // rows between a thread's copies
+  static constexpr int kBPerRow = VEC ? BN / 4 : BN;      // copies per B row
   static constexpr int kBPerThread = kSimtBK * kBPerRow / kSimtThreads;
   static constexpr int kBRowStep = kSimtThreads / kBPerRow;
-  static_assert(kSimtThreads % kBPerRow == 0 && kAPerThread == 8, "copy plan");
+  static_assert(kSimtBK % 8 == 0 && 8 % kKGroups == 0 && kAPerThread <= 32, "A copy plan");
+  static_assert(kSimtThreads % kBPerRow == 0 && kBPerThread >= 1, "B copy plan");
   const float* a_src;  // A + (m0 + a_row) * lda + a_k
   const float* b_src;  // B + b_row * ldb + n0 + b_n
-  int64_t a_step;      // 16 rows of A
+  int64_t a_step;      // kARowStep rows of A
   int64_t b_step;      // kBRowStep rows of B
   int64_t ldb;
   int a_dst, b_dst;    // shared offsets within a stage
   int a_k, b_row;
-  uint32_t a_rows_ok;  // bit j: row a_row + 16 j is below M
+  uint32_t a_rows_ok;  // bit j: row a_row + kARowStep j is below M
   uint32_t b_bytes;    // per B copy: 16 or fewer at a ragged N edge (VEC), 4 or 0 (scalar)
 
   __device__ __forceinline__ SimtCopy(const float* A, const float* B, int64_t M, int64_t N, int64_t lda,
                                       int64_t ldb_, int64_t m0, int64_t n0, int tid) {
     const int lane = tid & 31, warp = tid >> 5;
-    const int a_row = 4 * (warp >> 1) + (lane >> 3);
-    a_k = 8 * (warp & 1) + (lane & 7);
+    const int a_row = 4 * (warp / kKGroups) + (lane >> 3);
+    a_k = 8 * (warp % kKGroups) + (lane & 7);
     a_dst = a_k * kSimtAPitch + a_row;
     a_src = A + (m0 + a_row) * lda + a_k;
-    a_step = 16 * lda;
+    a_step = kARowStep * lda;
     a_rows_ok = 0;
 #pragma unroll
     for (int j = 0; j < kAPerThread; ++j)
-      if (m0 + a_row + 16 * j < M) a_rows_ok |= 1u << j;
+      if (m0 + a_row + kARowStep * j < M) a_rows_ok |= 1u << j;
     b_row = tid / kBPerRow;
     const int b_n = (tid % kBPerRow) * (VEC ? 4 : 1);
     b_dst = b_row * BN + b_n;
@@ -100,7 +105,7 @@ struct SimtCopy {
 #pragma unroll
     for (int j = 0; j < kAPerThread; ++j) {
       const bool ok = ka && ((a_rows_ok >> j) & 1u);
-      cp_async_4(as + a_dst + 16 * j, ok ? pa + j * a_step : A, ok ? 4u : 0u);
+      cp_async_4(as + a_dst + kARowStep * j, ok ? pa + j * a_step : A, ok ? 4u : 0u);
     }
     const float* pb = b_src + k0 * ldb;
 #pragma unroll
