@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define TILEC_MM_ABI_VERSION 4
+#define TILEC_MM_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define TILEC_API __attribute__((visibility("default")))
@@ -67,8 +67,15 @@ typedef enum tilec_mm_variant {
   TILEC_MM_3XTF32 = 4,    /* tcgen05 kind::tf32 with hi/lo operand split (3 MMAs) and fp32 promotion of
                              K-chunk partial sums: fp32-class accuracy; hi(x) is the tensor core's own
                              tf32 reading of x (its low 13 mantissa bits ignored) */
-  TILEC_MM_3XTF32_MASKED = 5 /* as 3XTF32 with hi(x) written explicitly (low 13 bits cleared) in shared
+  TILEC_MM_3XTF32_MASKED = 5, /* as 3XTF32 with hi(x) written explicitly (low 13 bits cleared) in shared
                                 memory; same results, one more shared store per element (cross-check) */
+  TILEC_MM_3XMIXED = 6    /* ABI version 5.  The same three-product split with the two small cross terms,
+                             a.lo(b) and lo(a).hi(b), on the bf16 tensor pipe (kind::f16, twice the tf32
+                             rate): 4 tf32-MMA slots per 16 of K instead of 6.  hi(a).hi(b) stays tf32.
+                             Adds at most 2^-16 relative error per product (bf16 rounding of
+                             terms below 2^-10 of it), about 1e-6 rms on random data.  Runs on the
+                             CTA-pair kernel (M >= 256, N > 128); other shapes, and the stream-K
+                             form, run 3XTF32 instead (tilec_mm_plan reports the variant that runs) */
 } tilec_mm_variant;
 
 /* Per-call configuration.  Zero-initialise, then set what you need. */

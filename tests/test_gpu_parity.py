@@ -1,7 +1,7 @@
 """Parity of every kernel variant against the CPU oracle, on a B200 (run with -m gpu).
 
 Gates (relative Frobenius error against the oracle, fp32 in / fp32 out):
-  SIMT, SPLITK, 3XTF32 : <= 1e-5        TF32 : <= 5e-3
+  SIMT, SPLITK, 3XTF32, 3XMIXED : <= 1e-5        TF32 : <= 5e-3
 plus the reference test's own check, np.testing.assert_allclose(rtol=1e-3, atol=1e-2)
 against ``x1 @ x2`` (tests/test_matmul.py:40), on the reference test's shapes
 (tests/test_matmul.py:33).  Exactly representable inputs must match bit for bit.
@@ -21,9 +21,11 @@ from tilec_b200 import TilecError, _native, ext
 pytestmark = pytest.mark.gpu
 
 DEV = "cuda:0"
-TOL = {"simt": 1e-5, "splitk": 1e-5, "3xtf32": 1e-5, "3xtf32_masked": 1e-5, "tf32": 5e-3, "auto": 1e-5}
-TENSOR = ("tf32", "3xtf32", "3xtf32_masked")
-ALL = ("auto", "simt", "splitk", "tf32", "3xtf32", "3xtf32_masked")
+TOL = {"simt": 1e-5, "splitk": 1e-5, "3xtf32": 1e-5, "3xtf32_masked": 1e-5, "3xmixed": 1e-5, "tf32": 5e-3,
+       "auto": 1e-5}
+TENSOR = ("tf32", "3xtf32", "3xtf32_masked", "3xmixed")
+SK_VARIANTS = ("tf32", "3xtf32", "3xtf32_masked")  # variants with a stream-K form
+ALL = ("auto", "simt", "splitk", "tf32", "3xtf32", "3xtf32_masked", "3xmixed")
 
 
 def _aligned(k, n):
@@ -424,7 +426,7 @@ def _ref64(x1, x2, bias=None, act=None):
     return r
 
 
-@pytest.mark.parametrize("variant", ("simt", "splitk", "tf32", "3xtf32", "3xtf32_masked"))
+@pytest.mark.parametrize("variant", ("simt", "splitk", "tf32", "3xtf32", "3xtf32_masked", "3xmixed"))
 @pytest.mark.parametrize("split_k", (1, 3))
 @pytest.mark.parametrize("shape", [(5, 300, 520, 700), (3, 512, 2048, 64), (4, 33, 129, 65), (2, 1000, 3001, 777)])
 def test_batched_equals_single_products(shape, split_k, variant):
@@ -444,7 +446,7 @@ def test_batched_equals_single_products(shape, split_k, variant):
     assert _status_clean()
 
 
-@pytest.mark.parametrize("variant", ("auto", "simt", "3xtf32", "tf32"))
+@pytest.mark.parametrize("variant", ("auto", "simt", "3xtf32", "tf32", "3xmixed"))
 def test_batched_shared_transposed_and_misaligned(variant):
     """A shared by the batch (2-D x1), B shared (2-D x2), column views of each slice, and
     batch strides that are not 16-byte multiples (packed for TMA)."""
@@ -468,7 +470,7 @@ def test_batched_shared_transposed_and_misaligned(variant):
 
 @pytest.mark.parametrize("act", (None, "relu", "gelu"))
 @pytest.mark.parametrize("variant,split_k", [("3xtf32", 0), ("3xtf32", 5), ("tf32", 1), ("simt", 0), ("splitk", 4),
-                                             ("auto", 0)])
+                                             ("auto", 0), ("3xmixed", 0), ("3xmixed", 3)])
 def test_fused_bias_activation(variant, split_k, act):
     """C = act(A.B + bias) with the epilogue in the GEMM's store (one K slice) or in the
     split-K reduction.  Bias-only and ReLU results are exactly torch's fp32
@@ -542,6 +544,63 @@ def test_tf32_pair_kernel_matches_single_cta(shape, split_k):
     assert _status_clean()
 
 
+# ---------------------------------------------------------------- mixed split (tf32 main product, bf16 cross terms)
+
+def _tf32_exact(rows, cols, g):
+    """j / 1024 for integer |j| <= 1024: 11 significant bits, exact in tf32 (l(x) = 0)."""
+    return (torch.randint(-1024, 1025, (rows, cols), generator=g).float() / 1024).to(DEV)
+
+
+@pytest.mark.parametrize("shape", [(2048, 2048, 2048), (1000, 3001, 777), (300, 520, 700), (4096, 8192, 512)])
+def test_mixed_equals_3xtf32_when_low_parts_vanish(shape):
+    """On operands that tf32 holds exactly, l(x) = 0: both cross terms add exact zeros, and
+    the tf32 main product runs in the same K order with the same promotion as 3XTF32, so
+    the two variants agree bit for bit."""
+    m, k, n = shape
+    g = torch.Generator().manual_seed(m + k + n)
+    a, b = _tf32_exact(m, k, g), _tf32_exact(k, n, g)
+    assert ext.plan(a, b, variant="3xmixed")[0] == "3xmixed"
+    assert torch.equal(ext._matrix_mul(a, b, variant="3xmixed"), ext._matrix_mul(a, b, variant="3xtf32"))
+    assert _status_clean()
+
+
+@pytest.mark.parametrize("k", (256, 2048, 8192, 16384))
+@pytest.mark.parametrize("dist", ("normal", "uniform", "positive"))
+def test_mixed_error_gate_and_flat_in_k(k, dist):
+    """The bf16 cross terms keep the fp32-class gate (relFrob <= 1e-5 against fp64) on
+    zero-mean and on all-positive operands (where rounding errors cannot cancel in sign),
+    with K up to 16384; the error stays within 4x of 3XTF32's."""
+    g = torch.Generator(device=DEV).manual_seed(k + len(dist))
+    if dist == "normal":
+        a = torch.randn(512, k, device=DEV, generator=g)
+        b = torch.randn(k, 512, device=DEV, generator=g)
+    else:
+        a = torch.rand(512, k, device=DEV, generator=g)
+        b = torch.rand(k, 512, device=DEV, generator=g)
+        if dist == "uniform":
+            a, b = 2 * a - 1, 2 * b - 1
+    ref = a.double() @ b.double()
+    mixed = _rel(ext._matrix_mul(a, b, variant="3xmixed"), ref)
+    three = _rel(ext._matrix_mul(a, b, variant="3xtf32"), ref)
+    assert mixed <= 1e-5, f"3xmixed K={k} {dist}: relFrob {mixed:.3e}"
+    assert mixed <= 4 * three + 1e-7, (mixed, three)
+
+
+def test_mixed_plan_falls_back_where_no_pair_kernel_runs():
+    """Shapes outside the CTA-pair kernel (M < 256 or N <= 128) and stream-K requests run
+    3XTF32, and the plan says so."""
+    a = torch.randn(200, 512, device=DEV)
+    b = torch.randn(512, 600, device=DEV)
+    assert ext.plan(a, b, variant="3xmixed")[0] == "3xtf32"
+    c = torch.randn(512, 100, device=DEV)
+    assert ext.plan(b.t(), c, variant="3xmixed")[0] == "3xtf32"
+    x = torch.randn(2304, 2048, device=DEV)
+    info = ext.plan(x, x.t(), variant="3xmixed", stream_k=True, detail=True)
+    assert info["variant"] == "3xmixed" and not info["stream_k"]
+    got = ext._matrix_mul(x, x.t(), variant="3xmixed", stream_k=True)
+    assert _rel(got, x.double() @ x.t().double()) <= 1e-5
+
+
 # ---------------------------------------------------------------- stream-K form of the CTA-pair kernel
 
 def _rel(got, ref):
@@ -559,7 +618,7 @@ SK_SHAPES = [
 ]
 
 
-@pytest.mark.parametrize("variant", TENSOR)
+@pytest.mark.parametrize("variant", SK_VARIANTS)
 @pytest.mark.parametrize("shape", SK_SHAPES, ids=lambda s: "x".join(map(str, s)))
 def test_stream_k_matches_oracle_and_one_pair_per_tile(shape, variant):
     """Stream-K (pairs share out the k-blocks of the tiles and add each tile's partial

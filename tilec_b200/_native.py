@@ -17,7 +17,7 @@ STATUS_NAMES = {
     8: "TILEC_ERR_TOO_LARGE",
 }
 
-VARIANTS = {"auto": 0, "simt": 1, "splitk": 2, "tf32": 3, "3xtf32": 4, "3xtf32_masked": 5}
+VARIANTS = {"auto": 0, "simt": 1, "splitk": 2, "tf32": 3, "3xtf32": 4, "3xtf32_masked": 5, "3xmixed": 6}
 VARIANT_NAMES = {v: k for k, v in VARIANTS.items()}
 
 # Every function the header declares (tests check the library exports exactly these).

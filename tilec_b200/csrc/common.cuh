@@ -313,11 +313,32 @@ __device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t adesc, 
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Same, kind::f16 with bf16 operands (both A and B bf16, K = 16 per instruction).
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive once on the mbarrier at `cluster_addr` (either CTA of the pair) when every
 // cta_group::2 tcgen05.mma issued so far by this thread has completed.
 __device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
                : "memory");
+}
+// One arrive on the mbarrier at the same offset (`local_addr`, this CTA's shared-memory
+// address) in both CTAs of the pair, from a single commit.  Each tcgen05 instruction the
+// MMA thread issues costs it issue time; two single-CTA commits per stage instead of this
+// one held the CTA-pair 3XTF32 kernel at 262-268 vs 286 TFLOP/s at 8192^3 (B200).
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t local_addr) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          local_addr),
+      "h"(static_cast<unsigned short>(3))
+      : "memory");
 }
 
 // ---------------------------------------------------------------- UMMA descriptors
@@ -349,6 +370,20 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_
 __host__ __device__ constexpr uint32_t make_idesc_tf32(int m, int n, bool a_mn = false, bool b_mn = true) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
          ((uint32_t(n) >> 3) << 17) | ((uint32_t(m) >> 4) << 24);
+}
+
+// Instruction descriptor for kind::f16 with bf16 A and B (format 1), fp32 accumulate,
+// both operands K-major.
+__host__ __device__ constexpr uint32_t make_idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t(n) >> 3) << 17) | ((uint32_t(m) >> 4) << 24);
+}
+
+// Two floats rounded to nearest-even bf16 and packed: `lo` in bits 0-15 (the lower
+// address in shared memory), `hi` in bits 16-31.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // Operand tile layouts of the tcgen05 kernels (runtime flags; the same bits as

@@ -14,8 +14,8 @@
 // memory with its own mbarriers (plain cta_group::1 TMA, no multicast).  Cross-CTA
 // signalling:
 //   split[s]      (leader)  <- 8 split warps of each CTA, remote mbarrier arrive (release.cluster)
-//   empty[s]      (each)    <- leader's tcgen05.commit, once to its own, once to the peer's barrier
-//   chunk_full[b] (each)    <- leader's tcgen05.commit, both CTAs
+//   empty[s]      (each)    <- leader's tcgen05.commit, multicast to the same barrier in both CTAs
+//   chunk_full[b] (each)    <- leader's tcgen05.commit, multicast to both CTAs
 //   chunk_empty[b](leader)  <- 8 epilogue warps of each CTA after draining their TMEM rows
 // TMEM is allocated and freed by warp 1 of both CTAs together (cta_group::2).  A cluster
 // barrier after set-up and another before teardown keep either CTA from touching the
@@ -70,10 +70,52 @@ struct Tc2Cfg {
   static_assert((3 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");  // mbarriers + TMEM slot + abort flag
 };
 
+// Operand readers for the mixed split (MIXED below): 8 consecutive k of one row of an fp32
+// stage tile as TMA left it.
+//   K-major tile ([rows x 16] fp32, 64-byte rows, 64-byte swizzle: the 16-byte granule
+//   index, address bits 4-5, is XORed with bits 7-8, i.e. with (row >> 1) & 3):
+__device__ __forceinline__ void read_kmajor8(const uint8_t* tile, int r, int kh, float (&v)[8]) {
+  const uint8_t* row = tile + r * 64;
+  const int sw = (r >> 1) & 3;
+  const float4 x0 = *reinterpret_cast<const float4*>(row + 16 * ((2 * kh) ^ sw));
+  const float4 x1 = *reinterpret_cast<const float4*>(row + 16 * ((2 * kh + 1) ^ sw));
+  v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+  v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+}
+//   MN-major tile (slabs of [16 k x 32] fp32, 2 KB apart, 128-byte rows with 32-byte granules:
+//   granule index, address bits 5-6, XORed with bits 7-8, i.e. with k & 3):
+__device__ __forceinline__ void read_mnmajor8(const uint8_t* tile, int r, int kh, float (&v)[8]) {
+  const uint8_t* slab = tile + (r >> 5) * 2048;
+  const int c = r & 31;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int k = 8 * kh + i;
+    v[i] = *reinterpret_cast<const float*>(slab + k * 128 + 32 * ((c >> 3) ^ (k & 3)) + 4 * (c & 7));
+  }
+}
+// Byte offset of row r, k in [8kh, 8kh+8) (16 bytes) in a [128 x 16] bf16 tile laid out
+// K-major with the 32-byte swizzle, as the kind::f16 descriptors describe it: 32-byte rows,
+// the 16-byte half selected by kh XORed with address bit 7, i.e. with (r >> 2) & 1; 8-row
+// groups 256 bytes apart (SBO).  (A no-swizzle layout with the K halves 2 KB apart, tried
+// first, halved the bf16 MMA rate on B200.)  A quarter warp storing 8 consecutive rows of
+// one K half covers all 32 banks.
+__device__ __forceinline__ uint32_t bf16_tile_offset(int r, int kh) {
+  return r * 32 + 16 * (kh ^ ((r >> 2) & 1));
+}
+
 // M = 256 (pair), N = BN, kind::tf32; A K-major and B MN-major unless `layout` flips
 // them (kOpAMN / kOpBK, operands stored transposed).
 // ANY_LAYOUT as in tc_gemm_kernel.
-template <int BN, int STAGES, bool SPLIT3, bool HI_EXPLICIT, bool ANY_LAYOUT>
+// MIXED (with SPLIT3): the 3-product split with the two cross terms on the bf16 pipe.  With
+// h(x) the tensor core's tf32 reading of x and l(x) = x - h(x) (exact in fp32),
+//   a.b = h(a).h(b) + a.l(b) + l(a).h(b)      (exactly),
+// and the cross terms are about 2^-11 of the product, so their operands need only bf16's
+// 8 bits: h.h runs as two kind::tf32 MMAs (K = 8) on the raw tiles, a.l(b) and l(a).h(b) as
+// one kind::f16 MMA each (K = 16) on bf16 tiles the split warps write.  Per 16 of K that is
+// 4 tensor slots of a tf32 K=8 MMA's length instead of 6.  Rounding the cross-term operands
+// to bf16 (relative error <= 2^-8 each, on terms below 2^-10 of the product) adds at most
+// 2^-16 relative error per product, about 1e-6 rms on random data.
+template <int BN, int STAGES, bool SPLIT3, bool HI_EXPLICIT, bool ANY_LAYOUT, bool MIXED = false>
 __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3>::kThreads, 1)
     tc2_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     float* __restrict__ out, int M, int N, int64_t ldo, int64_t out_slab, int K, int k_chunk,
@@ -81,6 +123,7 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3>::kThreads, 1)
                     const float* __restrict__ bias, int act, int shared) {
   const int layout = ANY_LAYOUT ? layout_arg : 0;
   using Cfg = Tc2Cfg<BN, STAGES, SPLIT3>;
+  static_assert(!MIXED || (SPLIT3 && !HI_EXPLICIT && BN == 256), "mixed split: 3-product stages, 128-row tiles");
   constexpr int BK = Cfg::BK;
   constexpr int KC = Cfg::kChunkBlocks;
   extern __shared__ uint8_t smem_raw[];
@@ -211,7 +254,6 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3>::kThreads, 1)
         return b_k ? make_smem_desc(base + kk * 32, 16, Cfg::kASbo, Cfg::kALayout)
                    : make_smem_desc(base + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
       };
-      const uint32_t peer = 1u;
       bool ok = true;
       for (int kb = 0; kb < nkb && ok; ++kb) {
         const int s = kb % STAGES;
@@ -229,7 +271,17 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3>::kThreads, 1)
         for (int kk = 0; kk < BK / 8; ++kk) {
           const uint64_t ad = desc_a(a_hi, kk), bd = desc_b(b_hi, kk);
           const uint32_t accum = (chunk_start && kk == 0) ? 0u : 1u;
-          if constexpr (SPLIT3) {
+          if constexpr (MIXED) {
+            if (kk == 0) {  // both cross terms first (bf16, K = 16 covers the stage)
+              const uint32_t la = smem_u32(a_lo(s)), lb = smem_u32(b_lo(s));
+              constexpr uint32_t idesc16 = make_idesc_bf16(256, BN);
+              umma_bf16_pair(tmem + dcol, make_smem_desc(la, 16, 256, kLayoutSw32),
+                             make_smem_desc(lb, 16, 256, kLayoutSw32), idesc16, accum);  // a . l(b)
+              umma_bf16_pair(tmem + dcol, make_smem_desc(la + 4096, 16, 256, kLayoutSw32),
+                             make_smem_desc(lb + 4096, 16, 256, kLayoutSw32), idesc16, 1u);  // l(a) . h(b)
+            }
+            umma_tf32_pair(tmem + dcol, ad, bd, idesc, 1u);
+          } else if constexpr (SPLIT3) {
             const uint64_t adl = desc_a(smem_u32(a_lo(s)), kk), bdl = desc_b(smem_u32(b_lo(s)), kk);
             umma_tf32_pair(tmem + dcol, adl, bd, idesc, accum);  // small terms first
             umma_tf32_pair(tmem + dcol, ad, bdl, idesc, 1u);
@@ -239,12 +291,10 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3>::kThreads, 1)
           }
         }
         const uint32_t e_local = smem_u32(&empty[s]);
-        umma_commit_pair(e_local);
-        umma_commit_pair(mapa_shared(e_local, peer));
+        umma_commit_pair_both(e_local);
         if (kb % KC == KC - 1 || kb == nkb - 1) {
           const uint32_t c_local = smem_u32(&chunk_full[chunk & 1]);
-          umma_commit_pair(c_local);
-          umma_commit_pair(mapa_shared(c_local, peer));
+          umma_commit_pair_both(c_local);
         }
       }
       if (!ok) {
@@ -289,7 +339,39 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3>::kThreads, 1)
       const int s = kb % STAGES;
       const uint32_t ph = (kb / STAGES) & 1;
       if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
-      if constexpr (SPLIT3) {
+      if constexpr (MIXED) {
+        // One (row, K half) unit per thread for A and for B: warps 0-3 of the eight take
+        // k 0-7, warps 4-7 k 8-15, 32 consecutive rows each, so the MN-major reads of a warp
+        // hit 32 banks, the K-major 16-byte reads and the 16-byte stores of each quarter
+        // warp 128 distinct bytes.
+        const int r = (e & 3) * 32 + lane, kh = e >> 2;
+        const uint32_t off = bf16_tile_offset(r, kh);
+        float v[8];
+        if (layout & kOpAMN) read_mnmajor8(a_raw(s), r, kh, v); else read_kmajor8(a_raw(s), r, kh, v);
+        uint4 xa, la;
+        uint32_t* pxa = &xa.x;
+        uint32_t* pla = &la.x;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          pxa[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+          pla[i] = pack_bf16x2(v[2 * i] - tf32_hi(v[2 * i]), v[2 * i + 1] - tf32_hi(v[2 * i + 1]));
+        }
+        *reinterpret_cast<uint4*>(a_lo(s) + off) = xa;         // bf16(a)
+        *reinterpret_cast<uint4*>(a_lo(s) + 4096 + off) = la;  // bf16(l(a))
+        if (layout & kOpBK) read_kmajor8(b_raw(s), r, kh, v); else read_mnmajor8(b_raw(s), r, kh, v);
+        uint4 lb, hb;
+        uint32_t* plb = &lb.x;
+        uint32_t* phb = &hb.x;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float h0 = tf32_hi(v[2 * i]), h1 = tf32_hi(v[2 * i + 1]);
+          plb[i] = pack_bf16x2(v[2 * i] - h0, v[2 * i + 1] - h1);
+          phb[i] = pack_bf16x2(h0, h1);
+        }
+        *reinterpret_cast<uint4*>(b_lo(s) + off) = lb;         // bf16(l(b))
+        *reinterpret_cast<uint4*>(b_lo(s) + 4096 + off) = hb;  // bf16(h(b))
+        fence_proxy_async_smem();
+      } else if constexpr (SPLIT3) {
         float4* src_a = reinterpret_cast<float4*>(a_raw(s));
         float4* dst_a = reinterpret_cast<float4*>(a_lo(s));
 #pragma unroll

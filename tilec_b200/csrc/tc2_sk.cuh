@@ -250,7 +250,6 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, true>::kThreads, 1)
         return b_k ? make_smem_desc(base + kk * 32, 16, Cfg::kASbo, Cfg::kALayout)
                    : make_smem_desc(base + kk * 1024, Cfg::kBLbo, Cfg::kBSbo, kLayoutSw128Base32);
       };
-      const uint32_t peer = 1u;
       bool ok = true;
       int g = 0, gc = 0;  // stages consumed and TMEM chunks started, over all segments
       for (int si = 0; si < n_seg && ok; ++si) {
@@ -284,12 +283,10 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, true>::kThreads, 1)
             }
           }
           const uint32_t e_local = smem_u32(&empty[s]);
-          umma_commit_pair(e_local);
-          umma_commit_pair(mapa_shared(e_local, peer));
+          umma_commit_pair_both(e_local);
           if (r % KC == KC - 1 || r == n - 1) {
             const uint32_t c_local = smem_u32(&chunk_full[chunk & 1]);
-            umma_commit_pair(c_local);
-            umma_commit_pair(mapa_shared(c_local, peer));
+            umma_commit_pair_both(c_local);
           }
         }
         gc += chunks_of(n);

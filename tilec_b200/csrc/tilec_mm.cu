@@ -117,6 +117,8 @@ cudaError_t init_device_attrs() {
   pair_attr(tc2_gemm_kernel<256, kPairStages, true, true, false>, k3x);
   pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, true>, k3x);
   pair_attr(tc2_gemm_kernel<256, kPairStages, true, true, true>, k3x);
+  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, false, true>, k3x);
+  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, true, true>, k3x);
   pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, false>, kTf);
   pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, true>, kTf);
   constexpr int s3x = Tc2Cfg<256, kPairStages, true, true>::kSmemBytes;
@@ -262,7 +264,8 @@ void choose_auto(const DeviceInfo& d, const float* A, const float* B, int64_t M,
         const int32_t* t = &g_table[r];
         if (lm >= t[0] && lm < t[1] && ln >= t[2] && ln < t[3] && lk2 >= t[4] && lk2 < t[5]) {
           int v = t[6];
-          const bool tc = v == TILEC_MM_TF32 || v == TILEC_MM_3XTF32 || v == TILEC_MM_3XTF32_MASKED;
+          const bool tc = v == TILEC_MM_TF32 || v == TILEC_MM_3XTF32 || v == TILEC_MM_3XTF32_MASKED ||
+                          v == TILEC_MM_3XMIXED;
           if (tc && !tensor_dims_ok(M, N, K)) v = TILEC_MM_SIMT;
           *variant = v;
           *split = t[7];
@@ -330,7 +333,7 @@ double cta_seconds(int64_t rows, int64_t cols, int64_t b_cols, int64_t K, double
 
 // Measured per-SM rates on B200: 3xTF32 ~1.7 TFLOP/s (250 TFLOP/s / 148), TF32 ~4.3, SIMT
 // FMA ~0.31; HBM share ~38 GB/s per SM with every SM streaming.
-constexpr double kRate3x = 1.7e12, kRateTf32 = 4.3e12, kRateSimt = 0.31e12, kBwPerSm = 38.0e9;
+constexpr double kRate3x = 1.7e12, kRateMix = 2.4e12, kRateTf32 = 4.3e12, kRateSimt = 0.31e12, kBwPerSm = 38.0e9;
 
 // Stream-K form of the pair kernel (Plan::sk).  T tiles on P pair slots take ceil(T / P)
 // waves of tile-times as one pair per tile, and T / P tile-times as stream-K, times a
@@ -388,8 +391,9 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
   p->b_shared = nb > 1 && q.stride_b == 0;
   if (requested_split < 0) return TILEC_ERR_BAD_ARG;
   if (variant == TILEC_MM_AUTO) choose_auto(d, q.A, q.B, M, N, K, q.lda, q.ldb, nb, &variant, &requested_split);
-  if (variant < TILEC_MM_SIMT || variant > TILEC_MM_3XTF32_MASKED) return TILEC_ERR_BAD_ARG;
-  const bool tensor = variant == TILEC_MM_TF32 || variant == TILEC_MM_3XTF32 || variant == TILEC_MM_3XTF32_MASKED;
+  if (variant < TILEC_MM_SIMT || variant > TILEC_MM_3XMIXED) return TILEC_ERR_BAD_ARG;
+  const bool tensor = variant == TILEC_MM_TF32 || variant == TILEC_MM_3XTF32 || variant == TILEC_MM_3XTF32_MASKED ||
+                      variant == TILEC_MM_3XMIXED;
   if (tensor && !tensor_dims_ok(M, N, K)) return TILEC_ERR_UNSUPPORTED;
   if (tensor) {
     // TMA also needs each batch's base 16-byte aligned: batch strides a multiple of 4.
@@ -404,19 +408,22 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
   if (tensor) {
     p->bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
     p->pair = p->bn == 256 && M >= kPairMinM;
+    // The mixed split exists only in the one-pair-per-tile kernel.
+    if (variant == TILEC_MM_3XMIXED && !p->pair) p->variant = variant = TILEC_MM_3XTF32;
+    const bool mixed = variant == TILEC_MM_3XMIXED;
     const int bk = variant == TILEC_MM_TF32 ? 32 : k3xBK;
     const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
     // The CTA pair launches two CTAs per 256-row x 256-column tile; each computes 128 rows
     // and loads half of the B columns.
     const int64_t ctas = (p->pair ? 2 * cdiv(M, 256) * cdiv(N, 256) : tiles) * nb;
     const double cta_s = cta_seconds(kTcBM, p->bn, p->pair ? p->bn / 2 : p->bn, K,
-                                     variant == TILEC_MM_TF32 ? kRateTf32 : kRate3x, kBwPerSm);
+                                     variant == TILEC_MM_TF32 ? kRateTf32 : (mixed ? kRateMix : kRate3x), kBwPerSm);
     p->split = choose_split(ctas, d.sms, cta_s, double(M) * double(round_up(N, 4)) * 4.0 * double(nb),
                             K / (int64_t(bk) * 4), requested_split, /*one_wave=*/true);
     p->k_chunk = round_up(cdiv(K, p->split), bk);
     p->split = static_cast<int>(cdiv(K, p->k_chunk > 0 ? p->k_chunk : 1));
     if (p->split < 1) p->split = 1;
-    if (p->pair && K > 0 && requested_split <= 1 && (want_sk || (requested_split == 0 && p->split == 1)))
+    if (p->pair && !mixed && K > 0 && requested_split <= 1 && (want_sk || (requested_split == 0 && p->split == 1)))
       plan_stream_k(d, M, N, K, nb, bk, cta_s, want_sk, p);
   } else {
     p->bn = N <= 64 ? 64 : 128;
@@ -604,7 +611,7 @@ int launch_tc_mode(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int6
     return launch_tc<BN, 32, TcShape<BN>::kTf32Stages, false, false>(ma, mb, M, N, K, L, s);
 }
 
-template <bool SPLIT3, bool HI>
+template <bool SPLIT3, bool HI, bool MIXED = false>
 int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
                cudaStream_t s) {
   using Cfg = Tc2Cfg<256, kPairStages, SPLIT3>;
@@ -618,8 +625,8 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t 
                     static_cast<int>(N), L.ldo, L.out_slab, static_cast<int>(K), static_cast<int>(L.k_chunk),
                     mp_tiles, n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias, L.act, L.shared);
   };
-  return L.layout ? go(tc2_gemm_kernel<256, kPairStages, SPLIT3, HI, true>)
-                  : go(tc2_gemm_kernel<256, kPairStages, SPLIT3, HI, false>);
+  return L.layout ? go(tc2_gemm_kernel<256, kPairStages, SPLIT3, HI, true, MIXED>)
+                  : go(tc2_gemm_kernel<256, kPairStages, SPLIT3, HI, false, MIXED>);
 }
 
 // Stream-K form: the flag reset (programmatic serialisation on both sides, so the GEMM's
@@ -992,9 +999,10 @@ int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, vo
            : p.variant == TILEC_MM_3XTF32 ? launch_tc2_sk<true, false>(ma, mb, M, N, K, L, sk, p.sk_pairs, s)
                                           : launch_tc2_sk<true, true>(ma, mb, M, N, K, L, sk, p.sk_pairs, s);
     } else if (p.pair)
-      rc = p.variant == TILEC_MM_TF32     ? launch_tc2<false, false>(ma, mb, M, N, K, L, s)
-           : p.variant == TILEC_MM_3XTF32 ? launch_tc2<true, false>(ma, mb, M, N, K, L, s)
-                                          : launch_tc2<true, true>(ma, mb, M, N, K, L, s);
+      rc = p.variant == TILEC_MM_TF32      ? launch_tc2<false, false>(ma, mb, M, N, K, L, s)
+           : p.variant == TILEC_MM_3XTF32  ? launch_tc2<true, false>(ma, mb, M, N, K, L, s)
+           : p.variant == TILEC_MM_3XMIXED ? launch_tc2<true, false, true>(ma, mb, M, N, K, L, s)
+                                           : launch_tc2<true, true>(ma, mb, M, N, K, L, s);
     else if (p.variant == TILEC_MM_TF32)
       rc = dispatch_tc_bn<false, false>(p.bn, ma, mb, M, N, K, L, s);
     else if (p.variant == TILEC_MM_3XTF32)
@@ -1141,7 +1149,7 @@ int tilec_mm_set_table(const int32_t* rows, int32_t nrows) {
   if (nrows < 0 || (nrows > 0 && rows == nullptr)) return TILEC_ERR_BAD_ARG;
   for (int32_t r = 0; r < nrows; ++r) {
     const int32_t v = rows[r * 8 + 6];
-    if (v < TILEC_MM_SIMT || v > TILEC_MM_3XTF32_MASKED || rows[r * 8 + 7] < 0) return TILEC_ERR_BAD_ARG;
+    if (v < TILEC_MM_SIMT || v > TILEC_MM_3XMIXED || rows[r * 8 + 7] < 0) return TILEC_ERR_BAD_ARG;
   }
   std::lock_guard<std::mutex> lk(g_table_mu);
   g_table.assign(rows, rows + size_t(nrows) * 8);

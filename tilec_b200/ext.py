@@ -119,7 +119,8 @@ def _matrix_mul(x1, x2, variant=None, split_k=0, out=None, stream_k=False):
     """matrix_mul with explicit kernel choice.
 
     variant: None (= $TILEC_MM_VARIANT or "auto"), "simt", "splitk", "tf32", "3xtf32",
-    "3xtf32_masked".  split_k: K slices for split variants (0 = library choice; 1 = none,
+    "3xtf32_masked", "3xmixed" (3xtf32 with its two cross terms on the bf16 tensor pipe;
+    CTA-pair shapes only, others run "3xtf32").  split_k: K slices for split variants (0 = library choice; 1 = none,
     which also rules out stream-K).  stream_k: run the CTA-pair kernel in its stream-K form
     whenever it is the kernel and split_k <= 1 (the library picks it by itself where it
     pays).  out: optional preallocated [M, N] float32 result (unit column stride).
