@@ -72,38 +72,111 @@ def variant_peak(variant, pk, sustained):
         return bf16 / 2 / 3, f"{tag} / 2 (tf32 rate) / 3 (MMAs per useful FLOP)"
     if variant == "tf32":
         return bf16 / 2, f"{tag} / 2 (tf32 rate)"
+    if variant == "3xmixed":
+        return bf16 / 2 / 2, (f"{tag} / 2 (tf32 rate) / 2 (per 16 of K: two tf32 K=8 MMAs + two bf16 K=16 "
+                              "MMAs at twice the tf32 rate = 2 tf32-equivalent MMAs per useful FLOP)")
     # SIMT FP32: 148 SMs x 128 FFMA lanes x 2 FLOP x max SM clock (nominal; no measured figure)
     return 148 * 128 * 2 * 1965e6 / 1e12, "nominal FP32 SIMT peak at 1965 MHz (148 SMs x 128 lanes x 2)"
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock, power and clock-event reasons of the timed GPUs during the timed region.
+
+    Polled every 20 ms through NVML (read-only queries), so even a sub-second timed region
+    gets tens of samples; `nvidia-smi -lms 200` when NVML cannot be loaded.  Devices are
+    matched to the CUDA devices by PCI bus id (NVML and CUDA numberings can differ)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvmlClocksEventReason*).
+    REASONS = (("gpu_idle", 1), ("applications_clocks_setting", 2), ("sw_power_cap", 4), ("hw_slowdown", 8),
+               ("sync_boost", 16), ("sw_thermal_slowdown", 32), ("hw_thermal_slowdown", 64),
+               ("hw_power_brake_slowdown", 128), ("display_clock_setting", 256))
+    PERIOD_S = 0.02
 
-    def __init__(self, indices):
-        self.indices = indices
+    def __init__(self, cuda_indices):
+        self.cuda_indices = cuda_indices
         self.proc = None
+        self.nvml = None
         self.lines = []
+        self.samples = []  # (sm_mhz, max_mhz, power_w, reason_bits)
+        self._stop = threading.Event()
+        self._recording = threading.Event()
+
+    def _nvml_handles(self, nv):
+        handles = []
+        for i in self.cuda_indices:
+            h = None
+            try:
+                p = torch.cuda.get_device_properties(i)
+                bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+                h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:  # noqa: BLE001
+                h = nv.nvmlDeviceGetHandleByIndex(i)
+            handles.append(h)
+        return handles
 
     def start(self):
         try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.handles = self._nvml_handles(nv)
+            self.nvml = nv
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return
+        except Exception:  # noqa: BLE001
+            self.nvml = None
+        try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", ",".join(map(str, self.indices))],
+                 "-i", ",".join(map(str, self.cuda_indices))],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except (OSError, ValueError):
             self.proc = None
 
+    def begin(self):
+        """Start keeping samples (call right before the timed region; NVML needs no warm-up)."""
+        self._recording.set()
+
+    def _poll(self):
+        nv = self.nvml
+        while not self._stop.is_set():
+            for h in (self.handles if self._recording.is_set() else ()):
+                try:
+                    self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                         nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM),
+                                         nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                         nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                except Exception:  # noqa: BLE001
+                    pass
+            self._stop.wait(self.PERIOD_S)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml is not None:
+            self._stop.set()
+            self.t.join(timeout=5)
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:  # noqa: BLE001
+                pass
+            if not self.samples:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no NVML samples"], "samples": 0}
+            bits = 0
+            for smp in self.samples:
+                bits |= int(smp[3])
+            return {"sm_mhz": statistics.median(x[0] for x in self.samples),
+                    "sm_max_mhz": max(x[1] for x in self.samples),
+                    "reasons": sorted(n for n, b in self.REASONS if bits & b),
+                    "samples": len(self.samples), "power_w_max": round(max(x[2] for x in self.samples), 1),
+                    "source": f"NVML every {int(self.PERIOD_S * 1000)} ms during the timed region"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -126,7 +199,7 @@ class ClockSampler:
                 if val.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi -lms 200"}
 
 
 def setup_dist():
@@ -326,6 +399,29 @@ def extra_configs(pk):
     return out
 
 
+def other_variants(x1, x2, out, pk, names=("3xmixed", "tf32")):
+    """The config-5 product in the other tensor-core variants on the same resident inputs:
+    mean CUDA-event time of 3 launches after 2 warm-ups, fraction of the variant's own
+    burst roof, and relFrob against fp64 on 64 sampled rows."""
+    from tilec_b200 import ext
+    m, k = x1.shape
+    n = x2.shape[1]
+    rows = torch.linspace(0, m - 1, 64, device=x1.device).round().long()
+    ref = x1[rows].double() @ x2.double()
+    res = {}
+    for v in names:
+        def go():
+            ext._matrix_mul(x1, x2, variant=v, out=out)
+        ms = time_launches(go, 3, warm=2)
+        tfl = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+        peak, note = variant_peak(v, pk, sustained=False)
+        err = ((out[rows].double() - ref).norm() / ref.norm()).item()
+        res[v] = {"ms": round(ms, 3), "tflops": round(tfl, 2), "roofline_tflops": round(peak, 2),
+                  "roofline_frac": round(tfl / peak, 4), "peak_note": note,
+                  "relfrob_sampled_rows": float(f"{err:.3e}"), "plan": ext.plan(x1, x2, variant=v)[0]}
+    return res
+
+
 def main():
     args = parse()
     world, rank, local = setup_dist()
@@ -375,11 +471,14 @@ def main():
     clocks = ClockSampler(list(range(world)) if world > 1 else [dev.index]) if rank == 0 else None
     if clocks:
         clocks.start()
-        time.sleep(0.3)
+        if clocks.nvml is None:
+            time.sleep(0.3)  # nvidia-smi's first sample
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if clocks:
+        clocks.begin()
     t_start.record()
     for _ in range(args.steps):
         step(timed_gemm)
@@ -478,6 +577,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1:
         if not args.no_extra:
+            others = other_variants(x1, x2, out, pk)
             extra = extra_configs(pk)
         if not args.no_cpu:
             cpu = cpu_baseline()
@@ -489,7 +589,9 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
             "dtype": "f32 (3xTF32 split on tcgen05: fp32-class accuracy, relFrob <= 1e-5)"
-            if variant.startswith("3xtf32") else ("tf32" if variant == "tf32" else "f32"),
+            if variant.startswith("3xtf32") else
+            ("f32 (3-product split, tf32 main product + bf16 cross terms on tcgen05: relFrob <= 1e-5)"
+             if variant == "3xmixed" else ("tf32" if variant == "tf32" else "f32")),
             "data": "synthetic",
             "config": {"workload": f"config5 row-sharded GEMM [{M5},{K5}] @ [{K5},{N5}] fp32, x2 broadcast "
                                    f"from rank 0 in {len(op.bounds)} column panel(s)",
@@ -499,7 +601,7 @@ def main():
             "roofline": {"bound": "tensor" if "tf32" in variant else "fp32", "achieved": round(achieved, 2),
                          "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "algorithmic_bytes": int(bytes_launch),
-                         "kernel": (f"{'tc2_gemm (CTA pair)' if variant.startswith('3xtf32') and rows >= 256 and panel_w > 128 else 'tc_gemm'}"
+                         "kernel": (f"{'tc2_gemm (CTA pair)' if variant in ('3xtf32', '3xtf32_masked', '3xmixed', 'tf32') and rows >= 256 and panel_w > 128 else 'tc_gemm'}"
                                     f" ({variant}) on [{rows},{K5}] @ [{K5},{panel_w}]"),
                          "launch_ms": round(gemm_ms_max, 4), "peak_note": peak_note + " (of measured)"
                          if pk["src"] == "measured" else peak_note,
@@ -512,6 +614,7 @@ def main():
             "clocks": clk,
         }
         if extra:
+            line["config5_other_variants"] = others
             line["configs_1_3"] = extra
         print(json.dumps(line), flush=True)
     if world > 1:

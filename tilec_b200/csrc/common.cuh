@@ -372,10 +372,11 @@ __host__ __device__ constexpr uint32_t make_idesc_tf32(int m, int n, bool a_mn =
          ((uint32_t(n) >> 3) << 17) | ((uint32_t(m) >> 4) << 24);
 }
 
-// Instruction descriptor for kind::f16 with bf16 A and B (format 1), fp32 accumulate,
-// both operands K-major.
-__host__ __device__ constexpr uint32_t make_idesc_bf16(int m, int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t(n) >> 3) << 17) | ((uint32_t(m) >> 4) << 24);
+// Instruction descriptor for kind::f16 with bf16 A and B (format 1), fp32 accumulate;
+// major bits as in make_idesc_tf32.
+__host__ __device__ constexpr uint32_t make_idesc_bf16(int m, int n, bool a_mn = false, bool b_mn = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
+         ((uint32_t(n) >> 3) << 17) | ((uint32_t(m) >> 4) << 24);
 }
 
 // Two floats rounded to nearest-even bf16 and packed: `lo` in bits 0-15 (the lower

@@ -82,23 +82,32 @@ __device__ __forceinline__ void read_kmajor8(const uint8_t* tile, int r, int kh,
   v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
   v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
 }
-//   MN-major tile (slabs of [16 k x 32] fp32, 2 KB apart, 128-byte rows with 32-byte granules:
-//   granule index, address bits 5-6, XORed with bits 7-8, i.e. with k & 3):
-__device__ __forceinline__ void read_mnmajor8(const uint8_t* tile, int r, int kh, float (&v)[8]) {
-  const uint8_t* slab = tile + (r >> 5) * 2048;
-  const int c = r & 31;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int k = 8 * kh + i;
-    v[i] = *reinterpret_cast<const float*>(slab + k * 128 + 32 * ((c >> 3) ^ (k & 3)) + 4 * (c & 7));
-  }
+// 8 consecutive MN indices 8q..8q+7 at one k of an MN-major fp32 stage tile (slabs of
+// [16 k x 32] fp32 2 KB apart, 128-byte rows with 32-byte granules: granule index, address
+// bits 5-6, XORed with bits 7-8, i.e. with k & 3): one granule, two 16-byte loads.  Odd
+// slabs read their upper half first, so a quarter warp's eight loads cover all 32 banks.
+__device__ __forceinline__ void read_mnmajor_chunk8(const uint8_t* tile, int k, int q, float (&v)[8]) {
+  const int j = q >> 2, h0 = j & 1;
+  const uint8_t* g = tile + j * 2048 + k * 128 + 32 * ((q & 3) ^ (k & 3));
+  const float4 x0 = *reinterpret_cast<const float4*>(g + 16 * h0);
+  const float4 x1 = *reinterpret_cast<const float4*>(g + 16 * (h0 ^ 1));
+  const float4 lo = h0 ? x1 : x0, hi = h0 ? x0 : x1;
+  v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+  v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+}
+// Byte offset of MN indices 8q..8q+7 at k (16 bytes) in a [16 x 128] bf16 tile laid out
+// MN-major with the 128-byte swizzle: 64-element (128-byte) rows along MN, the 16-byte chunk
+// index XORed with k & 7; the two 64-wide MN halves 1 KB apart (LBO), the two 8-row K
+// groups 2 KB apart (SBO).  A quarter warp storing one k's 8 chunks fills one 128-byte row.
+__device__ __forceinline__ uint32_t bf16_mn_tile_offset(int k, int q) {
+  return (k >> 3) * 2048 + (q >> 3) * 1024 + (k & 7) * 128 + (((q & 7) ^ (k & 7)) << 4);
 }
 // Byte offset of row r, k in [8kh, 8kh+8) (16 bytes) in a [128 x 16] bf16 tile laid out
 // K-major with the 32-byte swizzle, as the kind::f16 descriptors describe it: 32-byte rows,
 // the 16-byte half selected by kh XORed with address bit 7, i.e. with (r >> 2) & 1; 8-row
-// groups 256 bytes apart (SBO).  (A no-swizzle layout with the K halves 2 KB apart, tried
-// first, halved the bf16 MMA rate on B200.)  A quarter warp storing 8 consecutive rows of
-// one K half covers all 32 banks.
+// groups 256 bytes apart (SBO).  A quarter warp storing 8 consecutive rows of one K half
+// covers all 32 banks.  (A no-swizzle layout with the K halves 2 KB apart measured 3 %
+// slower.)
 __device__ __forceinline__ uint32_t bf16_tile_offset(int r, int kh) {
   return r * 32 + 16 * (kh ^ ((r >> 2) & 1));
 }
@@ -274,11 +283,12 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3>::kThreads, 1)
           if constexpr (MIXED) {
             if (kk == 0) {  // both cross terms first (bf16, K = 16 covers the stage)
               const uint32_t la = smem_u32(a_lo(s)), lb = smem_u32(b_lo(s));
-              constexpr uint32_t idesc16 = make_idesc_bf16(256, BN);
-              umma_bf16_pair(tmem + dcol, make_smem_desc(la, 16, 256, kLayoutSw32),
-                             make_smem_desc(lb, 16, 256, kLayoutSw32), idesc16, accum);  // a . l(b)
-              umma_bf16_pair(tmem + dcol, make_smem_desc(la + 4096, 16, 256, kLayoutSw32),
-                             make_smem_desc(lb + 4096, 16, 256, kLayoutSw32), idesc16, 1u);  // l(a) . h(b)
+              const uint32_t idesc16 = make_idesc_bf16(256, BN, a_mn, !b_k);
+              auto d16 = [](uint32_t base, bool mn) {
+                return mn ? make_smem_desc(base, 1024, 2048, kLayoutSw128) : make_smem_desc(base, 16, 256, kLayoutSw32);
+              };
+              umma_bf16_pair(tmem + dcol, d16(la, a_mn), d16(lb, !b_k), idesc16, accum);                // a . l(b)
+              umma_bf16_pair(tmem + dcol, d16(la + 4096, a_mn), d16(lb + 4096, !b_k), idesc16, 1u);  // l(a) . h(b)
             }
             umma_tf32_pair(tmem + dcol, ad, bd, idesc, 1u);
           } else if constexpr (SPLIT3) {
@@ -340,36 +350,41 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3>::kThreads, 1)
       const uint32_t ph = (kb / STAGES) & 1;
       if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
       if constexpr (MIXED) {
-        // One (row, K half) unit per thread for A and for B: warps 0-3 of the eight take
-        // k 0-7, warps 4-7 k 8-15, 32 consecutive rows each, so the MN-major reads of a warp
-        // hit 32 banks, the K-major 16-byte reads and the 16-byte stores of each quarter
-        // warp 128 distinct bytes.
-        const int r = (e & 3) * 32 + lane, kh = e >> 2;
-        const uint32_t off = bf16_tile_offset(r, kh);
-        float v[8];
-        if (layout & kOpAMN) read_mnmajor8(a_raw(s), r, kh, v); else read_kmajor8(a_raw(s), r, kh, v);
-        uint4 xa, la;
-        uint32_t* pxa = &xa.x;
-        uint32_t* pla = &la.x;
+        // Each operand tile's bf16 copies keep its major-ness.  K-major: one (row, K half)
+        // unit per thread, warps 0-3 of the eight taking k 0-7 and warps 4-7 k 8-15 for 32
+        // consecutive rows each; MN-major: one (k, 8 MN indices) chunk per thread, 16 per k.
+        // Either way each quarter warp's 16-byte loads and stores cover all 32 banks.
+        auto to_bf16 = [&](const uint8_t* raw, uint8_t* dst, bool mn, bool lhs) {
+          float v[8];
+          uint32_t off;
+          if (mn) {
+            read_mnmajor_chunk8(raw, et >> 4, et & 15, v);
+            off = bf16_mn_tile_offset(et >> 4, et & 15);
+          } else {
+            const int r = (e & 3) * 32 + lane, kh = e >> 2;
+            read_kmajor8(raw, r, kh, v);
+            off = bf16_tile_offset(r, kh);
+          }
+          uint4 o0, o1;
+          uint32_t* p0 = &o0.x;
+          uint32_t* p1 = &o1.x;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          pxa[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-          pla[i] = pack_bf16x2(v[2 * i] - tf32_hi(v[2 * i]), v[2 * i + 1] - tf32_hi(v[2 * i + 1]));
-        }
-        *reinterpret_cast<uint4*>(a_lo(s) + off) = xa;         // bf16(a)
-        *reinterpret_cast<uint4*>(a_lo(s) + 4096 + off) = la;  // bf16(l(a))
-        if (layout & kOpBK) read_kmajor8(b_raw(s), r, kh, v); else read_mnmajor8(b_raw(s), r, kh, v);
-        uint4 lb, hb;
-        uint32_t* plb = &lb.x;
-        uint32_t* phb = &hb.x;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float h0 = tf32_hi(v[2 * i]), h1 = tf32_hi(v[2 * i + 1]);
-          plb[i] = pack_bf16x2(v[2 * i] - h0, v[2 * i + 1] - h1);
-          phb[i] = pack_bf16x2(h0, h1);
-        }
-        *reinterpret_cast<uint4*>(b_lo(s) + off) = lb;         // bf16(l(b))
-        *reinterpret_cast<uint4*>(b_lo(s) + 4096 + off) = hb;  // bf16(h(b))
+          for (int i = 0; i < 4; ++i) {
+            const float x0 = v[2 * i], x1 = v[2 * i + 1];
+            const float h0 = tf32_hi(x0), h1 = tf32_hi(x1);
+            if (lhs) {  // A side: bf16(a), bf16(l(a))
+              p0[i] = pack_bf16x2(x0, x1);
+              p1[i] = pack_bf16x2(x0 - h0, x1 - h1);
+            } else {    // B side: bf16(l(b)), bf16(h(b))
+              p0[i] = pack_bf16x2(x0 - h0, x1 - h1);
+              p1[i] = pack_bf16x2(h0, h1);
+            }
+          }
+          *reinterpret_cast<uint4*>(dst + off) = o0;
+          *reinterpret_cast<uint4*>(dst + 4096 + off) = o1;
+        };
+        to_bf16(a_raw(s), a_lo(s), (layout & kOpAMN) != 0, true);
+        to_bf16(b_raw(s), b_lo(s), (layout & kOpBK) == 0, false);
         fence_proxy_async_smem();
       } else if constexpr (SPLIT3) {
         float4* src_a = reinterpret_cast<float4*>(a_raw(s));
