@@ -72,10 +72,12 @@ typedef enum tilec_mm_variant {
   TILEC_MM_3XMIXED = 6    /* ABI version 5.  The same three-product split with the two small cross terms,
                              a.lo(b) and lo(a).hi(b), on the bf16 tensor pipe (kind::f16, twice the tf32
                              rate): 4 tf32-MMA slots per 16 of K instead of 6.  hi(a).hi(b) stays tf32.
-                             Adds at most 2^-16 relative error per product (bf16 rounding of
-                             terms below 2^-10 of it), about 1e-6 rms on random data.  Runs on the
-                             CTA-pair kernel (M >= 256, N > 128); other shapes, and the stream-K
-                             form, run 3XTF32 instead (tilec_mm_plan reports the variant that runs) */
+                             Error per product at most 3 * 2^-18 (about 1.1e-5) relative, against
+                             3 * 2^-20 for 3XTF32 (bf16 rounding of terms below 2^-10 of the
+                             product); relFrob about 1.5e-6 on random data (3XTF32: 1.2e-6).  Runs on the
+                             CTA-pair kernel (M >= 256, N > 128), one pair per tile (TILEC_MM_STREAM_K
+                             is ignored); other shapes run 3XTF32 instead (tilec_mm_plan reports the
+                             variant that runs) */
 } tilec_mm_variant;
 
 /* Per-call configuration.  Zero-initialise, then set what you need. */
