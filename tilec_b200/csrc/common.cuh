@@ -105,6 +105,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait that ignores the abort flag (used while draining after an abort).
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - t0 > 100000000ull) return;  // 100 ms
+  }
+}
+
 // ---------------------------------------------------------------- flags between CTAs in global memory
 // A producer CTA publishes data with plain stores, then one thread raises a flag with a
 // release at GPU scope; the consumer polls the flag with acquire loads.

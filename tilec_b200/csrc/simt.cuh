@@ -10,12 +10,16 @@
 //   * CTA tile 128 x BN x 16 (BN = 128 or 64), 256 threads, each thread an 8 x (BN/16)
 //     register block (2-D register blocking, 64 or 32 FFMA per k), at most 128 registers
 //     so that two CTAs (16 warps) share an SM.
-//   * 4-stage cp.async pipeline global -> shared; the tail of a ragged tile is
-//     zero-filled by cp.async's src-size operand, so no out-of-range address is read.
+//   * 4-stage pipeline global -> shared.  B tiles with 16-byte aligned rows are staged by
+//     TMA (one [16 x BN] box per stage, completion on a per-stage mbarrier; the tensor
+//     map's extent zero-fills ragged edges); others, and A always, by cp.async, whose
+//     src-size operand zero-fills the tail of a ragged tile, so no out-of-range address is
+//     read.  TMA cannot stage A: the kernel wants A k-major and TMA does not transpose
+//     4-byte elements.
 //   * Both shared tiles are k-major: A as [16][128 + 4] (transposed on the way in by
 //     4-byte copies; a warp copies 4 rows x 8 k, 32-byte runs of global memory, and the
-//     pitch of 132 puts its 32 stores in 32 banks), B as [16][BN] (16-byte copies when
-//     rows are 16-byte aligned, VEC; 4-byte otherwise).  A thread owns the 8 consecutive
+//     pitch of 132 puts its 32 stores in 32 banks), B as [16][BN] (the dense box TMA
+//     writes, or 16-byte / 4-byte cp.async copies).  A thread owns the 8 consecutive
 //     rows tm*8.. and reads them at one k with two 16-byte loads, as it reads its B
 //     columns: 4 shared loads per 64 FFMA and only 16 operand registers live.
 //   * Split-K (gridDim.z = S > 1): CTA z covers K range [z*k_chunk, min(K,(z+1)*k_chunk))
@@ -32,10 +36,14 @@ constexpr int kSimtBK = 16;
 constexpr int kSimtStages = 4;
 constexpr int kSimtThreads = 256;
 constexpr int kSimtAPitch = kSimtBM + 4;  // floats per k row of the k-major A tile
+constexpr int kSimtBarBytes = 64;         // TMA-staged B: kSimtStages mbarriers + abort flag
+
+// How B reaches shared memory: 4-byte cp.async (any alignment), 16-byte cp.async, TMA.
+enum : int { kBScalar = 0, kBVec = 1, kBTma = 2 };
 
 template <int BN>
 constexpr int simt_smem_bytes() {
-  return kSimtStages * (kSimtBK * kSimtAPitch + kSimtBK * BN) * 4;
+  return kSimtStages * (kSimtBK * kSimtAPitch + kSimtBK * BN) * 4 + kSimtBarBytes;
 }
 // Dynamic shared memory asked for by grids of at most one CTA per SM: more than half of an
 // SM's 228 KB, so the block scheduler cannot place two such CTAs on one SM.
@@ -52,8 +60,9 @@ static_assert(simt_smem_bytes<128>() <= kSimtSpreadSmem, "spread request covers 
 //   B: 16-byte chunk (VEC) or element b_n of rows b_row + kBRowStep * i.
 // Out-of-range elements are zero-filled through cp.async's src-size operand, with the
 // operand's base address as the (unread) source.
-template <int BN, bool VEC>
+template <int BN, int BMODE>
 struct SimtCopy {
+  static constexpr bool VEC = BMODE != kBScalar;
   static constexpr int kAPerThread = kSimtBM * kSimtBK / kSimtThreads;
   static constexpr int kKGroups = kSimtBK / 8;            // G
   static constexpr int kARowStep = 4 * (8 / kKGroups);    // rows between a thread's copies
@@ -107,6 +116,7 @@ struct SimtCopy {
       const bool ok = ka && ((a_rows_ok >> j) & 1u);
       cp_async_4(as + a_dst + kARowStep * j, ok ? pa + j * a_step : A, ok ? 4u : 0u);
     }
+    if constexpr (BMODE == kBTma) return;  // B arrives by TMA
     const float* pb = b_src + k0 * ldb;
 #pragma unroll
     for (int i = 0; i < kBPerThread; ++i) {
@@ -122,16 +132,24 @@ struct SimtCopy {
 // out/ldo: C (one K slice) or the split-K workspace (slab z at out + z*out_slab).
 // blockIdx.z = batch * splits + K slice; batch b reads A + b*stride_a, B + b*stride_b and
 // writes out + b*out_batch.  bias / act: fused epilogue (only when writing C directly).
-template <int BN, bool VEC>
+// tmB (BMODE == kBTma): B as a 3-D map {N, K, batch} with a {BN, 16, 1} box; batch index 0
+// when stride_b == 0 (shared B).  K slices start at multiples of 16, so a stage's 16 rows
+// never straddle a slice boundary, and rows past K read as zero.
+template <int BN, int BMODE>
 __global__ void __launch_bounds__(kSimtThreads, 2)
-    simt_gemm_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ out,
+    simt_gemm_kernel(const __grid_constant__ CUtensorMap tmB, const float* __restrict__ A,
+                     const float* __restrict__ B, float* __restrict__ out,
                      int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldo, int64_t out_slab,
                      int64_t k_chunk, int vec_out, int splits, int64_t stride_a, int64_t stride_b,
                      int64_t out_batch, const float* __restrict__ bias, int act) {
   constexpr int TN = BN / 16;  // columns per thread: 8 (two float4 groups 64 apart) or 4
-  extern __shared__ __align__(16) float smem[];
+  extern __shared__ __align__(128) float smem[];
   float* As = smem;
-  float* Bs = smem + kSimtStages * kSimtBK * kSimtAPitch;
+  float* Bs = smem + kSimtStages * kSimtBK * kSimtAPitch;  // 128-byte aligned: a TMA destination
+  uint64_t* full = reinterpret_cast<uint64_t*>(Bs + kSimtStages * kSimtBK * BN);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + kSimtStages);
+  static_assert((kSimtStages * kSimtBK * kSimtAPitch * 4) % 128 == 0, "B tiles 128-byte aligned");
+  static_assert(kSimtStages * 8 + 4 <= kSimtBarBytes, "barrier area");
 
   pdl_wait();
   if (blockDim.x != kSimtThreads) {
@@ -149,7 +167,26 @@ __global__ void __launch_bounds__(kSimtThreads, 2)
   const int64_t k_end = (k_begin + k_chunk < K) ? k_begin + k_chunk : K;
   const int64_t nkt = (k_end > k_begin) ? (k_end - k_begin + kSimtBK - 1) / kSimtBK : 0;
   out += kslice * out_slab + batch * out_batch;
-  const SimtCopy<BN, VEC> copy(A, B, M, N, lda, ldb, m0, n0, tid);
+  const SimtCopy<BN, BMODE> copy(A, B, M, N, lda, ldb, m0, n0, tid);
+  // Thread 0 stages B tile `it` (k rows k_begin + 16 it ..) into stage it % kSimtStages.
+  // Coordinates are recomputed from blockIdx at each use rather than held in registers.
+  auto issue_b = [&](int it) {
+    const int st = it % kSimtStages;
+    const int bz = static_cast<int>(blockIdx.z) / splits;
+    mbar_arrive_expect_tx(&full[st], kSimtBK * BN * 4);
+    tma_load_3d(Bs + st * kSimtBK * BN, &tmB, &full[st], static_cast<int>(blockIdx.y) * BN,
+                static_cast<int>((static_cast<int>(blockIdx.z) % splits) * k_chunk) + it * kSimtBK,
+                stride_b == 0 ? 0 : bz);
+  };
+  if constexpr (BMODE == kBTma) {
+    if (tid == 0) {
+      for (int s = 0; s < kSimtStages; ++s) mbar_init(&full[s], 1);
+      *abort_flag = 0;
+      fence_barrier_init();
+      tma_prefetch_desc(&tmB);
+    }
+    __syncthreads();
+  }
 
   const int tm = tid >> 4;
   const int tn = tid & 15;
@@ -162,18 +199,39 @@ __global__ void __launch_bounds__(kSimtThreads, 2)
 
 #pragma unroll
   for (int s = 0; s < kSimtStages - 1; ++s) {
-    if (s < nkt)
+    if (s < nkt) {
       copy.load(As + s * kSimtBK * kSimtAPitch, Bs + s * kSimtBK * BN, A, B, k_begin + s * kSimtBK, k_end);
+      if (BMODE == kBTma && tid == 0) issue_b(s);
+    }
     cp_async_commit();
   }
 
-  for (int64_t kt = 0; kt < nkt; ++kt) {
+  bool ok = true;
+  int64_t kt = 0;
+  for (; kt < nkt; ++kt) {
     cp_async_wait<kSimtStages - 2>();
+    if constexpr (BMODE == kBTma) {
+      // Thread 0 waits (bounded) for the stage's B tile; the barrier below then orders the
+      // TMA's writes, which its wait acquired, before every thread's reads.  On a timeout it
+      // raises the abort flag, which every thread reads after the barrier, so the whole CTA
+      // leaves the loop together.
+      if (tid == 0) {
+        const int it = static_cast<int>(kt);
+        mbar_wait(&full[it % kSimtStages], static_cast<uint32_t>((it / kSimtStages) & 1), abort_flag);
+      }
+    }
     __syncthreads();
+    if constexpr (BMODE == kBTma) {
+      if (*abort_flag) {
+        ok = false;
+        break;
+      }
+    }
     const int64_t nt = kt + kSimtStages - 1;
     if (nt < nkt) {
       const int ns = static_cast<int>(nt % kSimtStages);
       copy.load(As + ns * kSimtBK * kSimtAPitch, Bs + ns * kSimtBK * BN, A, B, k_begin + nt * kSimtBK, k_end);
+      if (BMODE == kBTma && tid == 0) issue_b(static_cast<int>(nt));
     }
     cp_async_commit();
 
@@ -199,6 +257,16 @@ __global__ void __launch_bounds__(kSimtThreads, 2)
     }
   }
   cp_async_wait<0>();
+  if constexpr (BMODE == kBTma) {
+    if (!ok) {
+      // Let the TMA copies still in flight (tiles kt .. kt + 2) land before the CTA's
+      // shared memory goes away; store nothing (the status word records the timeout).
+      if (tid == 0)
+        for (int64_t it = kt; it < nkt && it < kt + kSimtStages - 1; ++it)
+          mbar_drain(&full[it % kSimtStages], static_cast<uint32_t>((it / kSimtStages) & 1));
+      return;
+    }
+  }
   // Let the next kernel launch only now: CTAs of a dependent kernel that wait resident on
   // the SM while this FMA-bound loop runs cost it issue slots (measured 40% slower).
   pdl_launch_dependents();

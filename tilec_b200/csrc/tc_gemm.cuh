@@ -76,13 +76,6 @@ __device__ __forceinline__ float tf32_hi(float x) {
   return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
 
-// Bounded wait that ignores the abort flag (used while draining after an abort).
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-  const unsigned long long t0 = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - t0 > 100000000ull) return;  // 100 ms
-  }
-}
 
 // Writes a 32-row x NC-column block, held one row per lane in v[], to rows row0.. and
 // columns col0.. of `out` (masked at M and N).  The warp transposes it through its own

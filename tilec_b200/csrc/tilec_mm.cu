@@ -91,14 +91,15 @@ cudaError_t init_device_attrs() {
     if (e == cudaSuccess && x != cudaSuccess) e = x;
   };
   // Up to kSimtSpreadSmem: small grids ask for that much to keep to one CTA per SM.
-  acc(cudaFuncSetAttribute(simt_gemm_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kSimtSpreadSmem));
-  acc(cudaFuncSetAttribute(simt_gemm_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kSimtSpreadSmem));
-  acc(cudaFuncSetAttribute(simt_gemm_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kSimtSpreadSmem));
-  acc(cudaFuncSetAttribute(simt_gemm_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kSimtSpreadSmem));
+  auto simt_attr = [&](auto kern) {
+    acc(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSimtSpreadSmem));
+  };
+  simt_attr(simt_gemm_kernel<128, kBScalar>);
+  simt_attr(simt_gemm_kernel<128, kBVec>);
+  simt_attr(simt_gemm_kernel<128, kBTma>);
+  simt_attr(simt_gemm_kernel<64, kBScalar>);
+  simt_attr(simt_gemm_kernel<64, kBVec>);
+  simt_attr(simt_gemm_kernel<64, kBTma>);
   acc(set_tc_attr<256, 32, TcShape<256>::kTf32Stages, false, false>());
   acc(set_tc_attr<128, 32, TcShape<128>::kTf32Stages, false, false>());
   acc(set_tc_attr<64, 32, TcShape<64>::kTf32Stages, false, false>());
@@ -524,6 +525,24 @@ int encode_maps(const float* A, const float* B, int64_t M, int64_t N, int64_t K,
   return ok_a && ok_b ? TILEC_OK : TILEC_ERR_BAD_ARG;
 }
 
+// B of the SIMT kernel as a TMA map: {N, K, batch} with a dense {bn, 16, 1} box (no swizzle:
+// the kernel reads the [16][bn] tile as written); extent N and K zero-fill ragged edges.
+int encode_simt_b_map(const float* B, int64_t N, int64_t K, int64_t ldb, int64_t stride_b, int64_t nbb, int bn,
+                      CUtensorMap* mb) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode();
+  if (!enc) return TILEC_ERR_NO_DEVICE;
+  cuuint64_t dims[3] = {cuuint64_t(N), cuuint64_t(K), cuuint64_t(nbb)};
+  const int64_t bs = nbb > 1 ? stride_b : round_up(K * ldb, 4);
+  cuuint64_t strides[2] = {cuuint64_t(ldb) * 4, cuuint64_t(bs) * 4};
+  cuuint32_t box[3] = {cuuint32_t(bn), cuuint32_t(kSimtBK), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(B), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? TILEC_OK
+             : TILEC_ERR_BAD_ARG;
+}
+
 // Programmatic dependent launch is on unless TILEC_MM_PDL=0 (read once per process).
 bool pdl_enabled() {
   static const bool on = [] {
@@ -867,9 +886,11 @@ int launch_fill_zero(float* C, int64_t M, int64_t N, int64_t ldc, int64_t batche
 
 // grid: (M tiles, N tiles, batches * L.split).  A / B advance by stride_a / stride_b per
 // batch (0 = shared).
-int launch_simt(int bn, bool vec, dim3 grid, const float* A, const float* B, int64_t M, int64_t N, int64_t K,
-                int64_t lda, int64_t ldb, int64_t stride_a, int64_t stride_b, const Launch& L, int sms,
-                cudaStream_t s) {
+// mb: B's tensor map for TMA staging (encode_simt_b_map), or nullptr for cp.async copies
+// (16-byte ones when `vec`).
+int launch_simt(int bn, bool vec, const CUtensorMap* mb, dim3 grid, const float* A, const float* B, int64_t M,
+                int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t stride_a, int64_t stride_b, const Launch& L,
+                int sms, cudaStream_t s) {
   // Launched without programmatic serialisation: two SIMT CTAs fit on an SM, and CTAs
   // placed while the previous kernel still occupies the GPU were measured to double up on
   // some SMs (a 128-CTA grid ran 40% slower).  For the same reason a grid of at most one
@@ -877,16 +898,20 @@ int launch_simt(int bn, bool vec, dim3 grid, const float* A, const float* B, int
   // (B200, config 1 as SPLITK, 148 CTAs: 12.2 us with two allowed, 11.6 us spread).
   const dim3 block(kSimtThreads);
   const bool spread = int64_t(grid.x) * grid.y * grid.z <= sms;
+  CUtensorMap unused{};
+  const CUtensorMap& map = mb ? *mb : unused;
   auto go = [&](auto kern, size_t smem) {
-    return launch_kx(false, kern, grid, block, spread ? size_t(kSimtSpreadSmem) : smem, s, 1, A, B, L.out, M, N,
-                     K, lda, ldb, L.ldo, L.out_slab, L.k_chunk, L.vec_out, L.split, stride_a, stride_b,
+    return launch_kx(false, kern, grid, block, spread ? size_t(kSimtSpreadSmem) : smem, s, 1, map, A, B, L.out, M,
+                     N, K, lda, ldb, L.ldo, L.out_slab, L.k_chunk, L.vec_out, L.split, stride_a, stride_b,
                      L.out_batch, L.bias, L.act);
   };
   if (bn == 64)
-    return vec ? go(simt_gemm_kernel<64, true>, simt_smem_bytes<64>())
-               : go(simt_gemm_kernel<64, false>, simt_smem_bytes<64>());
-  return vec ? go(simt_gemm_kernel<128, true>, simt_smem_bytes<128>())
-             : go(simt_gemm_kernel<128, false>, simt_smem_bytes<128>());
+    return mb ? go(simt_gemm_kernel<64, kBTma>, simt_smem_bytes<64>())
+              : vec ? go(simt_gemm_kernel<64, kBVec>, simt_smem_bytes<64>())
+                    : go(simt_gemm_kernel<64, kBScalar>, simt_smem_bytes<64>());
+  return mb ? go(simt_gemm_kernel<128, kBTma>, simt_smem_bytes<128>())
+            : vec ? go(simt_gemm_kernel<128, kBVec>, simt_smem_bytes<128>())
+                  : go(simt_gemm_kernel<128, kBScalar>, simt_smem_bytes<128>());
 }
 
 constexpr int64_t kMaxBatch = 65535;  // grid y / z limit; larger batches run in chunks
@@ -982,7 +1007,11 @@ int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, vo
     const int64_t mt = cdiv(M, kSimtBM), nt = cdiv(N, p.bn);
     if (nt > 65535 || nb * p.split > 65535) return TILEC_ERR_UNSUPPORTED;
     const dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(nb * p.split));
-    rc = launch_simt(p.bn, vec, grid, A, B, M, N, K, lda, ldb, sa, sb, L, d.sms, s);
+    // B with 16-byte aligned rows (and batch strides) is staged by TMA.
+    CUtensorMap mbs;
+    const bool tma_b = rows_aligned(B, ldb) && (nbb == 1 || sb % 4 == 0) && tensor_dims_ok(M, N, K) &&
+                       nbb < (int64_t(1) << 31) && encode_simt_b_map(B, N, K, ldb, sb, nbb, p.bn, &mbs) == TILEC_OK;
+    rc = launch_simt(p.bn, vec, tma_b ? &mbs : nullptr, grid, A, B, M, N, K, lda, ldb, sa, sb, L, d.sms, s);
   } else {
     CUtensorMap ma, mb;
     const int bk = p.variant == TILEC_MM_TF32 ? 32 : k3xBK;
@@ -1278,7 +1307,7 @@ extern "C" int tilec_mm_f32_splitk_noalloc(const float* A, const float* B, float
   L.k_chunk = k_chunk;
   const bool vec = aligned16(A) && aligned16(B) && (lda % 4 == 0) && (ldb % 4 == 0);
   dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(split));
-  rc = launch_simt(bn, vec, grid, A, B, M, N, K, lda, ldb, 0, 0, L, d->sms, s);
+  rc = launch_simt(bn, vec, nullptr, grid, A, B, M, N, K, lda, ldb, 0, 0, L, d->sms, s);
   if (rc || split == 1) return rc;
   Reduce r;
   r.ws = scratch;
