@@ -10,7 +10,8 @@ from tilec_b200 import _native, select, tune
 def test_committed_table_is_valid_and_fp32_class():
     """The table holds rows only where the sweep beat the built-in rules by a margin (it may
     be empty: then AUTO is the built-in rules), each fp32-accurate, and it records its
-    held-out and cross-validated reports, which never rate it worse than the rules."""
+    held-out and cross-validated reports: a fit that cross-validation rates worse than the
+    rules ships no rows."""
     rows = select.load_table(select.TABLE_PATH)
     names = {_native.VARIANT_NAMES[r[6]] for r in rows}
     assert names <= set(tune.FP32_CLASS), "AUTO may only pick fp32-accurate variants"
@@ -18,7 +19,10 @@ def test_committed_table_is_valid_and_fp32_class():
         doc = json.load(f)
     assert doc["heldout"]["shapes"] > 0 and doc["shapes"] >= 64
     cv = doc["cross_validation"]
-    assert cv["selector_x_of_best"] <= cv["builtin_x_of_best"] + 1e-9
+    if doc.get("fitted_table_kept", True):
+        assert cv["selector_x_of_best"] <= cv["builtin_x_of_best"] + 1e-9
+    else:  # the fit lost to the rules under cross-validation, so none of it ships
+        assert rows == []
     for m, n, k in [(1, 1, 1), (512, 64, 4096), (65536, 8192, 8192), (3, 777, 3001), (2 ** 40, 2, 2)]:
         hit = select.lookup(rows, m, n, k)
         assert hit is None or hit[0] in tune.FP32_CLASS

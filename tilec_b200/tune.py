@@ -101,15 +101,22 @@ def bench(n=64, path=DEFAULT_CSV, seed=4):
             # Built-in rules (no table) and each variant family with the library's own split.
             from . import select
             select.install([])
-            ms = time_ms(lambda: ext._matrix_mul(a, b, variant="auto", out=c))
-            w.writerow([dev, m, k, nn, "builtin", 0, f"{ms:.6f}"])
+            auto = lambda: ext._matrix_mul(a, b, variant="auto", out=c)  # noqa: E731
+            ms_auto = time_ms(auto)
             cands = [("simt", 0), ("splitk", 0), ("3xtf32", 0), ("tf32", 0)] + ext.mm_configs(m, k, nn)
+            out_rows = []
             for v, s in cands:
                 # Family rows (the library's own split) feed the fit, so they are always
                 # measured in full; explicit splits may stop early when far behind.
                 ms = time_ms(lambda: ext._matrix_mul(a, b, variant=v, split_k=s, out=c), None if s == 0 else best)
                 best = ms if best is None else min(best, ms)
-                w.writerow([dev, m, k, nn, v, s, f"{ms:.6f}"])
+                out_rows.append([dev, m, k, nn, v, s, f"{ms:.6f}"])
+            # The built-in rule is timed before and after the families and keeps the faster:
+            # the first calls on fresh operands read a few microseconds slow, which at the
+            # launch floor would otherwise look like a loss of the rule.
+            ms_auto = min(ms_auto, time_ms(auto))
+            w.writerow([dev, m, k, nn, "builtin", 0, f"{ms_auto:.6f}"])
+            w.writerows(out_rows)
             f.flush()
             print(f"{i + 1}/{n}  {m}x{k} @ {k}x{nn}  best {best:.4f} ms", flush=True)
 
@@ -200,8 +207,17 @@ def train(path=DEFAULT_CSV, out=None, test_frac=0.2, seed=0):
     print(f"selector: {gm(ratio_sel):.3f}x of best (geo mean), worst {max(ratio_sel, default=1):.2f}x")
     print(f"default : {gm(ratio_default):.3f}x of best (geo mean), worst {max(ratio_default, default=1):.2f}x")
     table = fit(rows)
+    # A table ships only if it beats the built-in rules under cross-validation; otherwise its
+    # rows fit measurement noise (launch-floor shapes differ by a few microseconds from run
+    # to run) and AUTO stays the built-in rule.
+    kept = cv["selector_x_of_best"] < cv["builtin_x_of_best"]
+    if not kept and table:
+        print(f"cross-validation: the fitted table ({len(table)} rows) does not beat the built-in rules; "
+              "writing an empty table")
+        table = []
     doc = {"device": rows[0]["device"] if rows else "", "source": os.path.basename(path),
            "shapes": len(keys), "grid_log2_edges": list(GRID_EDGES), "rows": table,
+           "fitted_table_kept": kept,
            "heldout": {"shapes": len(test), "selector_x_of_best": round(gm(ratio_sel), 4),
                        "builtin_x_of_best": round(gm(ratio_default), 4),
                        "selector_worst": round(max(ratio_sel, default=1), 3),
