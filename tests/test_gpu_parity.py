@@ -712,3 +712,36 @@ def test_stream_k_concurrent_streams():
     for r, os_ in zip(alone, outs):
         for o in os_:
             assert torch.equal(o, r)
+
+
+# ---------------------------------------------------------------- non-finite operands
+
+@pytest.mark.parametrize("variant", ALL)
+def test_non_finite_operands(variant):
+    """Inf / NaN in x1 or x2 reach exactly the outputs whose dot products contain them, as in
+    the reference's fp32 dot (each output is an independent sum): those rows / columns are
+    non-finite and every other output is finite and within the variant's gate.  SIMT and
+    SPLITK (fp32 FMA) also reproduce the IEEE values, +-Inf or NaN, of `x1 @ x2` on CPU; the
+    tensor split variants may give NaN where IEEE gives +-Inf (a zero low part times an
+    infinite high part)."""
+    g = torch.Generator().manual_seed(31)
+    x1 = torch.randn(300, 520, generator=g)
+    x2 = torch.randn(520, 700, generator=g)
+    x1[5, 17] = float("inf")
+    x1[40, 3] = float("nan")
+    x1[77, 100] = float("-inf")
+    x2[100, 9] = float("-inf")
+    x2[200, 650] = float("nan")
+    ref = x1 @ x2  # CPU fp32, IEEE
+    got = ext._matrix_mul(x1.to(DEV), x2.to(DEV), variant=variant).cpu()
+    bad = ~torch.isfinite(ref)
+    assert bad.any() and (~bad).any()
+    assert torch.equal(~torch.isfinite(got), bad), "non-finite outputs differ from the IEEE pattern"
+    if variant in ("simt", "splitk"):
+        assert torch.equal(torch.isnan(got), torch.isnan(ref))
+        assert torch.equal(got[torch.isinf(ref)], ref[torch.isinf(ref)])
+    fin = ~bad
+    ref64 = (x1.double() @ x2.double())[fin]
+    err = ((got[fin].double() - ref64).norm() / ref64.norm()).item()
+    assert err <= TOL[variant], f"{variant}: finite outputs relFrob {err:.3e}"
+    assert _status_clean()
