@@ -13,7 +13,7 @@
 // Data movement stays local: each CTA TMA-loads only its own halves into its own shared
 // memory with its own mbarriers (plain cta_group::1 TMA, no multicast).  Cross-CTA
 // signalling:
-//   split[s]      (leader)  <- 8 split warps of each CTA, remote mbarrier arrive (release.cluster)
+//   split[s]      (leader)  <- 8 split warps of each CTA, mbarrier arrive on the leader's barrier (release.cta)
 //   empty[s]      (each)    <- leader's tcgen05.commit, multicast to the same barrier in both CTAs
 //   chunk_full[b] (each)    <- leader's tcgen05.commit, multicast to both CTAs
 //   chunk_empty[b](leader)  <- 8 epilogue warps of each CTA after draining their TMEM rows

@@ -70,6 +70,7 @@ def _check_out(out, M, N, device):
 
 
 _WS_BYTES = {}   # (shape, strides, 16-byte alignment of A/B/C, variant, split) -> workspace bytes
+_WS_BYTES_MAX = 4096
 _WS = {}         # (device index, stream handle) -> grow-only workspace tensor
 _installed = False
 
@@ -105,6 +106,8 @@ def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k, flags=0):
         ws_bytes = _WS_BYTES.get(key)
         if ws_bytes is None:
             ws_bytes = lib.tilec_mm_workspace_bytes(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg))
+            if len(_WS_BYTES) >= _WS_BYTES_MAX:  # a process that sees many shapes: start over
+                _WS_BYTES.clear()
             _WS_BYTES[key] = ws_bytes
         ws_ptr = _workspace(dev, stream, ws_bytes).data_ptr() if ws_bytes else None
         rc = lib.tilec_mm_f32(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg), ws_ptr, ws_bytes, stream)
@@ -120,8 +123,9 @@ def _matrix_mul(x1, x2, variant=None, split_k=0, out=None, stream_k=False):
 
     variant: None (= $TILEC_MM_VARIANT or "auto"), "simt", "splitk", "tf32", "3xtf32",
     "3xtf32_masked", "3xmixed" (3xtf32 with its two cross terms on the bf16 tensor pipe;
-    CTA-pair shapes only, others run "3xtf32").  split_k: K slices for split variants (0 = library choice; 1 = none,
-    which also rules out stream-K).  stream_k: run the CTA-pair kernel in its stream-K form
+    CTA-pair shapes only, others run "3xtf32").  split_k: K slices for split variants
+    (0 = library choice; 1 = none, which also rules out stream-K).  stream_k: run the
+    CTA-pair kernel in its stream-K form
     whenever it is the kernel and split_k <= 1 (the library picks it by itself where it
     pays).  out: optional preallocated [M, N] float32 result (unit column stride).
     """
