@@ -554,13 +554,16 @@ def _tf32_exact(rows, cols, g):
 @pytest.mark.parametrize("shape", [(2048, 2048, 2048), (1000, 3001, 777), (300, 520, 700), (4096, 8192, 512)])
 def test_mixed_equals_3xtf32_when_low_parts_vanish(shape):
     """On operands that tf32 holds exactly, l(x) = 0: both cross terms add exact zeros, and
-    the tf32 main product runs in the same K order with the same promotion as 3XTF32, so
-    the two variants agree bit for bit."""
+    the tf32 main product runs in the same K order with the same promotion as 3XTF32 (whose
+    pair kernel takes 32 of K per stage against the mixed kernel's 16, with the same MMA
+    sequence), so with the same K slices the two variants agree bit for bit."""
     m, k, n = shape
     g = torch.Generator().manual_seed(m + k + n)
     a, b = _tf32_exact(m, k, g), _tf32_exact(k, n, g)
     assert ext.plan(a, b, variant="3xmixed")[0] == "3xmixed"
-    assert torch.equal(ext._matrix_mul(a, b, variant="3xmixed"), ext._matrix_mul(a, b, variant="3xtf32"))
+    split = ext.plan(a, b, variant="3xtf32")[1]  # same K slices for both (the plans' speed models differ)
+    assert torch.equal(ext._matrix_mul(a, b, variant="3xmixed", split_k=split),
+                       ext._matrix_mul(a, b, variant="3xtf32", split_k=split))
     assert _status_clean()
 
 

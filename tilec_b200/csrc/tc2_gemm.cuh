@@ -35,16 +35,21 @@
 
 namespace tilec {
 
-// SPLIT3: 3XTF32 (BK 16, raw + lo tiles per stage, K-chunk promotion through two TMEM
-// buffers); otherwise TF32 (BK 32, raw tiles only, one accumulator over all of K, the
-// split warps only relay "stage full" to the leader).
+// SPLIT3: 3XTF32 (raw + lo tiles per stage, K-chunk promotion every 128 of K through two
+// TMEM buffers); otherwise TF32 (raw tiles only, one accumulator over all of K, the split
+// warps only relay "stage full" to the leader).  BK: K per stage, 32 unless BKX says 16
+// (the stream-K form and the mixed split keep 16-deep stages; the one-pair-per-tile 3XTF32
+// kernel runs 3 stages of 32: half the per-stage handshakes of 6 stages of 16 for the same
+// depth in K, 282.7 -> 300.0 TFLOP/s at 8192^3 and 246.7 -> 264.4 on 65536x8192x8192,
+// same box).
 // SK: the stream-K kernel (tc2_sk.cuh) on the same stages: two TMEM buffers in both modes
 // (a segment's sums are read out while the next segment's MMAs run), a smaller barrier
 // area and a 32 x 33 float block per epilogue warp for stores made while the stages
 // still stream.  SK = false is the one-pair-per-tile kernel below.
-template <int BN, int STAGES, bool SPLIT3 = true, bool SK = false>
+template <int BN, int STAGES, bool SPLIT3 = true, bool SK = false, int BKX = 0>
 struct Tc2Cfg {
-  static constexpr int BK = SPLIT3 ? 16 : 32;
+  static constexpr int BK = BKX ? BKX : (SPLIT3 ? 16 : 32);
+  static_assert(BK == 16 || BK == 32, "BK");
   static constexpr int kBNHalf = BN / 2;
   static constexpr int kEpiWarps = 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
@@ -57,18 +62,23 @@ struct Tc2Cfg {
   static constexpr int kBlockBytes = SK ? kEpiWarps * 32 * kBlockPitch * 4 : 0;
   static constexpr int kSmemBytes = STAGES * kStageBytes + 1024 + kBarBytes + kBlockBytes;
   static constexpr uint32_t kASbo = 8u * BK * 4u;       // 8 rows x BK*4 bytes (K-major)
-  static constexpr uint32_t kALayout = SPLIT3 ? kLayoutSw64 : kLayoutSw128;
+  static constexpr uint32_t kALayout = BK == 32 ? kLayoutSw128 : kLayoutSw64;  // BK*4-byte rows
   static constexpr uint32_t kBLbo = BK * 128u;          // stride between 32-column slabs
   static constexpr uint32_t kBSbo = 512u;               // stride between 4-row K groups
   static constexpr uint32_t kTmemCols = (SPLIT3 || SK) ? 2 * BN : BN;  // chunk buffers of BN columns
   static constexpr int kColsPerThread = BN / 2;
-  static constexpr int kChunkBlocks = SPLIT3 ? 8 : (1 << 30);  // TF32: one chunk (per segment)
+  static constexpr int kChunkBlocks = SPLIT3 ? 128 / BK : (1 << 30);  // TF32: one chunk (per segment)
   static constexpr int kPartialFloats = 2 * kEpiWarps * 32 * kColsPerThread;  // one pair's tile
   static_assert(BN == 256 || BN == 128, "BN");
   static_assert(kSmemBytes <= 232448, "shared memory");
   static_assert(kEpiWarps * 32 * (kColsPerThread + 4) * 4 <= STAGES * kStageBytes, "output staging");
   static_assert((3 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");  // mbarriers + TMEM slot + abort flag
 };
+
+// K per stage of the one-pair-per-tile kernel: 32, except 16 for the mixed split (its bf16
+// tiles hold one K=16 bf16 MMA per stage).
+template <bool SPLIT3, bool MIXED>
+constexpr int kTc2Bk = (SPLIT3 && MIXED) ? 16 : 32;
 
 // Operand readers for the mixed split (MIXED below): 8 consecutive k of one row of an fp32
 // stage tile as TMA left it.
@@ -126,14 +136,15 @@ __device__ __forceinline__ uint32_t bf16_tile_offset(int r, int kh) {
 // 3 * 2^-18 relative error per product (2^-18 from bf16(a) and from bf16(h(b)), 2^-19 from
 // each rounded l()), about 1e-6 rms on random data.
 template <int BN, int STAGES, bool SPLIT3, bool HI_EXPLICIT, bool ANY_LAYOUT, bool MIXED = false>
-__global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3>::kThreads, 1)
+__global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, false, kTc2Bk<SPLIT3, MIXED>>::kThreads, 1)
     tc2_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     float* __restrict__ out, int M, int N, int64_t ldo, int64_t out_slab, int K, int k_chunk,
                     int mp_tiles, int n_tiles, int group_m, int vec_out, int layout_arg, int64_t out_batch,
                     const float* __restrict__ bias, int act, int shared) {
   const int layout = ANY_LAYOUT ? layout_arg : 0;
-  using Cfg = Tc2Cfg<BN, STAGES, SPLIT3>;
-  static_assert(!MIXED || (SPLIT3 && !HI_EXPLICIT && BN == 256), "mixed split: 3-product stages, 128-row tiles");
+  using Cfg = Tc2Cfg<BN, STAGES, SPLIT3, false, kTc2Bk<SPLIT3, MIXED>>;
+  static_assert(!MIXED || (SPLIT3 && !HI_EXPLICIT && BN == 256 && Cfg::BK == 16),
+                "mixed split: 3-product stages of 16, 128-row tiles");
   constexpr int BK = Cfg::BK;
   constexpr int KC = Cfg::kChunkBlocks;
   extern __shared__ uint8_t smem_raw[];

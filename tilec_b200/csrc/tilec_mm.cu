@@ -83,6 +83,9 @@ struct TcShape {
 // measured slower), used for M >= kPairMinM and N > 128 (B200: 245 vs 210 TFLOP/s for the
 // 1-CTA kernel at 8192^3).
 constexpr int kPairStages = 6;
+// The one-pair-per-tile 3XTF32 kernel: 3 stages of K = 32 (64 KB each), the same depth in K
+// as 6 stages of 16 with half the per-stage barrier handshakes and commits.
+constexpr int kPair3xStages = 3;
 constexpr int64_t kPairMinM = 256;
 
 cudaError_t init_device_attrs() {
@@ -113,13 +116,15 @@ cudaError_t init_device_attrs() {
     acc(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   };
   // Every (mode, layout) instantiation of both pair kernels that the launch paths use.
-  constexpr int k3x = Tc2Cfg<256, kPairStages, true>::kSmemBytes, kTf = Tc2Cfg<256, kPairStages, false>::kSmemBytes;
-  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, false>, k3x);
-  pair_attr(tc2_gemm_kernel<256, kPairStages, true, true, false>, k3x);
-  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, true>, k3x);
-  pair_attr(tc2_gemm_kernel<256, kPairStages, true, true, true>, k3x);
-  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, false, true>, k3x);
-  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, true, true>, k3x);
+  constexpr int k3x = Tc2Cfg<256, kPair3xStages, true, false, 32>::kSmemBytes;
+  constexpr int kMix = Tc2Cfg<256, kPairStages, true>::kSmemBytes;
+  constexpr int kTf = Tc2Cfg<256, kPairStages, false>::kSmemBytes;
+  pair_attr(tc2_gemm_kernel<256, kPair3xStages, true, false, false>, k3x);
+  pair_attr(tc2_gemm_kernel<256, kPair3xStages, true, true, false>, k3x);
+  pair_attr(tc2_gemm_kernel<256, kPair3xStages, true, false, true>, k3x);
+  pair_attr(tc2_gemm_kernel<256, kPair3xStages, true, true, true>, k3x);
+  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, false, true>, kMix);
+  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, true, true>, kMix);
   pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, false>, kTf);
   pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, true>, kTf);
   constexpr int s3x = Tc2Cfg<256, kPairStages, true, true>::kSmemBytes;
@@ -228,6 +233,7 @@ struct Plan {
   bool tpose_a = false, tpose_b = false;  // SIMT variants: transposed operand -> row-major copy
   bool pair = false;  // 3XTF32 on a CTA pair (tc2_gemm_kernel, 256 x 256 tiles)
   bool sk = false;    // pair kernel in its stream-K form (split == 1)
+  int bk = 16;        // tensor variants: K per pipeline stage of the kernel that runs (TMA box depth)
   int sk_pairs = 0, sk_dp_tiles = 0, sk_tiles = 0, sk_tiles_per_batch = 0;
   size_t off_sk = 0;  // [sk_pairs partial tiles][sk_pairs x 16 ready flags]
   bool a_shared = false, b_shared = false;  // batch > 1 with a zero batch stride
@@ -412,7 +418,11 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
     // The mixed split exists only in the one-pair-per-tile kernel.
     if (variant == TILEC_MM_3XMIXED && !p->pair) p->variant = variant = TILEC_MM_3XTF32;
     const bool mixed = variant == TILEC_MM_3XMIXED;
-    const int bk = variant == TILEC_MM_TF32 ? 32 : k3xBK;
+    // K per stage: 32 for TF32 and the one-pair-per-tile 3XTF32 kernel, 16 otherwise.  K
+    // slices of the pair kernel are multiples of 32 in every variant, so 3XTF32, its masked
+    // form and 3XMIXED cut K at the same points.
+    const int bk = (variant == TILEC_MM_TF32 || (p->pair && !mixed)) ? 32 : k3xBK;
+    const int slice_align = p->pair ? 32 : bk;
     const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
     // The CTA pair launches two CTAs per 256-row x 256-column tile; each computes 128 rows
     // and loads half of the B columns.
@@ -420,12 +430,17 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
     const double cta_s = cta_seconds(kTcBM, p->bn, p->pair ? p->bn / 2 : p->bn, K,
                                      variant == TILEC_MM_TF32 ? kRateTf32 : (mixed ? kRateMix : kRate3x), kBwPerSm);
     p->split = choose_split(ctas, d.sms, cta_s, double(M) * double(round_up(N, 4)) * 4.0 * double(nb),
-                            K / (int64_t(bk) * 4), requested_split, /*one_wave=*/true);
-    p->k_chunk = round_up(cdiv(K, p->split), bk);
+                            K / (int64_t(slice_align) * 4), requested_split, /*one_wave=*/true);
+    p->k_chunk = round_up(cdiv(K, p->split), slice_align);
     p->split = static_cast<int>(cdiv(K, p->k_chunk > 0 ? p->k_chunk : 1));
     if (p->split < 1) p->split = 1;
-    if (p->pair && !mixed && K > 0 && requested_split <= 1 && (want_sk || (requested_split == 0 && p->split == 1)))
-      plan_stream_k(d, M, N, K, nb, bk, cta_s, want_sk, p);
+    p->bk = bk;
+    if (p->pair && !mixed && K > 0 && requested_split <= 1 && (want_sk || (requested_split == 0 && p->split == 1))) {
+      // The stream-K kernel keeps 16-deep stages for 3XTF32.
+      const int sk_bk = variant == TILEC_MM_TF32 ? 32 : k3xBK;
+      plan_stream_k(d, M, N, K, nb, sk_bk, cta_s, want_sk, p);
+      if (p->sk) p->bk = sk_bk;
+    }
   } else {
     p->bn = N <= 64 ? 64 : 128;
     const int64_t tiles = cdiv(M, kSimtBM) * cdiv(N, p->bn) * nb;
@@ -633,7 +648,8 @@ int launch_tc_mode(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int6
 template <bool SPLIT3, bool HI, bool MIXED = false>
 int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
                cudaStream_t s) {
-  using Cfg = Tc2Cfg<256, kPairStages, SPLIT3>;
+  constexpr int kStages = (SPLIT3 && !MIXED) ? kPair3xStages : kPairStages;
+  using Cfg = Tc2Cfg<256, kStages, SPLIT3, false, kTc2Bk<SPLIT3, MIXED>>;
   const int mp_tiles = static_cast<int>(cdiv(M, 256));
   const int n_tiles = static_cast<int>(cdiv(N, 256));
   const int group_m = 8;
@@ -644,8 +660,8 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t 
                     static_cast<int>(N), L.ldo, L.out_slab, static_cast<int>(K), static_cast<int>(L.k_chunk),
                     mp_tiles, n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias, L.act, L.shared);
   };
-  return L.layout ? go(tc2_gemm_kernel<256, kPairStages, SPLIT3, HI, true, MIXED>)
-                  : go(tc2_gemm_kernel<256, kPairStages, SPLIT3, HI, false, MIXED>);
+  return L.layout ? go(tc2_gemm_kernel<256, kStages, SPLIT3, HI, true, MIXED>)
+                  : go(tc2_gemm_kernel<256, kStages, SPLIT3, HI, false, MIXED>);
 }
 
 // Stream-K form: the flag reset (programmatic serialisation on both sides, so the GEMM's
@@ -1014,7 +1030,7 @@ int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, vo
     rc = launch_simt(p.bn, vec, tma_b ? &mbs : nullptr, grid, A, B, M, N, K, lda, ldb, sa, sb, L, d.sms, s);
   } else {
     CUtensorMap ma, mb;
-    const int bk = p.variant == TILEC_MM_TF32 ? 32 : k3xBK;
+    const int bk = p.bk;
     rc = encode_maps(A, B, M, N, K, lda, ldb, sa, na, sb, nbb, bk, L.layout, p.pair ? 128 : p.bn, &ma, &mb);
     if (rc) return rc;
     if (p.sk) {
