@@ -90,13 +90,13 @@ struct PairSeg {
 // Grid: x = 2 x pairs, y = z = 1 (batch and tile come from the schedule); other arguments
 // as tc2_gemm_kernel (no K slices: k_chunk is unused, out_slab 0).
 template <int BN, int STAGES, bool SPLIT3, bool HI_EXPLICIT, bool ANY_LAYOUT>
-__global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, true>::kThreads, 1)
+__global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, true, 32>::kThreads, 1)
     tc2_sk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                   float* __restrict__ out, int M, int N, int64_t ldo, int K, int mp_tiles, int n_tiles,
                   int group_m, int vec_out, int layout_arg, int64_t out_batch, const float* __restrict__ bias,
                   int act, int shared, const Tc2StreamK sk) {
   const int layout = ANY_LAYOUT ? layout_arg : 0;
-  using Cfg = Tc2Cfg<BN, STAGES, SPLIT3, true>;
+  using Cfg = Tc2Cfg<BN, STAGES, SPLIT3, true, 32>;
   constexpr int BK = Cfg::BK;
   constexpr int KC = Cfg::kChunkBlocks;
   constexpr int COLS = Cfg::kColsPerThread;

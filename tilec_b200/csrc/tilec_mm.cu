@@ -127,12 +127,12 @@ cudaError_t init_device_attrs() {
   pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, true, true>, kMix);
   pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, false>, kTf);
   pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, true>, kTf);
-  constexpr int s3x = Tc2Cfg<256, kPairStages, true, true>::kSmemBytes;
-  constexpr int sTf = Tc2Cfg<256, kPairStages, false, true>::kSmemBytes;
-  pair_attr(tc2_sk_kernel<256, kPairStages, true, false, false>, s3x);
-  pair_attr(tc2_sk_kernel<256, kPairStages, true, true, false>, s3x);
-  pair_attr(tc2_sk_kernel<256, kPairStages, true, false, true>, s3x);
-  pair_attr(tc2_sk_kernel<256, kPairStages, true, true, true>, s3x);
+  constexpr int s3x = Tc2Cfg<256, kPair3xStages, true, true, 32>::kSmemBytes;
+  constexpr int sTf = Tc2Cfg<256, kPairStages, false, true, 32>::kSmemBytes;
+  pair_attr(tc2_sk_kernel<256, kPair3xStages, true, false, false>, s3x);
+  pair_attr(tc2_sk_kernel<256, kPair3xStages, true, true, false>, s3x);
+  pair_attr(tc2_sk_kernel<256, kPair3xStages, true, false, true>, s3x);
+  pair_attr(tc2_sk_kernel<256, kPair3xStages, true, true, true>, s3x);
   pair_attr(tc2_sk_kernel<256, kPairStages, false, false, false>, sTf);
   pair_attr(tc2_sk_kernel<256, kPairStages, false, false, true>, sTf);
   return e;
@@ -142,7 +142,7 @@ cudaError_t init_device_attrs() {
 // one GPC, so this can be below SMs / 2).  A stream-K launch never asks for more: its pairs
 // wait on one another's partial tiles.  0 disables stream-K.
 int query_pair_slots() {
-  using Cfg = Tc2Cfg<256, kPairStages, true, true>;
+  using Cfg = Tc2Cfg<256, kPair3xStages, true, true, 32>;
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(2, 1, 1);
   lc.blockDim = dim3(Cfg::kThreads);
@@ -155,7 +155,7 @@ int query_pair_slots() {
   lc.attrs = &attr;
   lc.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, tc2_sk_kernel<256, kPairStages, true, false, false>, &lc) !=
+  if (cudaOccupancyMaxActiveClusters(&n, tc2_sk_kernel<256, kPair3xStages, true, false, false>, &lc) !=
       cudaSuccess) {
     cudaGetLastError();
     return 0;
@@ -350,11 +350,11 @@ constexpr double kRate3x = 1.7e12, kRateMix = 2.4e12, kRateTf32 = 4.3e12, kRateS
 // unless `forced`, when that is at least 3 % faster, every tile has at most three pairs
 // (T >= P / 2) and K has at least 8 blocks.  The tiles of all waves but the last complete
 // one stay one per pair (sk_dp_tiles); the rest, P to 2P - 1 tiles, are shared out.
-constexpr size_t kPartialBytes = size_t(Tc2Cfg<256, kPairStages, true, true>::kPartialFloats) * sizeof(float);
-constexpr int kSkFlagsPerPair = 2 * Tc2Cfg<256, kPairStages, true, true>::kEpiWarps;
+constexpr size_t kPartialBytes = size_t(Tc2Cfg<256, kPair3xStages, true, true, 32>::kPartialFloats) * sizeof(float);
+constexpr int kSkFlagsPerPair = 2 * Tc2Cfg<256, kPair3xStages, true, true, 32>::kEpiWarps;
 
-void plan_stream_k(const DeviceInfo& d, int64_t M, int64_t N, int64_t K, int64_t nb, int bk, double cta_s,
-                   bool forced, Plan* p) {
+void plan_stream_k(const DeviceInfo& d, int64_t M, int64_t N, int64_t K, int64_t nb, int bk, bool tf32,
+                   double cta_s, bool forced, Plan* p) {
   const int64_t P = d.pair_slots;
   if (P <= 0) return;
   const int64_t per_batch = cdiv(M, 256) * cdiv(N, 256);
@@ -362,7 +362,7 @@ void plan_stream_k(const DeviceInfo& d, int64_t M, int64_t N, int64_t K, int64_t
   if (T >= (int64_t(1) << 30)) return;
   if (!forced) {
     if (nkb < 8 || 2 * T < P) return;
-    const double penalty = bk == 32 ? 1.17 : 1.08;
+    const double penalty = tf32 ? 1.17 : 1.08;
     const double dp = double(cdiv(T, P)) * cta_s;
     const double sk = double(T) / double(P) * cta_s * penalty + 5.0e-6;
     if (!(sk < 0.97 * dp)) return;
@@ -436,10 +436,7 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
     if (p->split < 1) p->split = 1;
     p->bk = bk;
     if (p->pair && !mixed && K > 0 && requested_split <= 1 && (want_sk || (requested_split == 0 && p->split == 1))) {
-      // The stream-K kernel keeps 16-deep stages for 3XTF32.
-      const int sk_bk = variant == TILEC_MM_TF32 ? 32 : k3xBK;
-      plan_stream_k(d, M, N, K, nb, sk_bk, cta_s, want_sk, p);
-      if (p->sk) p->bk = sk_bk;
+      plan_stream_k(d, M, N, K, nb, bk, variant == TILEC_MM_TF32, cta_s, want_sk, p);
     }
   } else {
     p->bn = N <= 64 ? 64 : 128;
@@ -671,7 +668,8 @@ int launch_tc2_sk(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64
                   const Tc2StreamK& sk, int pairs, cudaStream_t s) {
   int rc = launch_k(sk_flags_reset_kernel, dim3(1), dim3(256), 0, s, 1, sk.flags, pairs * kSkFlagsPerPair);
   if (rc) return rc;
-  using Cfg = Tc2Cfg<256, kPairStages, SPLIT3, true>;
+  constexpr int kStages = SPLIT3 ? kPair3xStages : kPairStages;
+  using Cfg = Tc2Cfg<256, kStages, SPLIT3, true, 32>;
   const int mp_tiles = static_cast<int>(cdiv(M, 256));
   const int n_tiles = static_cast<int>(cdiv(N, 256));
   const int group_m = 8;
@@ -680,8 +678,8 @@ int launch_tc2_sk(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64
                     mb, L.out, static_cast<int>(M), static_cast<int>(N), L.ldo, static_cast<int>(K), mp_tiles,
                     n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias, L.act, L.shared, sk);
   };
-  return L.layout ? go(tc2_sk_kernel<256, kPairStages, SPLIT3, HI, true>)
-                  : go(tc2_sk_kernel<256, kPairStages, SPLIT3, HI, false>);
+  return L.layout ? go(tc2_sk_kernel<256, kStages, SPLIT3, HI, true>)
+                  : go(tc2_sk_kernel<256, kStages, SPLIT3, HI, false>);
 }
 
 template <bool SPLIT3, bool HI>
