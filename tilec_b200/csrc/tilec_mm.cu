@@ -68,8 +68,10 @@ cudaError_t set_tc_attr() {
 }
 
 // Stages per mode (a 3XTF32 stage holds raw + lo tiles): BN 256: 4 x 48 KB; 128: 6 x 32 KB;
-// 64: 8 x 24 KB.  K per stage of the 1-CTA 3XTF32 kernel: 16 (32 was measured: no faster,
-// and twice the error, since fewer promotions per K).
+// 64: 8 x 24 KB.  K per stage of the 1-CTA 3XTF32 kernel: 16.  32 was measured twice: first
+// no faster and with twice the error (promotion every 256 of K), then, promoting every 128
+// of K, from 6 % faster (256x16384x64) to 16 % slower (200x4096x4096), config 1 1.5 % slower.
+// (The CTA-pair kernel does take 32: see kPair3xStages.)
 constexpr int k3xBK = 16;
 template <int BN>
 struct TcShape {
