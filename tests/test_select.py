@@ -78,3 +78,28 @@ def test_fit_overrides_only_where_builtin_loses():
     assert table and all(r[6] == "simt" for r in table)
     assert select.lookup([t[:6] + [_native.VARIANTS[t[6]], t[7]] for t in table], 2, 2, 2) == ("simt", 0)
     assert select.lookup([t[:6] + [_native.VARIANTS[t[6]], t[7]] for t in table], 4096, 4096, 4096) is None
+
+
+def test_train_ships_a_table_only_when_cross_validation_prefers_it(tmp_path, monkeypatch):
+    """`train` writes the fitted rows only if cross-validation rates them better than the
+    built-in rules; otherwise the table is empty (AUTO stays the built-in rules)."""
+    import csv
+    path = tmp_path / "sweep.csv"
+    with open(path, "w", newline="") as f:
+        w = csv.writer(f)
+        w.writerow(tune.FIELDS)
+        for m, k, n in [(2, 2, 2), (3, 2, 3), (2, 3, 3), (4096, 4096, 4096), (3000, 5000, 4000), (5000, 3000, 6000)]:
+            small = m < 100
+            w.writerow(["x", m, k, n, "builtin", 0, 2.0 if small else 1.0])
+            w.writerow(["x", m, k, n, "simt", 0, 1.0 if small else 5.0])
+            w.writerow(["x", m, k, n, "3xtf32", 0, 2.0 if small else 1.0])
+    base = {"folds": 5, "shuffles": 3, "selector_worst": 1.0, "builtin_worst": 1.0}
+    out = tmp_path / "table.json"
+    monkeypatch.setattr(tune, "cross_validate", lambda rows: dict(base, selector_x_of_best=1.2, builtin_x_of_best=1.0))
+    doc = tune.train(str(path), str(out))
+    assert doc["rows"] == [] and doc["fitted_table_kept"] is False
+    assert json.loads(out.read_text())["rows"] == []
+    monkeypatch.setattr(tune, "cross_validate", lambda rows: dict(base, selector_x_of_best=0.9, builtin_x_of_best=1.0))
+    doc = tune.train(str(path), str(out))
+    assert doc["rows"] and doc["fitted_table_kept"] is True
+    assert all(r[6] == "simt" for r in doc["rows"])
