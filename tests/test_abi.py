@@ -49,7 +49,9 @@ def test_abi_constants_match_header():
     assert lib.tilec_mm_built_arch() == 100
     for name, code in re.findall(r"(TILEC_(?:OK|ERR_\w+))\s*=\s*(\d+)", h):
         assert _native.STATUS_NAMES[int(code)] == name
-    for name, code in re.findall(r"TILEC_MM_(AUTO|SIMT|SPLITK|TF32|3XTF32|3XTF32_MASKED)\s*=\s*(\d+)", h):
+    found = re.findall(r"TILEC_MM_(AUTO|SIMT|SPLITK|TF32|3XTF32|3XTF32_MASKED|3XMIXED)\s*=\s*(\d+)", h)
+    assert {name.lower() for name, _ in found} == set(_native.VARIANTS), "header and binding list the same variants"
+    for name, code in found:
         assert _native.VARIANTS[name.lower()] == int(code)
     assert ctypes.sizeof(_native.MMConfig) == 32
 
