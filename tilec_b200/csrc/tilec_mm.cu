@@ -81,12 +81,12 @@ struct TcShape {
 
 
 
-// CTA-pair 3XTF32 kernel (tc2_gemm_kernel): 256 x 256 tiles, 6 stages of 32 KB (4 were
-// measured slower), used for M >= kPairMinM and N > 128 (B200: 245 vs 210 TFLOP/s for the
-// 1-CTA kernel at 8192^3).
+// CTA-pair kernels (tc2_gemm_kernel, tc2_sk_kernel): 256 x 256 tiles, used for
+// M >= kPairMinM and N > 128 (B200: 245 vs 210 TFLOP/s for the 1-CTA kernel at 8192^3).
+// TF32 and the mixed split: 6 stages of 32 KB (4 were measured slower).
 constexpr int kPairStages = 6;
-// The one-pair-per-tile 3XTF32 kernel: 3 stages of K = 32 (64 KB each), the same depth in K
-// as 6 stages of 16 with half the per-stage barrier handshakes and commits.
+// 3XTF32 (both forms): 3 stages of K = 32 (64 KB each), the same depth in K as 6 stages of
+// 16 with half the per-stage barrier handshakes and commits.
 constexpr int kPair3xStages = 3;
 constexpr int64_t kPairMinM = 256;
 
