@@ -75,51 +75,54 @@ struct Tc2Cfg {
   static_assert((3 * STAGES + 5) * 8 + 8 <= kBarBytes, "barrier area");  // mbarriers + TMEM slot + abort flag
 };
 
-// K per stage of the one-pair-per-tile kernel: 32, except 16 for the mixed split (its bf16
-// tiles hold one K=16 bf16 MMA per stage).
+// K per stage of the one-pair-per-tile kernel (every variant): 32.
 template <bool SPLIT3, bool MIXED>
-constexpr int kTc2Bk = (SPLIT3 && MIXED) ? 16 : 32;
+constexpr int kTc2Bk = 32;
 
 // Operand readers for the mixed split (MIXED below): 8 consecutive k of one row of an fp32
-// stage tile as TMA left it.
-//   K-major tile ([rows x 16] fp32, 64-byte rows, 64-byte swizzle: the 16-byte granule
-//   index, address bits 4-5, is XORed with bits 7-8, i.e. with (row >> 1) & 3):
-__device__ __forceinline__ void read_kmajor8(const uint8_t* tile, int r, int kh, float (&v)[8]) {
-  const uint8_t* row = tile + r * 64;
-  const int sw = (r >> 1) & 3;
-  const float4 x0 = *reinterpret_cast<const float4*>(row + 16 * ((2 * kh) ^ sw));
-  const float4 x1 = *reinterpret_cast<const float4*>(row + 16 * ((2 * kh + 1) ^ sw));
+// stage tile of depth BK as TMA left it.
+//   K-major tile ([rows x BK] fp32, BK*4-byte rows, BK*4-byte swizzle: the 16-byte granule
+//   index is XORed with (row >> 1) & 3 for 64-byte rows, with row & 7 for 128-byte rows):
+//   chunk kc holds k 8kc .. 8kc+7.
+template <int BK>
+__device__ __forceinline__ void read_kmajor8(const uint8_t* tile, int r, int kc, float (&v)[8]) {
+  const uint8_t* row = tile + r * (BK * 4);
+  const int sw = BK == 32 ? (r & 7) : ((r >> 1) & 3);
+  const float4 x0 = *reinterpret_cast<const float4*>(row + 16 * ((2 * kc) ^ sw));
+  const float4 x1 = *reinterpret_cast<const float4*>(row + 16 * ((2 * kc + 1) ^ sw));
   v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
   v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
 }
 // 8 consecutive MN indices 8q..8q+7 at one k of an MN-major fp32 stage tile (slabs of
-// [16 k x 32] fp32 2 KB apart, 128-byte rows with 32-byte granules: granule index, address
-// bits 5-6, XORed with bits 7-8, i.e. with k & 3): one granule, two 16-byte loads.  Odd
-// slabs read their upper half first, so a quarter warp's eight loads cover all 32 banks.
+// [BK k x 32] fp32 BK*128 bytes apart, 128-byte rows with 32-byte granules: granule index,
+// address bits 5-6, XORed with bits 7-8, i.e. with k & 3): one granule, two 16-byte loads.
+// Odd slabs read their upper half first, so a quarter warp's eight loads cover all 32 banks.
+template <int BK>
 __device__ __forceinline__ void read_mnmajor_chunk8(const uint8_t* tile, int k, int q, float (&v)[8]) {
   const int j = q >> 2, h0 = j & 1;
-  const uint8_t* g = tile + j * 2048 + k * 128 + 32 * ((q & 3) ^ (k & 3));
+  const uint8_t* g = tile + j * (BK * 128) + k * 128 + 32 * ((q & 3) ^ (k & 3));
   const float4 x0 = *reinterpret_cast<const float4*>(g + 16 * h0);
   const float4 x1 = *reinterpret_cast<const float4*>(g + 16 * (h0 ^ 1));
   const float4 lo = h0 ? x1 : x0, hi = h0 ? x0 : x1;
   v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
   v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
 }
-// Byte offset of MN indices 8q..8q+7 at k (16 bytes) in a [16 x 128] bf16 tile laid out
+// Byte offset of MN indices 8q..8q+7 at k (16 bytes) in a [BK x 128] bf16 tile laid out
 // MN-major with the 128-byte swizzle: 64-element (128-byte) rows along MN, the 16-byte chunk
-// index XORed with k & 7; the two 64-wide MN halves 1 KB apart (LBO), the two 8-row K
-// groups 2 KB apart (SBO).  A quarter warp storing one k's 8 chunks fills one 128-byte row.
+// index XORed with k & 7; the two 64-wide MN halves 1 KB apart (LBO), 8-row K groups 2 KB
+// apart (SBO).  A quarter warp storing one k's 8 chunks fills one 128-byte row.
 __device__ __forceinline__ uint32_t bf16_mn_tile_offset(int k, int q) {
   return (k >> 3) * 2048 + (q >> 3) * 1024 + (k & 7) * 128 + (((q & 7) ^ (k & 7)) << 4);
 }
-// Byte offset of row r, k in [8kh, 8kh+8) (16 bytes) in a [128 x 16] bf16 tile laid out
-// K-major with the 32-byte swizzle, as the kind::f16 descriptors describe it: 32-byte rows,
-// the 16-byte half selected by kh XORed with address bit 7, i.e. with (r >> 2) & 1; 8-row
-// groups 256 bytes apart (SBO).  A quarter warp storing 8 consecutive rows of one K half
-// covers all 32 banks.  (A no-swizzle layout with the K halves 2 KB apart measured 3 %
-// slower.)
-__device__ __forceinline__ uint32_t bf16_tile_offset(int r, int kh) {
-  return r * 32 + 16 * (kh ^ ((r >> 2) & 1));
+// Byte offset of row r, chunk kc (k 8kc .. 8kc+7, 16 bytes) in a [128 x BK] bf16 tile laid
+// out K-major with the BK*2-byte swizzle, as the kind::f16 descriptors describe it: BK*2-byte
+// rows, the 16-byte chunk index XORed with (r >> 2) & 1 (32-byte rows) or (r >> 1) & 3
+// (64-byte rows); 8-row groups BK*16 bytes apart (SBO).  A quarter warp storing 8 consecutive
+// rows of one chunk covers all 32 banks.  (A no-swizzle layout with the K halves 2 KB apart
+// measured 3 % slower at BK 16.)
+template <int BK>
+__device__ __forceinline__ uint32_t bf16_tile_offset(int r, int kc) {
+  return BK == 32 ? r * 64 + 16 * (kc ^ ((r >> 1) & 3)) : r * 32 + 16 * (kc ^ ((r >> 2) & 1));
 }
 
 // M = 256 (pair), N = BN, kind::tf32; A K-major and B MN-major unless `layout` flips
@@ -143,8 +146,8 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, false, kTc2Bk<SPLIT
                     const float* __restrict__ bias, int act, int shared) {
   const int layout = ANY_LAYOUT ? layout_arg : 0;
   using Cfg = Tc2Cfg<BN, STAGES, SPLIT3, false, kTc2Bk<SPLIT3, MIXED>>;
-  static_assert(!MIXED || (SPLIT3 && !HI_EXPLICIT && BN == 256 && Cfg::BK == 16),
-                "mixed split: 3-product stages of 16, 128-row tiles");
+  static_assert(!MIXED || (SPLIT3 && !HI_EXPLICIT && BN == 256 && (Cfg::BK == 16 || Cfg::BK == 32)),
+                "mixed split: 3-product stages, 128-row tiles");
   constexpr int BK = Cfg::BK;
   constexpr int KC = Cfg::kChunkBlocks;
   extern __shared__ uint8_t smem_raw[];
@@ -293,14 +296,23 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, false, kTc2Bk<SPLIT
           const uint64_t ad = desc_a(a_hi, kk), bd = desc_b(b_hi, kk);
           const uint32_t accum = (chunk_start && kk == 0) ? 0u : 1u;
           if constexpr (MIXED) {
-            if (kk == 0) {  // both cross terms first (bf16, K = 16 covers the stage)
+            if (kk == 0) {  // the stage's cross terms first: two bf16 MMAs (K = 16) per 16 of K
+              constexpr uint32_t kTile = 128 * BK * 2;  // one bf16 tile
               const uint32_t la = smem_u32(a_lo(s)), lb = smem_u32(b_lo(s));
               const uint32_t idesc16 = make_idesc_bf16(256, BN, a_mn, !b_k);
-              auto d16 = [](uint32_t base, bool mn) {
-                return mn ? make_smem_desc(base, 1024, 2048, kLayoutSw128) : make_smem_desc(base, 16, 256, kLayoutSw32);
+              // K step h (16 of K): 32 bytes along a K-major row, or two 8-row K groups of an
+              // MN-major tile.
+              auto d16 = [](uint32_t base, bool mn, int h) {
+                return mn ? make_smem_desc(base + h * 4096, 1024, 2048, kLayoutSw128)
+                          : make_smem_desc(base + h * 32, 16, BK * 16, BK == 32 ? kLayoutSw64 : kLayoutSw32);
               };
-              umma_bf16_pair(tmem + dcol, d16(la, a_mn), d16(lb, !b_k), idesc16, accum);                // a . l(b)
-              umma_bf16_pair(tmem + dcol, d16(la + 4096, a_mn), d16(lb + 4096, !b_k), idesc16, 1u);  // l(a) . h(b)
+#pragma unroll
+              for (int h = 0; h < BK / 16; ++h) {
+                umma_bf16_pair(tmem + dcol, d16(la, a_mn, h), d16(lb, !b_k, h), idesc16,
+                               h == 0 ? accum : 1u);                                             // a . l(b)
+                umma_bf16_pair(tmem + dcol, d16(la + kTile, a_mn, h), d16(lb + kTile, !b_k, h), idesc16,
+                               1u);                                                              // l(a) . h(b)
+              }
             }
             umma_tf32_pair(tmem + dcol, ad, bd, idesc, 1u);
           } else if constexpr (SPLIT3) {
@@ -362,20 +374,23 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, false, kTc2Bk<SPLIT
       const uint32_t ph = (kb / STAGES) & 1;
       if (!mbar_wait(&full[s], ph, abort_flag)) { ok = false; break; }
       if constexpr (MIXED) {
-        // Each operand tile's bf16 copies keep its major-ness.  K-major: one (row, K half)
-        // unit per thread, warps 0-3 of the eight taking k 0-7 and warps 4-7 k 8-15 for 32
-        // consecutive rows each; MN-major: one (k, 8 MN indices) chunk per thread, 16 per k.
-        // Either way each quarter warp's 16-byte loads and stores cover all 32 banks.
-        auto to_bf16 = [&](const uint8_t* raw, uint8_t* dst, bool mn, bool lhs) {
+        // Each operand tile's bf16 copies keep its major-ness.  BK / 16 units per thread.
+        // K-major: (row, 8-k chunk) units, warps 0-3 of the eight taking the even chunks and
+        // warps 4-7 the odd ones for 32 consecutive rows each; MN-major: (k, 8 MN indices)
+        // chunks, 16 per k.  Either way each quarter warp's 16-byte loads and stores cover all
+        // 32 banks.
+        constexpr uint32_t kTile = 128 * BK * 2;  // one bf16 tile
+        auto to_bf16 = [&](const uint8_t* raw, uint8_t* dst, bool mn, bool lhs, int u) {
           float v[8];
           uint32_t off;
           if (mn) {
-            read_mnmajor_chunk8(raw, et >> 4, et & 15, v);
-            off = bf16_mn_tile_offset(et >> 4, et & 15);
+            const int k = (et >> 4) + 16 * u, q = et & 15;
+            read_mnmajor_chunk8<BK>(raw, k, q, v);
+            off = bf16_mn_tile_offset(k, q);
           } else {
-            const int r = (e & 3) * 32 + lane, kh = e >> 2;
-            read_kmajor8(raw, r, kh, v);
-            off = bf16_tile_offset(r, kh);
+            const int r = (e & 3) * 32 + lane, kc = (e >> 2) + 2 * u;
+            read_kmajor8<BK>(raw, r, kc, v);
+            off = bf16_tile_offset<BK>(r, kc);
           }
           uint4 o0, o1;
           uint32_t* p0 = &o0.x;
@@ -393,10 +408,13 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, false, kTc2Bk<SPLIT
             }
           }
           *reinterpret_cast<uint4*>(dst + off) = o0;
-          *reinterpret_cast<uint4*>(dst + 4096 + off) = o1;
+          *reinterpret_cast<uint4*>(dst + kTile + off) = o1;
         };
-        to_bf16(a_raw(s), a_lo(s), (layout & kOpAMN) != 0, true);
-        to_bf16(b_raw(s), b_lo(s), (layout & kOpBK) == 0, false);
+#pragma unroll
+        for (int u = 0; u < BK / 16; ++u) {
+          to_bf16(a_raw(s), a_lo(s), (layout & kOpAMN) != 0, true, u);
+          to_bf16(b_raw(s), b_lo(s), (layout & kOpBK) == 0, false, u);
+        }
         fence_proxy_async_smem();
       } else if constexpr (SPLIT3) {
         float4* src_a = reinterpret_cast<float4*>(a_raw(s));

@@ -83,10 +83,10 @@ struct TcShape {
 
 // CTA-pair kernels (tc2_gemm_kernel, tc2_sk_kernel): 256 x 256 tiles, used for
 // M >= kPairMinM and N > 128 (B200: 245 vs 210 TFLOP/s for the 1-CTA kernel at 8192^3).
-// TF32 and the mixed split: 6 stages of 32 KB (4 were measured slower).
+// TF32: 6 stages of 32 KB (4 were measured slower).
 constexpr int kPairStages = 6;
-// 3XTF32 (both forms): 3 stages of K = 32 (64 KB each), the same depth in K as 6 stages of
-// 16 with half the per-stage barrier handshakes and commits.
+// 3XTF32 (both forms) and the mixed split: 3 stages of K = 32 (64 KB each), the same depth
+// in K as 6 stages of 16 with half the per-stage barrier handshakes and commits.
 constexpr int kPair3xStages = 3;
 constexpr int64_t kPairMinM = 256;
 
@@ -119,14 +119,14 @@ cudaError_t init_device_attrs() {
   };
   // Every (mode, layout) instantiation of both pair kernels that the launch paths use.
   constexpr int k3x = Tc2Cfg<256, kPair3xStages, true, false, 32>::kSmemBytes;
-  constexpr int kMix = Tc2Cfg<256, kPairStages, true>::kSmemBytes;
+  constexpr int kMix = Tc2Cfg<256, kPair3xStages, true, false, 32>::kSmemBytes;
   constexpr int kTf = Tc2Cfg<256, kPairStages, false>::kSmemBytes;
   pair_attr(tc2_gemm_kernel<256, kPair3xStages, true, false, false>, k3x);
   pair_attr(tc2_gemm_kernel<256, kPair3xStages, true, true, false>, k3x);
   pair_attr(tc2_gemm_kernel<256, kPair3xStages, true, false, true>, k3x);
   pair_attr(tc2_gemm_kernel<256, kPair3xStages, true, true, true>, k3x);
-  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, false, true>, kMix);
-  pair_attr(tc2_gemm_kernel<256, kPairStages, true, false, true, true>, kMix);
+  pair_attr(tc2_gemm_kernel<256, kPair3xStages, true, false, false, true>, kMix);
+  pair_attr(tc2_gemm_kernel<256, kPair3xStages, true, false, true, true>, kMix);
   pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, false>, kTf);
   pair_attr(tc2_gemm_kernel<256, kPairStages, false, false, true>, kTf);
   constexpr int s3x = Tc2Cfg<256, kPair3xStages, true, true, 32>::kSmemBytes;
@@ -420,10 +420,10 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
     // The mixed split exists only in the one-pair-per-tile kernel.
     if (variant == TILEC_MM_3XMIXED && !p->pair) p->variant = variant = TILEC_MM_3XTF32;
     const bool mixed = variant == TILEC_MM_3XMIXED;
-    // K per stage: 32 for TF32 and the one-pair-per-tile 3XTF32 kernel, 16 otherwise.  K
-    // slices of the pair kernel are multiples of 32 in every variant, so 3XTF32, its masked
-    // form and 3XMIXED cut K at the same points.
-    const int bk = (variant == TILEC_MM_TF32 || (p->pair && !mixed)) ? 32 : k3xBK;
+    // K per stage: 32 for TF32 and every pair-kernel variant, 16 in the 1-CTA 3XTF32 kernel.
+    // K slices of the pair kernel are multiples of 32, so 3XTF32, its masked form and
+    // 3XMIXED cut K at the same points.
+    const int bk = (variant == TILEC_MM_TF32 || p->pair) ? 32 : k3xBK;
     const int slice_align = p->pair ? 32 : bk;
     const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
     // The CTA pair launches two CTAs per 256-row x 256-column tile; each computes 128 rows
@@ -647,7 +647,7 @@ int launch_tc_mode(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int6
 template <bool SPLIT3, bool HI, bool MIXED = false>
 int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
                cudaStream_t s) {
-  constexpr int kStages = (SPLIT3 && !MIXED) ? kPair3xStages : kPairStages;
+  constexpr int kStages = SPLIT3 ? kPair3xStages : kPairStages;
   using Cfg = Tc2Cfg<256, kStages, SPLIT3, false, kTc2Bk<SPLIT3, MIXED>>;
   const int mp_tiles = static_cast<int>(cdiv(M, 256));
   const int n_tiles = static_cast<int>(cdiv(N, 256));
