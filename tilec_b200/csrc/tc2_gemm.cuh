@@ -37,18 +37,17 @@ namespace tilec {
 
 // SPLIT3: 3XTF32 (raw + lo tiles per stage, K-chunk promotion every 128 of K through two
 // TMEM buffers); otherwise TF32 (raw tiles only, one accumulator over all of K, the split
-// warps only relay "stage full" to the leader).  BK: K per stage, 32 unless BKX says 16
-// (the stream-K form and the mixed split keep 16-deep stages; the one-pair-per-tile 3XTF32
-// kernel runs 3 stages of 32: half the per-stage handshakes of 6 stages of 16 for the same
-// depth in K, 282.7 -> 300.0 TFLOP/s at 8192^3 and 246.7 -> 264.4 on 65536x8192x8192,
-// same box).
+// warps only relay "stage full" to the leader).  BK: K per stage, 32 in every pair kernel
+// (BKX = 16 builds the 16-deep form).  With raw + lo tiles a 32-deep stage is 64 KB, so
+// 3XTF32 runs 3 stages: half the per-stage handshakes of 6 stages of 16 for the same depth
+// in K, 282.7 -> 300.0 TFLOP/s at 8192^3 and 246.7 -> 264.4 on 65536x8192x8192, same box.
 // SK: the stream-K kernel (tc2_sk.cuh) on the same stages: two TMEM buffers in both modes
 // (a segment's sums are read out while the next segment's MMAs run), a smaller barrier
 // area and a 32 x 33 float block per epilogue warp for stores made while the stages
 // still stream.  SK = false is the one-pair-per-tile kernel below.
 template <int BN, int STAGES, bool SPLIT3 = true, bool SK = false, int BKX = 0>
 struct Tc2Cfg {
-  static constexpr int BK = BKX ? BKX : (SPLIT3 ? 16 : 32);
+  static constexpr int BK = BKX ? BKX : 32;
   static_assert(BK == 16 || BK == 32, "BK");
   static constexpr int kBNHalf = BN / 2;
   static constexpr int kEpiWarps = 8;
