@@ -356,7 +356,7 @@ def extra_configs(pk):
                 a = torch.randn(m, k, device="cuda", generator=g)
                 b = torch.randn(k, n, device="cuda", generator=g)
             xs.append((a, b, torch.empty(m, n, device="cuda")))
-        variant, split = ext.plan(xs[0][0], xs[0][1])
+        variant, split = ext.kernel_plan(xs[0][0], xs[0][1])
         i = [0]
 
         def step():
@@ -379,6 +379,11 @@ def extra_configs(pk):
                 step()
         replays = max(3, -(-reps // copies))
         ms = time_launches(graph.replay, replays, warm=2) / copies
+        a0, b0, c0 = xs[0]
+        ext._matrix_mul(a0, b0, out=c0)
+        ref0 = a0.double() @ b0.double()
+        relfrob = ((c0.double() - ref0).norm() / ref0.norm()).item()
+        del ref0
         flops = 2.0 * m * n * k
         tfl = flops / (ms * 1e-3) / 1e12
         peak, note = variant_peak(variant, pk, sustained=False)
@@ -391,12 +396,38 @@ def extra_configs(pk):
                      "peak_note": note, "l2": f"rotating {copies} input sets ({copies * per / 2**20:.0f} MiB > L2)",
                      "timing": f"CUDA graph of {copies} launches (one per input set) replayed {replays}x, CUDA "
                                "events; device time per launch incl. inter-kernel gaps",
+                     "relfrob_vs_fp64": float(f"{relfrob:.3e}"), "gate": gate_for(variant),
                      "ms_eager": round(ms_eager, 5),
                      "eager_timing": f"mean of {reps} back-to-back Python calls (host launch path included)"}
         del graph
         del xs
         torch.cuda.empty_cache()
     return out
+
+
+def gate_for(variant):
+    """relFrob gate of a variant against fp64: 5e-3 for plain TF32, 1e-5 otherwise."""
+    return 5e-3 if variant == "tf32" else 1e-5
+
+
+def sampled_rows(m, n_rows, device):
+    """n_rows row indices spread evenly over [0, m) (first and last included)."""
+    return torch.linspace(0, m - 1, min(n_rows, m), device=device).round().long()
+
+
+def parity_check(x1, x2_full, out, rows, chunk=4096):
+    """This rank's shard against fp64: (relFrob of the sampled rows, relative error of the
+    row-checksum identity C.1 = x1.(x2.1) over every row, fp64 reference of the sampled rows)."""
+    ref = x1[rows].double() @ x2_full.double()
+    err_rows = ((out[rows].double() - ref).norm() / ref.norm()).item()
+    v = x2_full.double().sum(1)
+    num = den = 0.0
+    for r0 in range(0, x1.shape[0], chunk):
+        want = x1[r0:r0 + chunk].double() @ v
+        got = out[r0:r0 + chunk].double().sum(1)
+        num += ((got - want) ** 2).sum().item()
+        den += (want ** 2).sum().item()
+    return err_rows, (num / den) ** 0.5 if den else 0.0, ref
 
 
 def other_variants(x1, x2, out, pk, names=("3xmixed", "tf32")):
@@ -418,7 +449,7 @@ def other_variants(x1, x2, out, pk, names=("3xmixed", "tf32")):
         err = ((out[rows].double() - ref).norm() / ref.norm()).item()
         res[v] = {"ms": round(ms, 3), "tflops": round(tfl, 2), "roofline_tflops": round(peak, 2),
                   "roofline_frac": round(tfl / peak, 4), "peak_note": note,
-                  "relfrob_sampled_rows": float(f"{err:.3e}"), "plan": ext.plan(x1, x2, variant=v)[0]}
+                  "relfrob_sampled_rows": float(f"{err:.3e}"), "plan": ext.kernel_plan(x1, x2, variant=v)[0]}
     return res
 
 
@@ -448,7 +479,7 @@ def main():
         os.environ["TILEC_MM_VARIANT"] = args.variant
     op = RowShardedMatmul(K5, N5, panels=args.panels, device=dev)
     panel_w = op.bounds[0][1] - op.bounds[0][0]
-    variant, split = ext.plan(x1, x2 if world == 1 else torch.empty(K5, panel_w, device=dev))
+    variant, split = ext.kernel_plan(x1, x2 if world == 1 else torch.empty(K5, panel_w, device=dev))
 
     gemm_events = []
 
@@ -517,6 +548,23 @@ def main():
         if key in tr:
             traffic = tr[key]["bytes"]
 
+    # Correctness of the timed product at every GPU count: each rank checks its shard of C
+    # (16 sampled rows against fp64, and the row-checksum identity over all its rows); the
+    # worst figures over the ranks go into the line, and a run above the gate exits non-zero.
+    x2_full = x2 if world == 1 else (torch.cat(op.bufs, 1) if len(op.bufs) > 1 else op.bufs[0])
+    rows_chk = sampled_rows(rows, 16, dev)
+    err_rows, err_sum, ref_rows = parity_check(x1, x2_full, out, rows_chk)
+    del x2_full
+    par = torch.tensor([err_rows, err_sum], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(par, op=dist.ReduceOp.MAX)
+    gate = gate_for(variant)
+    parity = {"relfrob_sampled_rows_max": float(f"{par[0].item():.3e}"),
+              "checksum_rel_max": float(f"{par[1].item():.3e}"), "gate": gate,
+              "rows_per_rank": int(rows_chk.numel()),
+              "how": "each rank: 16 evenly spaced rows of its C shard vs x1[rows].double() @ x2.double(), and "
+                     "C.1 = x1.(x2.1) in fp64 over all its rows; max over ranks"}
+
     # The same product in the other tensor-core variants (rank 0 at N = 1; before the end-to-
     # end leg frees the device inputs).
     others = None
@@ -578,6 +626,12 @@ def main():
             bound = ("host side shared by all ranks: all ranks' H2D + D2H bytes over the sum of the rates "
                      "measured with every rank copying at once (per-rank rates below are under that contention)")
         e2e["link"] = dict(link, bound=bound, floor_ms=round(floor_ms, 3), frac_of_floor=round(floor_ms / e2e_ms, 4))
+        # The host-buffer product is checked on the same sampled rows.
+        got = h_out[rows_chk.cpu()].to(dev).double()
+        pe = torch.tensor([((got - ref_rows).norm() / ref_rows.norm()).item()], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(pe, op=dist.ReduceOp.MAX)
+        parity["e2e_relfrob_sampled_rows_max"] = float(f"{pe.item():.3e}")
 
     extra = None
     cpu = None
@@ -587,6 +641,8 @@ def main():
         if not args.no_cpu:
             cpu = cpu_baseline()
 
+    ok_parity = (parity["relfrob_sampled_rows_max"] <= gate and parity["checksum_rel_max"] <= gate
+                 and parity.get("e2e_relfrob_sampled_rows_max", 0.0) <= gate)
     if rank == 0:
         launches_per_step = op.gemm_launches_per_call * (1 + (1 if split > 1 else 0))
         line = {
@@ -613,6 +669,7 @@ def main():
                          "frac_of_sustained": round(achieved / peak_sus, 4),
                          "sustained_note": "measured bf16 sustained (seconds back to back, power-capped clock) "
                                            "on the same pipe; the clocks line gives this run's SM clock"},
+            "parity": dict(parity, ok=ok_parity),
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": int(launches_per_step * args.steps),
@@ -626,6 +683,9 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if not ok_parity:
+        print(f"bench: parity check failed: {parity}", file=sys.stderr, flush=True)
+        sys.exit(3)
 
 
 if __name__ == "__main__":

@@ -25,7 +25,12 @@
  * legacy default stream).  They allocate no memory, never synchronise the device and
  * never throw; errors come back as a tilec_status code.  Kernels never trap: a fault
  * detected on the device is recorded in a device status word that
- * tilec_mm_device_status() reads.
+ * tilec_mm_device_status() reads.  Every wait inside a kernel is bounded (2 s by default,
+ * tilec_mm_set_wait_limit); a kernel that gives up sets TILEC_DEV_STATUS_TIMEOUT, lets
+ * its in-flight copies and MMAs land, and writes NaN over every output tile it owns
+ * (C, or the split-K / stream-K partial sums, whose NaN then reaches C), so a product
+ * that did not finish never reads as a finished one.  Callers that cannot tolerate NaN
+ * check the status word after the call.
  */
 #ifndef TILEC_MM_H
 #define TILEC_MM_H
@@ -37,7 +42,7 @@
 extern "C" {
 #endif
 
-#define TILEC_MM_ABI_VERSION 5
+#define TILEC_MM_ABI_VERSION 6
 
 #if defined(__GNUC__)
 #define TILEC_API __attribute__((visibility("default")))
@@ -181,6 +186,15 @@ TILEC_API int tilec_mm_set_table(const int32_t* rows, int32_t nrows);
  * Synchronises `stream`. */
 TILEC_API int tilec_mm_device_status(void* stream, int32_t* status_out);
 
+/* Failure-detection control (no counterpart in the reference).  Sets the limit of every
+ * bounded wait inside this library's kernels on the current device to `limit_ns`
+ * nanoseconds (0 restores the default of 2 s; larger values are clamped to 2 s), in
+ * stream order on `stream`, and synchronises `stream`.  Tests shorten it so that a real
+ * GEMM launch gives up -- its output tiles then read NaN and the status word reads
+ * TILEC_DEV_STATUS_TIMEOUT -- and then restore it; the context stays usable throughout.
+ * Device-wide state: do not lower it while products of other callers run on the device. */
+TILEC_API int tilec_mm_set_wait_limit(int64_t limit_ns, void* stream);
+
 /* Failure-detection self-test (no counterpart in the reference).  Launches one CTA on
  * `stream` that waits on a shared-memory mbarrier nothing ever arrives on, through the
  * same bounded wait every GEMM kernel uses, with a limit of `limit_ns` nanoseconds
@@ -215,9 +229,11 @@ TILEC_API int tilec_mm_built_arch(void);
  * nothing is freed, here or in any later call.
  *
  * split_k: number of K slices, or 0 to let the library choose (it then picks at most as
- * many as fit).  An explicit split_k > 1 whose partial sums need more than
- * split_k * M * round_up(N, 4) * 4 > TILEC_MM_NOALLOC_SCRATCH_BYTES bytes returns
- * TILEC_ERR_TOO_LARGE.  Every partial sum the reduction reads is written earlier in the
+ * many as fit).  An explicit split_k is capped at 64 and then rounded to whole 16-deep
+ * K blocks per slice, so the slices that run are S = cdiv(K, round_up(cdiv(K, s), 16))
+ * with s = min(split_k, 64); when S > 1 and their partial sums, S * M * round_up(N, 4) * 4
+ * bytes, exceed TILEC_MM_NOALLOC_SCRATCH_BYTES, the call returns TILEC_ERR_TOO_LARGE and
+ * launches nothing.  Every partial sum the reduction reads is written earlier in the
  * same call, so the array needs no clearing between calls; but all calls share it, so
  * calls that may overlap on the GPU (different streams, or different host threads without
  * ordering) race: serialise them on one stream. */

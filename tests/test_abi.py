@@ -105,3 +105,10 @@ def test_transposed_operand_leading_dimensions():
         # valid for the transposed layouts: gets past the argument checks to the device
         assert lib.tilec_mm_f32(16, 16, 16, M, N, K, 8, N, N, ctypes.byref(ta), None, 0, None) == 3
         assert lib.tilec_mm_f32(16, 16, 16, M, N, K, K, K, N, ctypes.byref(tb), None, 0, None) == 3
+
+
+def test_wait_limit_rejects_negative_before_device():
+    lib = _native.load()
+    assert lib.tilec_mm_set_wait_limit(-1, None) == 1  # TILEC_ERR_BAD_ARG
+    assert _native.status_bits(0) == "clean"
+    assert _native.status_bits(1) == "TIMEOUT" and _native.status_bits(5) == "TIMEOUT|BAD_LAUNCH"

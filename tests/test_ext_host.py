@@ -65,11 +65,11 @@ def test_operand_views_pass_through():
 
 def test_cdiv_and_configs():
     assert cdiv(5000, 4096) == 2 and cdiv(0, 64) == 0
-    cfgs = ext.mm_configs(512, 4096, 64)
+    cfgs = ext.kernel_configs(512, 4096, 64)
     assert ("simt", 1) in cfgs and ("3xtf32", 1) in cfgs
     assert all(v in ("simt", "splitk", "tf32", "3xtf32") for v, _ in cfgs)
     # misaligned shapes still get tensor-core candidates (their operands are packed first)
-    assert ("3xtf32", 1) in ext.mm_configs(1000, 3001, 777)
+    assert ("3xtf32", 1) in ext.kernel_configs(1000, 3001, 777)
 
 
 @pytest.mark.parametrize("M,chunks", [(65536, 8), (65536, 16), (8192, 3), (4096, 4), (1000, 8), (300, 2), (1, 8),

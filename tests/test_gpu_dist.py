@@ -48,7 +48,7 @@ def _worker(rank, world, port, q, M, K, N, panels):
         h_rows = op.run_host(x1_full[r0:r1].cpu().pin_memory(), x2_full.cpu().pin_memory() if rank == 0 else None,
                              chunks=3)
         shard = x1_full[r0:r1].contiguous()
-        sk = any(ext.plan(shard, buf, detail=True)["stream_k"] for buf in op.bufs)
+        sk = any(ext.kernel_plan(shard, buf, detail=True)["stream_k"] for buf in op.bufs)
         d_rows = c_full[r0:r1].cpu()
         if sk:
             same = ((h_rows.double() - d_rows.double()).norm() / d_rows.double().norm()).item() <= 1e-5

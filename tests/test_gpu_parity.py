@@ -197,12 +197,12 @@ def test_misaligned_rows_are_packed_for_tensor_cores():
     for v in ("3xtf32", "tf32", "3xtf32_masked", "auto"):
         got = ext._matrix_mul(x1, x2, variant=v).cpu().numpy()
         assert oracle.rel_frob(got, ref) <= TOL[v], v
-    assert ext.plan(torch.empty(1000, 3001, device=DEV), torch.empty(3001, 777, device=DEV))[0] == "3xtf32"
+    assert ext.kernel_plan(torch.empty(1000, 3001, device=DEV), torch.empty(3001, 777, device=DEV))[0] == "3xtf32"
 
 
 def test_plan_and_status():
     x1 = torch.randn(2048, 2048, device=DEV)
-    v, s = ext.plan(x1, x1)
+    v, s = ext.kernel_plan(x1, x1)
     assert v in ("simt", "splitk", "tf32", "3xtf32", "3xtf32_masked") and s >= 1
     assert _status_clean()
 
@@ -257,7 +257,7 @@ def test_matrix_mul_host_equals_device_bitwise(shape, chunks):
     x1 = torch.randn(m, k, generator=g).pin_memory()
     x2 = torch.randn(k, n, generator=g).pin_memory()
     d1, d2 = x1.to(DEV), x2.to(DEV)
-    v, s = ext.plan(d1, d2)
+    v, s = ext.kernel_plan(d1, d2)
     want = ext._matrix_mul(d1, d2, variant=v, split_k=s).cpu()
     assert oracle.rel_frob(want.numpy(), ext.matrix_mul(d1, d2).cpu().numpy()) <= 1e-5
     got = ext.matrix_mul_host(x1, x2, chunks=chunks)
@@ -412,7 +412,7 @@ def test_transposed_views_forced_split_and_pair():
         got = ext._matrix_mul(y.t(), z.t(), variant="3xtf32", split_k=split)
         want = ext._matrix_mul(y.t().contiguous(), z.t().contiguous(), variant="3xtf32", split_k=split)
         assert torch.equal(got, want), split
-    assert ext.plan(y.t(), z.t(), variant="3xtf32")[0] == "3xtf32"
+    assert ext.kernel_plan(y.t(), z.t(), variant="3xtf32")[0] == "3xtf32"
 
 
 def _ref64(x1, x2, bias=None, act=None):
@@ -560,8 +560,8 @@ def test_mixed_equals_3xtf32_when_low_parts_vanish(shape):
     m, k, n = shape
     g = torch.Generator().manual_seed(m + k + n)
     a, b = _tf32_exact(m, k, g), _tf32_exact(k, n, g)
-    assert ext.plan(a, b, variant="3xmixed")[0] == "3xmixed"
-    split = ext.plan(a, b, variant="3xtf32")[1]  # same K slices for both (the plans' speed models differ)
+    assert ext.kernel_plan(a, b, variant="3xmixed")[0] == "3xmixed"
+    split = ext.kernel_plan(a, b, variant="3xtf32")[1]  # same K slices for both (the plans' speed models differ)
     assert torch.equal(ext._matrix_mul(a, b, variant="3xmixed", split_k=split),
                        ext._matrix_mul(a, b, variant="3xtf32", split_k=split))
     assert _status_clean()
@@ -594,11 +594,11 @@ def test_mixed_plan_falls_back_where_no_pair_kernel_runs():
     3XTF32, and the plan says so."""
     a = torch.randn(200, 512, device=DEV)
     b = torch.randn(512, 600, device=DEV)
-    assert ext.plan(a, b, variant="3xmixed")[0] == "3xtf32"
+    assert ext.kernel_plan(a, b, variant="3xmixed")[0] == "3xtf32"
     c = torch.randn(512, 100, device=DEV)
-    assert ext.plan(b.t(), c, variant="3xmixed")[0] == "3xtf32"
+    assert ext.kernel_plan(b.t(), c, variant="3xmixed")[0] == "3xtf32"
     x = torch.randn(2304, 2048, device=DEV)
-    info = ext.plan(x, x.t(), variant="3xmixed", stream_k=True, detail=True)
+    info = ext.kernel_plan(x, x.t(), variant="3xmixed", stream_k=True, detail=True)
     assert info["variant"] == "3xmixed" and not info["stream_k"]
     got = ext._matrix_mul(x, x.t(), variant="3xmixed", stream_k=True)
     assert _rel(got, x.double() @ x.t().double()) <= 1e-5
@@ -632,7 +632,7 @@ def test_stream_k_matches_oracle_and_one_pair_per_tile(shape, variant):
     x1 = torch.randn(m, k, generator=g)
     x2 = torch.randn(k, n, generator=g)
     a, b = x1.to(DEV), x2.to(DEV)
-    info = ext.plan(a, b, variant=variant, stream_k=True, detail=True)
+    info = ext.kernel_plan(a, b, variant=variant, stream_k=True, detail=True)
     assert info["stream_k"] and info["split_k"] == 1, info
     sk = ext._matrix_mul(a, b, variant=variant, stream_k=True)
     dp = ext._matrix_mul(a, b, variant=variant, split_k=1)
@@ -647,17 +647,17 @@ def test_stream_k_is_auto_choice_where_tiles_leave_pairs_idle():
     tiles: two waves on 74 pair slots), not where the last wave is nearly full (2048^3:
     64 tiles in one wave, which stream-K's slower k-blocks would not win back)."""
     x = torch.empty(2304, 2048, device=DEV)
-    assert ext.plan(x, x.t(), detail=True) == {"variant": "3xtf32", "split_k": 1, "stream_k": True}
+    assert ext.kernel_plan(x, x.t(), detail=True) == {"variant": "3xtf32", "split_k": 1, "stream_k": True}
     a = torch.empty(2048, 2048, device=DEV)
-    assert not ext.plan(a, a, detail=True)["stream_k"]
+    assert not ext.kernel_plan(a, a, detail=True)["stream_k"]
     # Whole waves (or K slices asked for) keep one pair per tile.
     big = torch.empty(65536, 8192, device=DEV)
-    assert not ext.plan(big, torch.empty(8192, 8192, device=DEV), detail=True)["stream_k"]
-    assert not ext.plan(a, a, variant="3xtf32", split_k=2, stream_k=True, detail=True)["stream_k"]
-    assert not ext.plan(a, a, variant="3xtf32", split_k=1, detail=True)["stream_k"]
-    assert ext.plan(a, a, variant="3xtf32", split_k=1, stream_k=True, detail=True)["stream_k"]
+    assert not ext.kernel_plan(big, torch.empty(8192, 8192, device=DEV), detail=True)["stream_k"]
+    assert not ext.kernel_plan(a, a, variant="3xtf32", split_k=2, stream_k=True, detail=True)["stream_k"]
+    assert not ext.kernel_plan(a, a, variant="3xtf32", split_k=1, detail=True)["stream_k"]
+    assert ext.kernel_plan(a, a, variant="3xtf32", split_k=1, stream_k=True, detail=True)["stream_k"]
     # Kernels without a CTA pair ignore the flag.
-    assert not ext.plan(a[:, :64], a[:64, :64], stream_k=True, detail=True)["stream_k"]
+    assert not ext.kernel_plan(a[:, :64], a[:64, :64], stream_k=True, detail=True)["stream_k"]
 
 
 @pytest.mark.parametrize("ta,tb", [(False, True), (True, False), (True, True)])

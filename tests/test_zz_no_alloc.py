@@ -4,15 +4,19 @@ It serves callers that may not allocate device memory (an FFI host that binds on
 C ABI and owns no device allocator, or a process that reserves all device memory up
 front).  Its split-K partial sums live in a fixed device array inside the library, so
 the test checks, on two calls in a row, that it returns what the allocating entry point
-(tilec_mm_f32 with a caller-provided workspace, variant SPLITK) returns, within the
-tolerance the other parity tests use, and that oversized explicit requests are refused.
-This file sorts last so that a run stopping at the first failure has run every other test.
+(tilec_mm_f32 with a caller-provided workspace, variant SPLITK) returns and what the CPU
+oracle (the restated reference kernel, oracle.mm_tiled) returns, within the tolerance
+the other parity tests use, and that explicit requests whose slices do not fit are
+refused.  This file sorts last so that a run stopping at the first failure has run every
+other test.
 """
 import ctypes
 
+import numpy as np
 import pytest
 import torch
 
+import oracle
 from tilec_b200 import _native, ext
 
 pytestmark = pytest.mark.gpu
@@ -41,12 +45,14 @@ def test_noalloc_matches_allocating_entry_point(shape):
     x1 = torch.randn(m, k, device="cuda", generator=g)
     x2 = torch.randn(k, n, device="cuda", generator=g)
     ref = ext._matrix_mul(x1, x2, variant="splitk")
+    want = torch.from_numpy(oracle.mm_tiled(x1.cpu().numpy(), x2.cpu().numpy()))
     for _ in range(2):  # two calls in a row: the shared scratch keeps the previous call's sums
         out = torch.full((m, n), float("nan"), device="cuda")
         assert _noalloc(x1, x2, out) == 0
         torch.cuda.synchronize()
         assert torch.isfinite(out).all()
         assert _rel(out, ref) <= TOL
+        assert _rel(out.cpu(), want) <= TOL
 
 
 def test_noalloc_explicit_split_and_limit():
@@ -55,10 +61,12 @@ def test_noalloc_explicit_split_and_limit():
     x1 = torch.randn(m, k, device="cuda", generator=g)
     x2 = torch.randn(k, n, device="cuda", generator=g)
     ref = ext._matrix_mul(x1, x2, variant="splitk", split_k=8)
+    want = torch.from_numpy(oracle.mm_tiled(x1.cpu().numpy(), x2.cpu().numpy()))
     out = torch.empty(m, n, device="cuda")
     assert _noalloc(x1, x2, out, split_k=8) == 0
     torch.cuda.synchronize()
     assert _rel(out, ref) <= TOL
+    assert _rel(out.cpu(), want) <= TOL
     # 64 slices of a 4096 x 1024 output need 1 GiB of partial sums: refused, nothing launched.
     big1 = torch.randn(4096, 256, device="cuda", generator=g)
     big2 = torch.randn(256, 1024, device="cuda", generator=g)
@@ -71,3 +79,30 @@ def test_noalloc_explicit_split_and_limit():
     assert _rel(big_out, big1.double() @ big2.double()) <= TOL
     st = ctypes.c_int32(-1)
     assert _native.load().tilec_mm_device_status(None, ctypes.byref(st)) == 0 and st.value == 0
+
+
+def _case(m, k, n, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x1 = torch.randn(m, k, device="cuda", generator=g)
+    x2 = torch.randn(k, n, device="cuda", generator=g)
+    return x1, x2, torch.from_numpy(oracle.mm_tiled(x1.cpu().numpy(), x2.cpu().numpy()))
+
+
+def test_noalloc_split_above_cap_and_rounded_split():
+    # split_k = 100 runs as 64 slices (the cap); 64 x 64 x 64 x 4 bytes fit in the scratch.
+    x1, x2, want = _case(64, 4096, 64, 11)
+    out = torch.empty(64, 64, device="cuda")
+    assert _noalloc(x1, x2, out, split_k=100) == 0
+    torch.cuda.synchronize()
+    assert _rel(out.cpu(), want) <= TOL
+    # K = 33 with split_k = 8 runs as 3 slices of 16-deep K blocks: 3 slabs of 1024 x 1024
+    # fit (12 MiB of 16), although 8 would not.
+    x1, x2, want = _case(1024, 33, 1024, 12)
+    assert 8 * 1024 * 1024 * 4 > SCRATCH_BYTES >= 3 * 1024 * 1024 * 4
+    out = torch.empty(1024, 1024, device="cuda")
+    for _ in range(2):
+        out.fill_(float("nan"))
+        assert _noalloc(x1, x2, out, split_k=8) == 0
+        torch.cuda.synchronize()
+        assert np.isfinite(out.cpu().numpy()).all()
+        assert _rel(out.cpu(), want) <= TOL

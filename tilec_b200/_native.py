@@ -11,6 +11,7 @@ import threading
 from . import build as _build
 
 TILEC_OK = 0
+TILEC_ERR_DEVICE = 5
 STATUS_NAMES = {
     0: "TILEC_OK", 1: "TILEC_ERR_BAD_ARG", 2: "TILEC_ERR_MISALIGNED", 3: "TILEC_ERR_NO_DEVICE",
     4: "TILEC_ERR_LAUNCH", 5: "TILEC_ERR_DEVICE", 6: "TILEC_ERR_WORKSPACE", 7: "TILEC_ERR_UNSUPPORTED",
@@ -25,7 +26,20 @@ EXPORTS = [
     "tilec_mm_f32", "tilec_mm_workspace_bytes", "tilec_mm_plan", "tilec_mm_set_table",
     "tilec_mm_device_status", "tilec_strerror", "tilec_mm_abi_version", "tilec_mm_built_arch",
     "tilec_mm_f32_splitk_noalloc", "tilec_mm_selftest_wait", "tilec_mm_f32_ex", "tilec_mm_workspace_bytes_ex",
+    "tilec_mm_set_wait_limit",
 ]
+
+# Bits of the device status word (TILEC_DEV_STATUS_* in include/tilec_mm.h).
+DEV_STATUS_BITS = {1: "TIMEOUT", 2: "TMEM", 4: "BAD_LAUNCH"}
+
+
+def status_bits(word):
+    """Names of the bits set in a device status word, e.g. 'TIMEOUT|TMEM'."""
+    names = [n for b, n in DEV_STATUS_BITS.items() if word & b]
+    rest = word & ~sum(DEV_STATUS_BITS)
+    if rest:
+        names.append(hex(rest))
+    return "|".join(names) or "clean"
 
 
 class MMConfig(ctypes.Structure):
@@ -44,7 +58,11 @@ class TilecError(RuntimeError):
 
     def __init__(self, code, where):
         self.code = code
-        super().__init__(f"{where}: {STATUS_NAMES.get(code, code)}: {strerror(code)}")
+        try:
+            text = strerror(code)
+        except Exception:  # noqa: BLE001  (the library itself may be what failed to load)
+            text = "?"
+        super().__init__(f"{where}: {STATUS_NAMES.get(code, code)}: {text}")
 
 
 _lib = None
@@ -91,6 +109,8 @@ def load():
         lib.tilec_mm_f32_splitk_noalloc.restype = ctypes.c_int
         lib.tilec_mm_selftest_wait.argtypes = [i64, vp]
         lib.tilec_mm_selftest_wait.restype = ctypes.c_int
+        lib.tilec_mm_set_wait_limit.argtypes = [i64, vp]
+        lib.tilec_mm_set_wait_limit.restype = ctypes.c_int
         lib.tilec_mm_f32_ex.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64, cfgp, vp,
                                         sz, vp]
         lib.tilec_mm_f32_ex.restype = ctypes.c_int

@@ -23,6 +23,16 @@ __device__ int g_status = 0;
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
+// Limit of every bounded wait of the GEMM kernels on this device, in ns; 0 means
+// kWaitLimitNs.  Set only by tilec_mm_set_wait_limit (failure-detection tests shorten it so
+// that a real GEMM launch gives up, then restore it).
+__device__ unsigned long long g_wait_limit_ns = 0;
+
+__device__ __forceinline__ unsigned long long wait_limit() {
+  const unsigned long long v = *const_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+  return v ? v : kWaitLimitNs;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -87,14 +97,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity.  `abort_flag` (shared) lets
-// one role that gave up release every other role quickly.
+// one role that gave up release every other role quickly.  limit_ns == 0: the device's
+// limit (wait_limit()); the clock is read every 64 polls at the default limit and on
+// every poll below it.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned long long limit_ns = kWaitLimitNs) {
+                                          unsigned long long limit_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
+  if (limit_ns == 0) limit_ns = wait_limit();
+  const uint32_t mask = limit_ns < kWaitLimitNs ? 0u : 63u;
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0) {
+    if ((it & mask) == 0) {
       if (*abort_flag) return false;
       if (global_ns() - t0 > limit_ns) {
         *abort_flag = 1;
@@ -125,14 +139,15 @@ __device__ __forceinline__ int flag_acquire(const int* f) {
   return v;
 }
 // Bounded wait for a nonzero flag, with the same limit, abort flag and status bit as mbar_wait.
-__device__ __forceinline__ bool flag_wait(const int* f, volatile int* abort_flag,
-                                          unsigned long long limit_ns = kWaitLimitNs) {
+__device__ __forceinline__ bool flag_wait(const int* f, volatile int* abort_flag, unsigned long long limit_ns = 0) {
   if (flag_acquire(f)) return true;
   const unsigned long long t0 = global_ns();
+  if (limit_ns == 0) limit_ns = wait_limit();
+  const uint32_t mask = limit_ns < kWaitLimitNs ? 0u : 15u;
   for (uint32_t it = 1;; ++it) {
     __nanosleep(64);
     if (flag_acquire(f)) return true;
-    if ((it & 15u) == 0) {
+    if ((it & mask) == 0) {
       if (*abort_flag) return false;
       if (global_ns() - t0 > limit_ns) {
         *abort_flag = 1;
@@ -183,6 +198,22 @@ __device__ __forceinline__ float epilogue(float v, float bias, int act) {
   if (act == kActRelu) return fmaxf(v, 0.f);
   if (act == kActGelu) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
   return v;
+}
+
+// ---------------------------------------------------------------- abort: poisoned output
+// A kernel that gave up (a bounded wait expired, TILEC_DEV_TIMEOUT recorded) writes NaN
+// over the part of its output it owns -- C, a split-K slab or a stream-K partial -- once
+// every copy and MMA it issued has landed, so that an unfinished result is never left
+// looking like a finished one (NaN also propagates through a split-K reduction).  One
+// warp writes rows [row0, row0 + rows) x columns [col0, col0 + cols) of `out`, masked at
+// M and N: lane j takes columns col0 + j, col0 + j + 32, ...
+__device__ __forceinline__ void poison_rows(float* out, int64_t ldo, int64_t row0, int64_t rows, int64_t col0,
+                                            int64_t cols, int64_t M, int64_t N, int lane) {
+  const float nan = __int_as_float(0x7fc00000);
+  const int64_t r_end = row0 + rows < M ? row0 + rows : M;
+  const int64_t c_end = col0 + cols < N ? col0 + cols : N;
+  for (int64_t r = row0; r < r_end; ++r)
+    for (int64_t c = col0 + lane; c < c_end; c += 32) out[r * ldo + c] = nan;
 }
 
 // ---------------------------------------------------------------- cp.async (SIMT path)
@@ -279,15 +310,18 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
       : "memory");
   return ok != 0;
 }
-// Bounded wait with acquire at cluster scope (for barriers the peer CTA arrives on).
+// Bounded wait with acquire at cluster scope (for barriers the peer CTA arrives on); the
+// device's wait limit, as mbar_wait.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
+  const unsigned long long limit_ns = wait_limit();
+  const uint32_t mask = limit_ns < kWaitLimitNs ? 0u : 63u;
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((it & 63u) == 0) {
+    if ((it & mask) == 0) {
       if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         record_status(TILEC_DEV_TIMEOUT);
         return false;

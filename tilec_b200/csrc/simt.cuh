@@ -260,10 +260,12 @@ __global__ void __launch_bounds__(kSimtThreads, 2)
   if constexpr (BMODE == kBTma) {
     if (!ok) {
       // Let the TMA copies still in flight (tiles kt .. kt + 2) land before the CTA's
-      // shared memory goes away; store nothing (the status word records the timeout).
+      // shared memory goes away, and overwrite the CTA's tile with NaN (the status word
+      // records the timeout): each warp 16 of its 128 rows.
       if (tid == 0)
         for (int64_t it = kt; it < nkt && it < kt + kSimtStages - 1; ++it)
           mbar_drain(&full[it % kSimtStages], static_cast<uint32_t>((it / kSimtStages) & 1));
+      poison_rows(out, ldo, m0 + 16 * (tid >> 5), 16, n0, BN, M, N, tid & 31);
       return;
     }
   }

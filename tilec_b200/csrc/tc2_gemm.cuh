@@ -258,8 +258,10 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, false, kTc2Bk<SPLIT
         // Producer tail: wait for the release (leader's commit) of each of the last fills,
         // so no arrival targets this CTA's barriers after it exits.
         for (int kb = nkb - STAGES < 0 ? 0 : nkb - STAGES; kb < nkb; ++kb)
-          if (!mbar_wait_cluster(&empty[kb % STAGES], (kb / STAGES) & 1, abort_flag)) break;
-      } else {
+          if (!mbar_wait_cluster(&empty[kb % STAGES], (kb / STAGES) & 1, abort_flag)) { ok = false; break; }
+      }
+      if (!ok) {
+        // Gave up: let the last fills' copies land (a landed fill passes at once).
         for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb)
           mbar_drain(&full[kb % STAGES], (kb / STAGES) & 1);
       }
@@ -330,10 +332,11 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, false, kTc2Bk<SPLIT
           umma_commit_pair_both(c_local);
         }
       }
-      if (!ok) {
-        umma_commit_pair(smem_u32(drain_bar));
-        mbar_drain(drain_bar, 0);
-      }
+      // Every MMA issued here completes before this thread leaves its role, on every path
+      // (an epilogue that gave up must not let the pair free TMEM or exit under a running
+      // MMA, which also reads the peer CTA's shared memory).
+      umma_commit_pair(smem_u32(drain_bar));
+      mbar_drain(drain_bar, 0);
     }
   } else {
     // ------------------------------------------------------------ split + promotion epilogue (both CTAs)
@@ -464,6 +467,13 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, false, kTc2Bk<SPLIT
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem, Cfg::kTmemCols);
+  }
+  // This CTA gave up: both CTAs' copies and MMAs have landed (cluster barrier above), so
+  // its epilogue warps overwrite its 128 rows of the tile with NaN.
+  if (*abort_flag && warp >= 2) {
+    const int e = warp - 2;
+    poison_rows(out, ldo, m0 + 32 * (warp & 3), 32, n0 + (e >> 2) * Cfg::kColsPerThread, Cfg::kColsPerThread, M,
+                N, lane);
   }
 }
 

@@ -193,6 +193,7 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, true, 32>::kThreads
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_wait();
+  bool published = false;  // epilogue warps: this warp's partial (if it has one) is out
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -232,8 +233,10 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, true, 32>::kThreads
         // Producer tail: wait for the release (leader's commit) of each of the last fills,
         // so no arrival targets this CTA's barriers after it exits.
         for (int f = g - STAGES < 0 ? 0 : g - STAGES; f < g; ++f)
-          if (!mbar_wait_cluster(&empty[f % STAGES], (f / STAGES) & 1, abort_flag)) break;
-      } else {
+          if (!mbar_wait_cluster(&empty[f % STAGES], (f / STAGES) & 1, abort_flag)) { ok = false; break; }
+      }
+      if (!ok) {
+        // Gave up: let the last fills' copies land (a landed fill passes at once).
         for (int f = g - STAGES < 0 ? 0 : g - STAGES; f < g; ++f) mbar_drain(&full[f % STAGES], (f / STAGES) & 1);
       }
     }
@@ -291,10 +294,11 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, true, 32>::kThreads
         }
         gc += chunks_of(n);
       }
-      if (!ok) {
-        umma_commit_pair(smem_u32(drain_bar));
-        mbar_drain(drain_bar, 0);
-      }
+      // Every MMA issued here completes before this thread leaves its role, on every path
+      // (an epilogue that gave up must not let the pair free TMEM or exit under a running
+      // MMA, which also reads the peer CTA's shared memory).
+      umma_commit_pair(smem_u32(drain_bar));
+      mbar_drain(drain_bar, 0);
     }
   } else {
     // ------------------------------------------------------------ split + promotion epilogue (both CTAs)
@@ -390,6 +394,7 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, true, 32>::kThreads
         __threadfence();
         __syncwarp();
         if (lane == 0) flag_release(sk.flags + pair * 2 * Cfg::kEpiWarps + flag_slot, 1);
+        published = true;
         continue;
       }
       if (sg.kb_lo > 0) {
@@ -433,6 +438,30 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, true, 32>::kThreads
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem, Cfg::kTmemCols);
+  }
+  // This CTA gave up (copies and MMAs of both CTAs have landed): each epilogue warp
+  // overwrites its block of every tile the pair owns with NaN, and publishes a NaN partial
+  // in place of one it did not publish, so the owner of that tile finishes with NaN
+  // instead of waiting out its own limit.
+  if (*abort_flag && warp >= 2) {
+    const int e = warp - 2, q = warp & 3, h = e >> 2;
+    const int flag_slot = static_cast<int>(rank) * Cfg::kEpiWarps + e;
+    for (int si = 0; si < n_seg; ++si) {
+      const PairSeg sg = segment(si);
+      if (!sg.owner) {
+        if (published) continue;
+        float* slot = sk.partial + static_cast<int64_t>(pair) * Cfg::kPartialFloats +
+                      (static_cast<int64_t>(rank) * Cfg::kEpiWarps + e) * (COLS * 32);
+        poison_rows(slot, COLS * 32, 0, 1, 0, COLS * 32, 1, COLS * 32, lane);
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) flag_release(sk.flags + pair * 2 * Cfg::kEpiWarps + flag_slot, 1);
+        continue;
+      }
+      const TileAt ta = tile_at(sg.tile);
+      poison_rows(out + static_cast<int64_t>(ta.batch) * out_batch, ldo, ta.m0 + 32 * q, 32, ta.n0 + h * COLS, COLS,
+                  M, N, lane);
+    }
   }
 }
 

@@ -258,9 +258,11 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
       if (ok) {
         // Tail: the MMA's release of the last fills has arrived before the CTA exits.
         for (int kb = nkb - STAGES < 0 ? 0 : nkb - STAGES; kb < nkb; ++kb)
-          if (!mbar_wait(&empty[kb % STAGES], (kb / STAGES) & 1, abort_flag)) break;
-      } else {
-        // Let copies already in flight land before the CTA's shared memory goes away.
+          if (!mbar_wait(&empty[kb % STAGES], (kb / STAGES) & 1, abort_flag)) { ok = false; break; }
+      }
+      if (!ok) {
+        // Gave up (here or elsewhere): let the last fills' copies land before the CTA's
+        // shared memory goes away (a fill that already landed passes at once).
         for (int kb = issued - STAGES < 0 ? 0 : issued - STAGES; kb < issued; ++kb)
           mbar_drain(&full[kb % STAGES], (kb / STAGES) & 1);
       }
@@ -313,9 +315,10 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
         umma_commit(&empty[s]);
         if (SPLIT3 && (kb % KC == KC - 1 || kb == nkb - 1)) umma_commit(&chunk_full[chunk & 1]);
       }
-      if (ok) {
-        if (!SPLIT3 && nkb > 0) umma_commit(acc_bar);
-      } else {
+      if (ok && !SPLIT3 && nkb > 0) umma_commit(acc_bar);
+      // Every MMA issued here completes before this thread leaves its role, on every path:
+      // an epilogue that gave up must not let the CTA free TMEM or exit under a running MMA.
+      if (nkb > 0) {
         umma_commit(drain_bar);
         mbar_drain(drain_bar, 0);
       }
@@ -429,6 +432,13 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
+  // A role gave up: every copy and MMA of this CTA has landed (drained above), so the
+  // epilogue warps overwrite the CTA's tile with NaN, each the 32 rows x cols it stores.
+  if (*abort_flag && warp >= 2) {
+    constexpr int kWarpCols = BN / (Cfg::kEpiWarps / 4);
+    const int e = warp - 2;
+    poison_rows(out, ldo, m0 + 32 * (warp & 3), 32, n0 + (e >> 2) * kWarpCols, kWarpCols, M, N, lane);
   }
 }
 

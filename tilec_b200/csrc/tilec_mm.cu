@@ -1210,6 +1210,22 @@ int tilec_mm_selftest_wait(int64_t limit_ns, void* stream) {
   return launch_k(selftest_wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), 1, lim);
 }
 
+int tilec_mm_set_wait_limit(int64_t limit_ns, void* stream) {
+  if (limit_ns < 0) return TILEC_ERR_BAD_ARG;
+  DeviceInfo* d = nullptr;
+  const int rc = current_device(&d);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned long long v =
+      static_cast<unsigned long long>(limit_ns) > kWaitLimitNs ? kWaitLimitNs : static_cast<unsigned long long>(limit_ns);
+  if (cudaMemcpyToSymbolAsync(g_wait_limit_ns, &v, sizeof(v), 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess) {
+    cudaGetLastError();
+    return TILEC_ERR_DEVICE;
+  }
+  return TILEC_OK;
+}
+
 int tilec_mm_device_status(void* stream, int32_t* status_out) {
   if (!status_out) return TILEC_ERR_BAD_ARG;
   DeviceInfo* d = nullptr;
@@ -1304,15 +1320,17 @@ extern "C" int tilec_mm_f32_splitk_noalloc(const float* A, const float* B, float
   int64_t split;
   if (split_k > 0) {
     split = split_k > kMaxSplit ? kMaxSplit : split_k;
-    if (split > 1 && split > fit) return TILEC_ERR_TOO_LARGE;
   } else {
     const double cta_s = cta_seconds(kSimtBM, bn, bn, K, kRateSimt, kBwPerSm);
     split = choose_split(mt * nt, d->sms, cta_s, double(slab) * 4.0, K / (int64_t(kSimtBK) * 4), 0,
                          /*one_wave=*/false);
     if (split > fit) split = fit < 1 ? 1 : fit;
   }
+  // The slices that run: whole 16-deep K blocks per slice, so rounding can only lower the
+  // count.  Only those must fit in the scratch (the library's own choice always does).
   const int64_t k_chunk = round_up(cdiv(K, split), kSimtBK);
   split = cdiv(K, k_chunk);
+  if (split > 1 && split > fit) return TILEC_ERR_TOO_LARGE;
 
   Launch L;
   L.out = split > 1 ? scratch : C;

@@ -30,10 +30,16 @@ SIMT_TILE = (128, 128, 16)     # BM, BN, BK of the SIMT kernel
 TENSOR_TILE = (128, 256, 16)   # BM, BN, BK of the tcgen05 3xTF32 kernel
 
 _ENV_VARIANT = "TILEC_MM_VARIANT"
+_ENV_CHECK = "TILEC_MM_CHECK"
 
 
 def _default_variant():
     return os.environ.get(_ENV_VARIANT, "auto")
+
+
+def _check_enabled():
+    """TILEC_MM_CHECK=1: every call synchronises its stream and raises on a device fault."""
+    return os.environ.get(_ENV_CHECK, "0") not in ("", "0")
 
 
 def _check_operand(x):
@@ -111,10 +117,12 @@ def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k, flags=0):
             _WS_BYTES[key] = ws_bytes
         ws_ptr = _workspace(dev, stream, ws_bytes).data_ptr() if ws_bytes else None
         rc = lib.tilec_mm_f32(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg), ws_ptr, ws_bytes, stream)
+        _native.check(rc, "tilec_mm_f32")
+        if _check_enabled():
+            check_device(stream)
     finally:
         if switch:
             torch.cuda.set_device(prev)
-    _native.check(rc, "tilec_mm_f32")
     return out
 
 
@@ -154,8 +162,80 @@ def _matrix_mul(x1, x2, variant=None, split_k=0, out=None, stream_k=False):
 
 
 def matrix_mul(x1, x2):
-    """C = x1 @ x2 for float32 CUDA tensors x1 [M, K], x2 [K, N] (tilec/ext.py:66-67)."""
+    """C = x1 @ x2 for float32 CUDA tensors x1 [M, K], x2 [K, N] (tilec/ext.py:66-67).
+
+    Kernels never trap: a device-side wait that gives up (see tilec_mm.h) leaves NaN in
+    the output tiles it did not finish and sets the device status word.  Set
+    TILEC_MM_CHECK=1 (or call check_device()) to have it raised as a TilecError."""
     return _matrix_mul(x1, x2)
+
+
+def _matrix_mul_tiled(x1, x2, BM=64, BN=64, BK=16):
+    """The reference's tiled entry point (tilec/ext.py:54-63) with its signature.  BM, BN
+    and BK name the reference kernel's tile (64 x 64 x 16); the B200 kernels choose their
+    own tiles per shape, so the values are checked and otherwise unused."""
+    for name, v in (("BM", BM), ("BN", BN), ("BK", BK)):
+        if not isinstance(v, int) or v <= 0:
+            raise ValueError(f"_matrix_mul_tiled: {name} must be a positive int, got {v!r}")
+    return _matrix_mul(x1, x2)
+
+
+# ---------------------------------------------------------------- reference host helpers
+# The reference's module-level sizing helpers keep their names, signatures and results
+# (tilec/ext.py:10, 29-51), so code written against tilec.ext keeps working.  They describe
+# the reference's own Metal kernel configurations (row split, row join, block size); the
+# B200 kernels' launch configurations are kernel_plan() and kernel_configs() below.
+MAX_BLOCK = 4096
+SPLITS = (1, 2, 4, 8, 16, 32, 64)
+JOINS = (1, 2, 4, 8)
+BLOCKS = (256, 1024, 4096)
+
+
+def plan(N, block=None):
+    """(block, chunks) for a row of N elements (tilec/ext.py:29-34): unless given, block is
+    the smallest power of 4 that reaches min(N, MAX_BLOCK), and chunks = cdiv(N, block)."""
+    if block is None:
+        block = 1
+        while block < min(N, MAX_BLOCK):
+            block *= 4
+    return block, cdiv(N, block)
+
+
+def _candidate_blocks(n):
+    """Block sizes tried for rows of n elements (tilec/ext.py:43-45): the listed sizes below
+    plan(n)'s block that leave at most 16 chunks, then plan(n)'s block itself."""
+    top = plan(n)[0]
+    return [b for b in BLOCKS if b < top and cdiv(n, b) <= 16] + [top]
+
+
+def mm_configs(M1, N, M2):
+    """(split, join, block) triples of the reference's tuner (tilec/ext.py:48-51): a split
+    p > 1 needs N // p >= 32, a join r > 1 needs M1 >= r, and blocks come from
+    _candidate_blocks(cdiv(N, p)).  M2 does not restrict the space (as in the reference)."""
+    out = []
+    for p in SPLITS:
+        if p > 1 and N // p < 32:
+            continue
+        for r in JOINS:
+            if r > 1 and M1 < r:
+                continue
+            out.extend((p, r, b) for b in _candidate_blocks(cdiv(N, p)))
+    return out
+
+
+def check_device(stream=None):
+    """Read and clear the device status word of the current device (synchronising the
+    current stream, or `stream`); raise TilecError(TILEC_ERR_DEVICE) if a kernel recorded a
+    fault there (a bounded wait that gave up, a bad launch shape, an unexpected TMEM
+    address).  Returns the (zero) status word otherwise."""
+    lib = _native.load()
+    s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+    st = ctypes.c_int32(0)
+    _native.check(lib.tilec_mm_device_status(s, ctypes.byref(st)), "tilec_mm_device_status")
+    if st.value:
+        raise _native.TilecError(_native.TILEC_ERR_DEVICE, f"device status word {st.value:#x} "
+                                 f"({_native.status_bits(st.value)})")
+    return 0
 
 
 def _batched_operand(x):
@@ -235,11 +315,13 @@ def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, sp
         ws_ptr = _workspace(dev, stream, ws_bytes).data_ptr() if ws_bytes else None
         rc = lib.tilec_mm_f32_ex(pa, pb, pc, bias.data_ptr() if bias is not None else None, M, N, K, lda, ldb, ldc,
                                  nbatch, sa, sb, sc, ctypes.byref(cfg), ws_ptr, ws_bytes, stream)
-    _native.check(rc, "tilec_mm_f32_ex")
+        _native.check(rc, "tilec_mm_f32_ex")
+        if _check_enabled():
+            check_device(stream)
     return out
 
 
-def plan(x1, x2, variant=None, split_k=0, stream_k=False, detail=False):
+def kernel_plan(x1, x2, variant=None, split_k=0, stream_k=False, detail=False):
     """The (variant name, split_k) that matrix_mul would launch for these operands; with
     detail=True a dict that also says whether the pair kernel runs in its stream-K form."""
     M, K = x1.shape
@@ -262,7 +344,7 @@ def plan(x1, x2, variant=None, split_k=0, stream_k=False, detail=False):
     return name, res.split_k
 
 
-def mm_configs(M, K, N):
+def kernel_configs(M, K, N):
     """Candidate (variant, split_k) launch configs for an [M,K]x[K,N] product.
 
     B200 counterpart of the reference's config space (tilec/ext.py:48-51), which the
@@ -400,5 +482,5 @@ def chunk_compute(d_x1, d_x2, variant=None, split_k=0):
     """compute(rows_of_x1, rows_of_out) for one row chunk of the product d_x1 @ d_x2 with
     the kernel and K split that the unchunked product uses (planned once on the full-size
     buffers), so a chunked product equals the unchunked one bit for bit."""
-    v, s = plan(d_x1, d_x2, variant=variant, split_k=split_k)
+    v, s = kernel_plan(d_x1, d_x2, variant=variant, split_k=split_k)
     return lambda a, c: _matrix_mul(a, d_x2, variant=v, split_k=s, out=c)

@@ -5,7 +5,7 @@
     python -m tilec_b200.tune run    --shape M,K,N [--variant V] [--split S] [--reps R]
 
 ``bench`` mirrors tilec/tune.py:68-87: seeded shapes, every candidate config of
-``ext.mm_configs`` timed, resumable (shapes already in the CSV are skipped).  Timing is
+``ext.kernel_configs`` timed, resumable (shapes already in the CSV are skipped).  Timing is
 CUDA events around back-to-back launches after warm-up (tilec/tune.py:35-51 used
 perf_counter + synchronize and a median of 5), with the same early abort for configs far
 slower than the best so far.  The shape sampler follows tilec/tune.py:54-65 but spans
@@ -103,7 +103,7 @@ def bench(n=64, path=DEFAULT_CSV, seed=4):
             select.install([])
             auto = lambda: ext._matrix_mul(a, b, variant="auto", out=c)  # noqa: E731
             ms_auto = time_ms(auto)
-            cands = [("simt", 0), ("splitk", 0), ("3xtf32", 0), ("tf32", 0)] + ext.mm_configs(m, k, nn)
+            cands = [("simt", 0), ("splitk", 0), ("3xtf32", 0), ("tf32", 0)] + ext.kernel_configs(m, k, nn)
             out_rows = []
             for v, s in cands:
                 # Family rows (the library's own split) feed the fit, so they are always
@@ -283,7 +283,7 @@ def pick(M, K, N):
     from . import ext
     a = torch.empty(M, K, device="cuda")
     b = torch.empty(K, N, device="cuda")
-    return ext.plan(a, b)
+    return ext.kernel_plan(a, b)
 
 
 def run(shape, variant="auto", split=0, reps=3, seed=0, stream_k=False):
@@ -298,7 +298,7 @@ def run(shape, variant="auto", split=0, reps=3, seed=0, stream_k=False):
     for _ in range(reps):
         ext._matrix_mul(a, b, variant=variant, split_k=split, out=c, stream_k=stream_k)
     torch.cuda.synchronize()
-    plan = ext.plan(a, b, variant=variant, split_k=split, stream_k=stream_k, detail=True)
+    plan = ext.kernel_plan(a, b, variant=variant, split_k=split, stream_k=stream_k, detail=True)
     print(json.dumps({"shape": [m, k, n], "plan": plan, "reps": reps}))
 
 
