@@ -24,7 +24,12 @@ pytestmark = pytest.mark.gpu
 
 TOL = {"simt": 1e-5, "splitk": 1e-5, "3xtf32": 1e-5, "3xmixed": 1e-5, "tf32": 5e-3}
 
-# (variant, (M, K, N), split_k, stream_k): the kernel each case reaches.
+# (variant, (M, K, N), split_k, stream_k): the kernel each case reaches.  The tensor-core
+# kernels always meet a wait that does not pass at once (the MMA waits for the first
+# copies), so they must give up.  The SIMT kernel's only wait is for a B tile whose TMA copy
+# was issued three stages earlier and has landed by then, so it may finish: its cases accept
+# either outcome, a correct product or the visible give-up.
+MAY_FINISH = {"simt", "splitk"}
 CASES = [
     ("3xtf32", (512, 4096, 64), 0, False),      # 1-CTA 3xTF32, split-K slabs + reduction
     ("tf32", (512, 4096, 128), 4, False),       # 1-CTA TF32, split-K
@@ -71,12 +76,17 @@ def test_gave_up_is_nan_and_raises_then_context_works(variant, shape, split_k, s
         assert ext.kernel_plan(x1, x2, variant=variant, stream_k=True, detail=True)["stream_k"]
     out = torch.full((m, n), 12345.0, device="cuda")  # a value no path may leave behind
     monkeypatch.setenv("TILEC_MM_CHECK", "1")
+    raised = False
     with _wait_limit(1):
-        with pytest.raises(TilecError, match="TIMEOUT"):
+        try:
             ext._matrix_mul(x1, x2, variant=variant, split_k=split_k, out=out, stream_k=stream_k)
-    assert _status() == 0  # the raising check read and cleared the word
+        except TilecError as e:
+            assert "TIMEOUT" in str(e)
+            raised = True
+    assert raised or variant in MAY_FINISH, "a tensor-core kernel did not give up at a 1 ns limit"
+    assert _status() == 0  # the raising check read and cleared the word (or nothing was set)
     bad = torch.isnan(out)
-    assert bad.any(), "a kernel that gave up left no NaN"
+    assert bad.any() == raised, "NaN without a recorded give-up, or a give-up that left no NaN"
     done = ~bad
     if done.any():
         err = ((out.double() - ref)[done].norm() / ref[done].norm()).item()

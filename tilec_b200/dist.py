@@ -8,7 +8,8 @@ replicating x2 from one rank:
 * x2 ([K, N], on rank ``src``) is cut into ``panels`` column panels; rank ``src`` packs
   panel p into a contiguous [K, w_p] buffer and NCCL broadcasts it into every rank's
   own buffer (kernels only ever read local memory);
-* every broadcast is enqueued up front on the NCCL stream; the GEMM of panel p waits
+* rank ``src`` packs and broadcasts panel by panel, so the broadcast of panel p waits
+  only for its own pack and the pack of panel p+1 overlaps it; the GEMM of panel p waits
   for broadcast p only (``Work.wait()`` orders the compute stream behind the NCCL
   stream; no host blocking and no device spin-wait), so broadcast p+1 overlaps GEMM p;
 * panel p's GEMM writes C[:, n0:n1] in place (ldc = N): no reduction, no extra traffic;
@@ -17,8 +18,48 @@ replicating x2 from one rank:
 Process groups use the backend of the caller (NCCL on GPUs; the partition, broadcast
 and gather logic is also exercised with gloo on CPU ranks in the tests).
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
+
+_CUDART = None
+
+
+def _cudart():
+    """The CUDA runtime torch loaded (same soname, so the same runtime state and streams)."""
+    global _CUDART
+    if _CUDART is None:
+        torch.cuda.init()
+        lib = ctypes.CDLL("libcudart.so.12")
+        lib.cudaMemcpy2DAsync.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t,
+                                          ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+        lib.cudaMemcpy2DAsync.restype = ctypes.c_int
+        _CUDART = lib
+    return _CUDART
+
+
+def copy_columns_h2d(dst, h_src, n0, n1, stream=None):
+    """dst (a contiguous [K, n1 - n0] device tensor) <- h_src[:, n0:n1] (a host [K, N] tensor
+    with unit column stride), as one 2-D copy on `stream` (default: the current stream):
+    K rows of (n1 - n0) * 4 bytes, source pitch h_src.stride(0) * 4.  Asynchronous when
+    h_src is pinned; a column panel of a row-major x2 then needs no host-side packing."""
+    K = h_src.shape[0]
+    w = n1 - n0
+    if tuple(dst.shape) != (K, w) or not dst.is_contiguous() or dst.dtype != h_src.dtype:
+        raise ValueError(f"copy_columns_h2d: dst must be a contiguous [{K}, {w}] tensor of {h_src.dtype}")
+    if K == 0 or w == 0:
+        return dst
+    if h_src.stride(1) != 1 and w > 1:
+        dst.copy_(h_src[:, n0:n1], non_blocking=False)
+        return dst
+    s = stream if stream is not None else torch.cuda.current_stream(dst.device)
+    es = h_src.element_size()
+    rc = _cudart().cudaMemcpy2DAsync(dst.data_ptr(), w * es, h_src.data_ptr() + n0 * es, h_src.stride(0) * es,
+                                     w * es, K, 1, s.cuda_stream)  # 1 = cudaMemcpyHostToDevice
+    if rc != 0:
+        raise RuntimeError(f"copy_columns_h2d: cudaMemcpy2DAsync failed with error {rc}")
+    return dst
 
 
 def shard_rows(M, world, rank):
@@ -107,8 +148,13 @@ class RowShardedMatmul:
         if self.rank == self.src:
             if x2 is None or tuple(x2.shape) != (self.K, self.N):
                 raise ValueError(f"rank {self.rank} is the source: x2 must be [{self.K}, {self.N}]")
-            pack_panels(x2, self.bounds, self.bufs)
-        works = broadcast_panels(self.bufs, self.src, self.group)
+        works = []
+        for (n0, n1), buf in zip(self.bounds, self.bufs):
+            # Pack panel p, then enqueue its broadcast (which waits for this pack only); the
+            # next pack runs on the compute stream while the broadcast runs on NCCL's.
+            if self.rank == self.src:
+                buf.copy_(x2[:, n0:n1])
+            works.append(dist.broadcast(buf, src=self.src, group=self.group, async_op=True))
         for p, ((n0, n1), buf, w) in enumerate(zip(self.bounds, self.bufs, works)):
             w.wait()
 
@@ -123,39 +169,59 @@ class RowShardedMatmul:
 
     def run_host(self, h_x1_shard, h_x2=None, h_out=None, chunks=16, sync=True):
         """Host-buffer variant: x2 (rank src) and this rank's rows of x1 come from host memory
-        and this rank's rows of C go back to it.  x2 is copied to the device and broadcast in
-        panels first; then row chunks of x1 stream through H2D -> GEMM (all panels) -> D2H
-        with the three overlapping (tilec_b200.ext.pipelined_rows)."""
+        and this rank's rows of C go back to it.  Row chunks of x1 stream through H2D -> GEMM
+        (all panels) -> D2H with the three overlapping (tilec_b200.ext.pipelined_rows).  With
+        several ranks, rank src copies x2's column panels straight from host memory into the
+        panel buffers (one 2-D copy each, no packing) on the H2D stream, panel p just before
+        x1's chunk p, and broadcasts each as soon as its copy is enqueued; a chunk's GEMM of
+        panel p waits for broadcast p only."""
         from . import ext
         rows = h_x1_shard.shape[0]
         if h_out is None:
             h_out = torch.empty(rows, self.N, dtype=torch.float32, pin_memory=True)
         dev = self.device
+        if self.rank == self.src and (h_x2 is None or tuple(h_x2.shape) != (self.K, self.N)):
+            raise ValueError(f"rank {self.rank} is the source: h_x2 must be [{self.K}, {self.N}]")
         with torch.cuda.device(dev):
-            d_x2 = None
-            if self.rank == self.src:
+            if self.world == 1:
                 d_x2 = torch.empty(self.K, self.N, dtype=torch.float32, device=dev)
                 d_x2.copy_(h_x2, non_blocking=True)
-            if self.world == 1:
                 ext.pipelined_rows(h_x1_shard, h_out, dev, lambda d_x1, d_out: ext.chunk_compute(d_x1, d_x2),
                                    chunks=chunks, sync=sync)
                 return h_out
-            if self.rank == self.src:
-                pack_panels(d_x2, self.bounds, self.bufs)
-            works = broadcast_panels(self.bufs, self.src, self.group)
+            root = self.rank == self.src
+            n_pan = len(self.bufs)
+            works = [None] * n_pan
+            if not root:
+                # Enqueued before any H2D copy of this rank, so they wait for nothing local.
+                works = broadcast_panels(self.bufs, self.src, self.group)
+            staged = [0]
 
-            def waited():
-                for w in works:
-                    w.wait()
+            def stage(i):
+                # Rank src, on the H2D stream: panels up to p = i before x1's chunk i (all that
+                # remain once the chunks are out), each broadcast right after its copy.
+                if not root:
+                    return
+                upto = n_pan if i is None else min(n_pan, i + 1)
+                while staged[0] < upto:
+                    p = staged[0]
+                    n0, n1 = self.bounds[p]
+                    copy_columns_h2d(self.bufs[p], h_x2, n0, n1)
+                    works[p] = dist.broadcast(self.bufs[p], src=self.src, group=self.group, async_op=True)
+                    staged[0] += 1
 
             def make_compute(d_x1, d_out):
                 parts = [((n0, n1), ext.chunk_compute(d_x1, buf)) for (n0, n1), buf in zip(self.bounds, self.bufs)]
+                ready = [False] * n_pan
 
                 def compute(a, c):
-                    for (n0, n1), fn in parts:
+                    for p, ((n0, n1), fn) in enumerate(parts):
+                        if not ready[p]:
+                            works[p].wait()  # the compute stream waits for broadcast p
+                            ready[p] = True
                         fn(a, c[:, n0:n1])
                 return compute
-            ext.pipelined_rows(h_x1_shard, h_out, dev, make_compute, chunks=chunks, before=waited, sync=sync)
+            ext.pipelined_rows(h_x1_shard, h_out, dev, make_compute, chunks=chunks, sync=sync, h2d_hook=stage)
         return h_out
 
 

@@ -409,13 +409,15 @@ def _row_chunks(M, chunks, align=256, taper=True, min_rows=1024):
     return spans
 
 
-def pipelined_rows(h_x1, h_out, dev, make_compute, chunks=16, before=None, sync=True):
+def pipelined_rows(h_x1, h_out, dev, make_compute, chunks=16, before=None, sync=True, h2d_hook=None):
     """Stream host rows through the GPU: H2D of chunk i+1, compute(chunk i) and D2H of
     chunk i-1 overlap on three streams (copies on two side streams, compute on the current
     stream).  make_compute(d_x1, d_out) receives the full-size device buffers (so the
     caller can plan the unchunked product) and returns compute(d_x1_rows, d_out_rows),
     which launches the work for one chunk of rows; before() (optional) runs on the
-    current stream first (e.g. staging x2).  `chunks`: see _row_chunks."""
+    current stream first (e.g. staging x2).  h2d_hook(i) (optional) runs on the H2D stream
+    right before chunk i's copy, and h2d_hook(None) after the last one (e.g. copies of x2
+    interleaved with x1's rows).  `chunks`: see _row_chunks."""
     M, K = h_x1.shape
     N = h_out.shape[1]
     cur = torch.cuda.current_stream(dev)
@@ -428,9 +430,13 @@ def pipelined_rows(h_x1, h_out, dev, make_compute, chunks=16, before=None, sync=
     spans = _row_chunks(M, chunks)
     ev_in = []
     with torch.cuda.stream(h2d):
-        for r0, r1 in spans:
+        for i, (r0, r1) in enumerate(spans):
+            if h2d_hook is not None:
+                h2d_hook(i)
             d_x1[r0:r1].copy_(h_x1[r0:r1], non_blocking=True)
             ev_in.append(h2d.record_event())
+        if h2d_hook is not None:
+            h2d_hook(None)
     if before is not None:
         before()
     for (r0, r1), e in zip(spans, ev_in):
