@@ -48,6 +48,9 @@ def parse():
     p.add_argument("--variant", default="auto")
     p.add_argument("--panels", type=int, default=2)
     p.add_argument("--e2e-chunks", type=int, default=16)
+    p.add_argument("--nccl-priority", default="high", choices=["high", "normal"],
+                   help="priority of NCCL's streams (high: a broadcast's kernel is placed ahead of the GEMM's "
+                        "waiting CTAs)")
     p.add_argument("--no-extra", action="store_true", help="skip the configs 1-3 single-GPU figures")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (debug only)")
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end measurement (debug only)")
@@ -202,15 +205,18 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi -lms 200"}
 
 
-def setup_dist():
+def setup_dist(nccl_priority="high"):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         import datetime
         torch.cuda.set_device(local)
+        # High-priority NCCL streams: the GEMM holds every SM, so a broadcast's kernel on a
+        # normal-priority stream can wait for SMs behind the GEMM's own waiting CTAs.
+        opts = dist.ProcessGroupNCCL.Options(is_high_priority_stream=nccl_priority == "high")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+                                device_id=torch.device("cuda", local), pg_options=opts)
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
@@ -455,7 +461,7 @@ def other_variants(x1, x2, out, pk, names=("3xmixed", "tf32")):
 
 def main():
     args = parse()
-    world, rank, local = setup_dist()
+    world, rank, local = setup_dist(args.nccl_priority)
     if args.impl == "reference":
         reference_arm(args, world, rank)
         if world > 1:
@@ -657,7 +663,8 @@ def main():
             "config": {"workload": f"config5 row-sharded GEMM [{M5},{K5}] @ [{K5},{N5}] fp32, x2 broadcast "
                                    f"from rank 0 in {len(op.bounds)} column panel(s)",
                        "M": M5, "K": K5, "N": N5, "rows_per_rank": rows, "variant": variant, "split_k": split,
-                       "parallelism": f"row-shard x{world}" + (" + NCCL broadcast of x2" if world > 1 else ""),
+                       "parallelism": f"row-shard x{world}" + (f" + NCCL broadcast of x2 ({args.nccl_priority}-"
+                                                                 "priority NCCL streams)" if world > 1 else ""),
                        "l2": "inputs larger than L2 (4.56 GB per step)"},
             "roofline": {"bound": "tensor" if "tf32" in variant else "fp32", "achieved": round(achieved, 2),
                          "peak": round(peak, 2), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),

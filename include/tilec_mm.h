@@ -89,7 +89,8 @@ typedef enum tilec_mm_variant {
 typedef struct tilec_mm_cfg {
   int32_t variant;     /* tilec_mm_variant */
   int32_t split_k;     /* SPLITK / tensor variants: number of K slices (0 = choose) */
-  int32_t flags;       /* TILEC_MM_TRANS_A | TILEC_MM_TRANS_B (operand storage order), 0 = row-major */
+  int32_t flags;       /* TILEC_MM_TRANS_A | TILEC_MM_TRANS_B (operand storage order), TILEC_MM_STREAM_K,
+                          TILEC_MM_TILE_M64 | TILEC_MM_TILE_M128; 0 = row-major, library's choice */
   int32_t activation;  /* TILEC_MM_ACT_*: applied to every element of C as it is written */
   int32_t reserved[4]; /* must be zero */
 } tilec_mm_cfg;
@@ -118,6 +119,14 @@ typedef struct tilec_mm_cfg {
  * stream-K, so feeding that output back reproduces the plan.  Needs workspace (partial
  * tiles, 256 KiB per pair): ask tilec_mm_workspace_bytes. */
 #define TILEC_MM_STREAM_K 4
+
+/* cfg->flags (ABI version 6): rows per output tile of the 1-CTA tensor-core kernel.  AUTO
+ * takes 64-row tiles (tcgen05 M = 64) for products of at most 64 rows and 128-row tiles
+ * otherwise; these bits force one or the other (TILE_M64 also rules out the
+ * CTA-pair kernel; setting both is TILEC_ERR_BAD_ARG).  tilec_mm_plan sets the bit of the
+ * tile that runs whenever the 1-CTA tensor-core kernel is the plan. */
+#define TILEC_MM_TILE_M64 8
+#define TILEC_MM_TILE_M128 16
 
 /* C = A . B  (see the semantics block above).
  * cfg may be NULL (= AUTO).  workspace/ws_bytes: scratch for split-K partial sums;

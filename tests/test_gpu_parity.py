@@ -647,7 +647,8 @@ def test_stream_k_is_auto_choice_where_tiles_leave_pairs_idle():
     tiles: two waves on 74 pair slots), not where the last wave is nearly full (2048^3:
     64 tiles in one wave, which stream-K's slower k-blocks would not win back)."""
     x = torch.empty(2304, 2048, device=DEV)
-    assert ext.kernel_plan(x, x.t(), detail=True) == {"variant": "3xtf32", "split_k": 1, "stream_k": True}
+    assert ext.kernel_plan(x, x.t(), detail=True) == {"variant": "3xtf32", "split_k": 1, "stream_k": True,
+                                                      "tile_m": None}
     a = torch.empty(2048, 2048, device=DEV)
     assert not ext.kernel_plan(a, a, detail=True)["stream_k"]
     # Whole waves (or K slices asked for) keep one pair per tile.

@@ -50,6 +50,8 @@ class MMConfig(ctypes.Structure):
 TRANS_A = 1   # TILEC_MM_TRANS_A: A stored K x M (x1 is a column view, e.g. y.t())
 TRANS_B = 2   # TILEC_MM_TRANS_B: B stored N x K
 STREAM_K = 4  # TILEC_MM_STREAM_K: CTA-pair kernel as one wave of pairs sharing out K blocks
+TILE_M64 = 8     # TILEC_MM_TILE_M64: 1-CTA tensor-core kernel with 64-row tiles
+TILE_M128 = 16   # TILEC_MM_TILE_M128: 1-CTA tensor-core kernel with 128-row tiles
 ACTIVATIONS = {None: 0, "none": 0, "relu": 1, "gelu": 2}   # TILEC_MM_ACT_*
 
 

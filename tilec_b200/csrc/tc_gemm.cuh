@@ -4,7 +4,11 @@
 // out-of-range operand elements read as 0.0 (TMA zero fill, matching ext.py:21-22),
 // out-of-range outputs never stored (ext.py:24).
 //
-// One CTA owns a 128 x BN output tile (BN = 64/128/256); fp32 accumulators live in TMEM.
+// One CTA owns a BM x BN output tile (BM = 128 or 64, BN = 64/128/256); fp32 accumulators
+// live in TMEM.  BM = 64 (tcgen05.mma M = 64) serves products of at most 64 rows (batched
+// 64-row slices, GEMV-like shapes) without computing a half-empty tile, and halves the
+// partial-sum slabs of skinny split-K products.  Its accumulator holds tile row 16q + i in
+// TMEM lane 32q + i (i < 16) of quadrant q, so each epilogue warp drains 16 rows.
 // Warp-specialised:
 //   warp 0      TMA producer: A tile [128 x BK] K-major (128B/64B swizzle), B tile as
 //               BN/32 slabs of [BK x 32] MN-major (128B swizzle with 32-byte granules,
@@ -42,11 +46,13 @@ namespace tilec {
 
 constexpr int kTcBM = 128;
 
-template <int BN, int BK, int STAGES, bool SPLIT3>
+template <int BN, int BK, int STAGES, bool SPLIT3, int BM = kTcBM>
 struct TcCfg {
+  static_assert(BM == 128 || BM == 64, "BM");
   static constexpr int kEpiWarps = (SPLIT3 && BN >= 128) ? 8 : 4;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  static constexpr int kABytes = kTcBM * BK * 4;
+  static constexpr int kRowsPerWarp = BM / 4;  // tile rows an epilogue warp drains (TMEM lanes 0..rows-1 of its quadrant)
+  static constexpr int kABytes = BM * BK * 4;
   static constexpr int kBBytes = BK * BN * 4;
   // A stage holds the raw TMA tiles and, for 3XTF32, their lo(x) tiles next to them.  (A
   // separate, shallower lo ring was measured slower: it bounds how far the split stage can
@@ -85,14 +91,15 @@ __device__ __forceinline__ float tf32_hi(float x) {
 //
 // `bias` (per column, or nullptr) and `act` (kAct*) apply the fused epilogue on the way;
 // the test is made once, outside the store loop (EPI instantiates the loop with it).
-template <int NC, bool EPI>
+// ROWS: how many of the 32 staged rows to store (16 for a 64-row tile's warp).
+template <int NC, bool EPI, int ROWS = 32>
 __device__ __forceinline__ void store_rows_pass(const float* stage, float* out, int64_t ldo, int row0, int col0,
                                                 int M, int N, int vec_out, int lane, const float* __restrict__ bias,
                                                 int act) {
   constexpr int kPitch = NC + 4;
   constexpr int kChunks = NC / 4;  // 16-byte pieces per row
 #pragma unroll 4
-  for (int c = lane; c < 32 * kChunks; c += 32) {
+  for (int c = lane; c < ROWS * kChunks; c += 32) {
     const int r = c / kChunks, piece = c % kChunks;
     const int grow = row0 + r, gcol = col0 + 4 * piece;
     if (grow < M) {
@@ -119,7 +126,7 @@ __device__ __forceinline__ void store_rows_pass(const float* stage, float* out, 
   }
 }
 
-template <int NC>
+template <int NC, int ROWS = 32>
 __device__ __forceinline__ void store_rows_coalesced(float* stage, const float (&v)[NC], float* out, int64_t ldo,
                                                      int row0, int col0, int M, int N, int vec_out, int lane,
                                                      const float* __restrict__ bias = nullptr, int act = kActNone) {
@@ -129,9 +136,9 @@ __device__ __forceinline__ void store_rows_coalesced(float* stage, const float (
     *reinterpret_cast<float4*>(stage + lane * kPitch + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
   __syncwarp();
   if (bias != nullptr || act != kActNone)
-    store_rows_pass<NC, true>(stage, out, ldo, row0, col0, M, N, vec_out, lane, bias, act);
+    store_rows_pass<NC, true, ROWS>(stage, out, ldo, row0, col0, M, N, vec_out, lane, bias, act);
   else
-    store_rows_pass<NC, false>(stage, out, ldo, row0, col0, M, N, vec_out, lane, nullptr, kActNone);
+    store_rows_pass<NC, false, ROWS>(stage, out, ldo, row0, col0, M, N, vec_out, lane, nullptr, kActNone);
   __syncwarp();
 }
 
@@ -142,13 +149,14 @@ __device__ __forceinline__ void store_rows_coalesced(float* stage, const float (
 // ANY_LAYOUT = false fixes `layout` to row-major operands at compile time: the flipped
 // tile paths are then not in the kernel (keeping them there cost the common case 4-6 %
 // on B200, measured at 8192^3 and 65536x8192x8192).
-template <int BN, int BK, int STAGES, bool SPLIT3, bool HI_EXPLICIT, bool ANY_LAYOUT>
-__global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
+template <int BN, int BK, int STAGES, bool SPLIT3, bool HI_EXPLICIT, bool ANY_LAYOUT, int BM = kTcBM>
+__global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3, BM>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    float* __restrict__ out, int M, int N, int64_t ldo, int64_t out_slab, int K, int k_chunk,
                    int m_tiles, int n_tiles, int group_m, int vec_out, int layout_arg, int64_t out_batch,
                    const float* __restrict__ bias, int act, int shared) {
-  using Cfg = TcCfg<BN, BK, STAGES, SPLIT3>;
+  using Cfg = TcCfg<BN, BK, STAGES, SPLIT3, BM>;
+  constexpr int RW = Cfg::kRowsPerWarp;
   const int layout = ANY_LAYOUT ? layout_arg : 0;
   constexpr int KC = Cfg::kChunkBlocks;
   extern __shared__ uint8_t smem_raw[];
@@ -190,7 +198,7 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
   const int batch = static_cast<int>(blockIdx.y);
   const int a_batch = (shared & 1) ? 0 : batch, b_batch = (shared & 2) ? 0 : batch;
   out += static_cast<int64_t>(blockIdx.z) * out_slab + static_cast<int64_t>(batch) * out_batch;
-  const int m0 = tile_m * kTcBM;
+  const int m0 = tile_m * BM;
   const int n0 = tile_n * BN;
 
   const int k_begin = kslice * k_chunk;
@@ -241,7 +249,7 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
         const int k0 = k_begin + kb * BK;
         if (layout & kOpAMN) {
 #pragma unroll
-          for (int j = 0; j < kTcBM / 32; ++j)
+          for (int j = 0; j < BM / 32; ++j)
             tma_load_3d(a_raw(s) + j * BK * 128, &tmA, &full[s], m0 + 32 * j, k0, a_batch);
         } else {
           tma_load_3d(a_raw(s), &tmA, &full[s], k0, m0, a_batch);
@@ -271,7 +279,7 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const bool a_mn = (layout & kOpAMN) != 0, b_k = (layout & kOpBK) != 0;
-      const uint32_t idesc = make_idesc_tf32(kTcBM, BN, a_mn, !b_k);
+      const uint32_t idesc = make_idesc_tf32(BM, BN, a_mn, !b_k);
       // K step kk (8 elements) of a tile: 32 bytes along a K-major row, or 8 rows of 128
       // bytes in an MN-major slab.
       auto desc_a = [&](uint32_t base, int kk) {
@@ -397,8 +405,8 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
       pdl_launch_dependents();
       if (ok) {
         float* stage = reinterpret_cast<float*>(smem) + e * Cfg::kStageFloatsPerWarp;
-        store_rows_coalesced<COLS>(stage, tot, out, ldo, m0 + 32 * q, n0 + h * COLS, M, N, vec_out, lane, bias,
-                                   act);
+        store_rows_coalesced<COLS, RW>(stage, tot, out, ldo, m0 + RW * q, n0 + h * COLS, M, N, vec_out, lane, bias,
+                                       act);
       }
     } else {
       if (nkb > 0) ok = mbar_wait(acc_bar, 0, abort_flag);
@@ -419,7 +427,7 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          store_rows_coalesced<32>(stage, v, out, ldo, m0 + 32 * q, n0 + c * 32, M, N, vec_out, lane, bias, act);
+          store_rows_coalesced<32, RW>(stage, v, out, ldo, m0 + RW * q, n0 + c * 32, M, N, vec_out, lane, bias, act);
         }
       }
     }
@@ -438,7 +446,7 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3>::kThreads, 1)
   if (*abort_flag && warp >= 2) {
     constexpr int kWarpCols = BN / (Cfg::kEpiWarps / 4);
     const int e = warp - 2;
-    poison_rows(out, ldo, m0 + 32 * (warp & 3), 32, n0 + (e >> 2) * kWarpCols, kWarpCols, M, N, lane);
+    poison_rows(out, ldo, m0 + RW * (warp & 3), RW, n0 + (e >> 2) * kWarpCols, kWarpCols, M, N, lane);
   }
 }
 

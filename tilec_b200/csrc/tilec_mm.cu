@@ -57,13 +57,13 @@ std::once_flag g_encode_once;
 std::mutex g_table_mu;
 std::vector<int32_t> g_table;  // rows of 8 int32
 
-template <int BN, int BK, int STAGES, bool SPLIT3, bool HI>
+template <int BN, int BK, int STAGES, bool SPLIT3, bool HI, int BM = kTcBM>
 cudaError_t set_tc_attr() {
-  using Cfg = TcCfg<BN, BK, STAGES, SPLIT3>;
-  const cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, false>,
+  using Cfg = TcCfg<BN, BK, STAGES, SPLIT3, BM>;
+  const cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, false, BM>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, true>,
+  return cudaFuncSetAttribute(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, true, BM>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
 }
 
@@ -78,6 +78,16 @@ struct TcShape {
   static constexpr int kTf32Stages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int k3xStages = (BN == 256 ? 4 : (BN == 128 ? 6 : 8)) * 16 / k3xBK;
 };
+// 64-row tiles (16 / 24 / 40 KB stages at BN 64 / 128 / 256 in both modes).  Where the
+// registers allow two CTAs per SM (4 epilogue warps: TF32 at BN <= 128, 3XTF32 at BN 64)
+// the stages stop at 96 KB so that two CTAs fit; otherwise (one CTA per SM) 3XTF32 takes 8
+// stages at BN 128 and both modes 4 at BN 256.
+template <int BN>
+struct TcShape64 {
+  static constexpr int kTf32Stages = BN == 256 ? 4 : (BN == 128 ? 4 : 6);
+  static constexpr int k3xStages = BN == 256 ? 4 : (BN == 128 ? 8 : 6);
+};
+constexpr int kTcBM64 = 64;
 
 
 
@@ -114,6 +124,15 @@ cudaError_t init_device_attrs() {
   acc(set_tc_attr<256, k3xBK, TcShape<256>::k3xStages, true, false>());
   acc(set_tc_attr<128, k3xBK, TcShape<128>::k3xStages, true, false>());
   acc(set_tc_attr<64, k3xBK, TcShape<64>::k3xStages, true, false>());
+  acc(set_tc_attr<256, 32, TcShape64<256>::kTf32Stages, false, false, kTcBM64>());
+  acc(set_tc_attr<128, 32, TcShape64<128>::kTf32Stages, false, false, kTcBM64>());
+  acc(set_tc_attr<64, 32, TcShape64<64>::kTf32Stages, false, false, kTcBM64>());
+  acc(set_tc_attr<256, k3xBK, TcShape64<256>::k3xStages, true, true, kTcBM64>());
+  acc(set_tc_attr<128, k3xBK, TcShape64<128>::k3xStages, true, true, kTcBM64>());
+  acc(set_tc_attr<64, k3xBK, TcShape64<64>::k3xStages, true, true, kTcBM64>());
+  acc(set_tc_attr<256, k3xBK, TcShape64<256>::k3xStages, true, false, kTcBM64>());
+  acc(set_tc_attr<128, k3xBK, TcShape64<128>::k3xStages, true, false, kTcBM64>());
+  acc(set_tc_attr<64, k3xBK, TcShape64<64>::k3xStages, true, false, kTcBM64>());
   auto pair_attr = [&](auto kern, int smem) {
     acc(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   };
@@ -228,6 +247,7 @@ struct Plan {
   int split = 1;
   int64_t k_chunk = 0;
   int bn = 128;
+  int bm = kTcBM;     // tensor variants, 1-CTA kernel: rows per output tile (128 or 64)
   size_t ws_bytes = 0;
   int64_t ldw = 0;
   int flags = 0;      // TILEC_MM_TRANS_A / TILEC_MM_TRANS_B: how A and B are stored
@@ -387,7 +407,9 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
   int requested_split = cfg ? cfg->split_k : 0;
   const int flags = cfg ? cfg->flags : 0;
   const int act = cfg ? cfg->activation : 0;
-  if (flags & ~(TILEC_MM_TRANS_A | TILEC_MM_TRANS_B | TILEC_MM_STREAM_K)) return TILEC_ERR_BAD_ARG;
+  if (flags & ~(TILEC_MM_TRANS_A | TILEC_MM_TRANS_B | TILEC_MM_STREAM_K | TILEC_MM_TILE_M64 | TILEC_MM_TILE_M128))
+    return TILEC_ERR_BAD_ARG;
+  if ((flags & TILEC_MM_TILE_M64) && (flags & TILEC_MM_TILE_M128)) return TILEC_ERR_BAD_ARG;
   const bool want_sk = (flags & TILEC_MM_STREAM_K) != 0;
   if (act < TILEC_MM_ACT_NONE || act > TILEC_MM_ACT_GELU) return TILEC_ERR_BAD_ARG;
   if (cfg) {
@@ -416,7 +438,15 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
   p->variant = variant;
   if (tensor) {
     p->bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
-    p->pair = p->bn == 256 && M >= kPairMinM;
+    p->pair = p->bn == 256 && M >= kPairMinM && !(flags & TILEC_MM_TILE_M64);
+    if (!p->pair) {
+      // 64-row tiles: asked for, or products of at most 64 rows (a 128-row tile would be
+      // half empty).  Skinny products that split K keep 128-row tiles: 64-row tiles halve
+      // their partial-sum slabs but double each CTA's share of B, and measured slower on B200
+      // (512 x 4096 x 64: 10.2-12.4 us against 9.4 us).
+      const bool want64 = (flags & TILEC_MM_TILE_M64) || (!(flags & TILEC_MM_TILE_M128) && M <= 64);
+      if (want64) p->bm = kTcBM64;
+    }
     // The mixed split exists only in the one-pair-per-tile kernel.
     if (variant == TILEC_MM_3XMIXED && !p->pair) p->variant = variant = TILEC_MM_3XTF32;
     const bool mixed = variant == TILEC_MM_3XMIXED;
@@ -425,11 +455,11 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
     // 3XMIXED cut K at the same points.
     const int bk = (variant == TILEC_MM_TF32 || p->pair) ? 32 : k3xBK;
     const int slice_align = p->pair ? 32 : bk;
-    const int64_t tiles = cdiv(M, kTcBM) * cdiv(N, p->bn);
+    const int64_t tiles = cdiv(M, p->bm) * cdiv(N, p->bn);
     // The CTA pair launches two CTAs per 256-row x 256-column tile; each computes 128 rows
     // and loads half of the B columns.
     const int64_t ctas = (p->pair ? 2 * cdiv(M, 256) * cdiv(N, 256) : tiles) * nb;
-    const double cta_s = cta_seconds(kTcBM, p->bn, p->pair ? p->bn / 2 : p->bn, K,
+    const double cta_s = cta_seconds(p->bm, p->bn, p->pair ? p->bn / 2 : p->bn, K,
                                      variant == TILEC_MM_TF32 ? kRateTf32 : (mixed ? kRateMix : kRate3x), kBwPerSm);
     p->split = choose_split(ctas, d.sms, cta_s, double(M) * double(round_up(N, 4)) * 4.0 * double(nb),
                             K / (int64_t(slice_align) * 4), requested_split, /*one_wave=*/true);
@@ -515,7 +545,7 @@ int launch_status() {
 // N x K): box {bk, b_rows}, bk*4-byte swizzle.
 int encode_maps(const float* A, const float* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                 int64_t stride_a, int64_t nba, int64_t stride_b, int64_t nbb, int bk, int layout, int b_rows,
-                CUtensorMap* ma, CUtensorMap* mb) {
+                CUtensorMap* ma, CUtensorMap* mb, int a_rows = kTcBM) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = get_encode();
   if (!enc) return TILEC_ERR_NO_DEVICE;
   const CUtensorMapSwizzle k_sw = bk * 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
@@ -532,7 +562,7 @@ int encode_maps(const float* A, const float* B, int64_t M, int64_t N, int64_t K,
   };
   const bool ok_a = (layout & kOpAMN)
                         ? encode(ma, A, M, K, lda, stride_a, nba, 32, bk, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
-                        : encode(ma, A, K, M, lda, stride_a, nba, bk, kTcBM, k_sw);
+                        : encode(ma, A, K, M, lda, stride_a, nba, bk, a_rows, k_sw);
   const bool ok_b = (layout & kOpBK) ? encode(mb, B, K, N, ldb, stride_b, nbb, bk, b_rows, k_sw)
                                      : encode(mb, B, N, K, ldb, stride_b, nbb, 32, bk,
                                               CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
@@ -617,11 +647,11 @@ struct Launch {
   const float* bias = nullptr;
 };
 
-template <int BN, int BK, int STAGES, bool SPLIT3, bool HI>
+template <int BN, int BK, int STAGES, bool SPLIT3, bool HI, int BM = kTcBM>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
               cudaStream_t s) {
-  using Cfg = TcCfg<BN, BK, STAGES, SPLIT3>;
-  const int m_tiles = static_cast<int>(cdiv(M, kTcBM));
+  using Cfg = TcCfg<BN, BK, STAGES, SPLIT3, BM>;
+  const int m_tiles = static_cast<int>(cdiv(M, BM));
   const int n_tiles = static_cast<int>(cdiv(N, BN));
   const int group_m = 16;
   const dim3 grid(static_cast<unsigned>(int64_t(m_tiles) * n_tiles), static_cast<unsigned>(L.batch),
@@ -631,13 +661,19 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N
                     static_cast<int>(N), L.ldo, L.out_slab, static_cast<int>(K), static_cast<int>(L.k_chunk), m_tiles,
                     n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias, L.act, L.shared);
   };
-  return L.layout ? go(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, true>)
-                  : go(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, false>);
+  return L.layout ? go(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, true, BM>)
+                  : go(tc_gemm_kernel<BN, BK, STAGES, SPLIT3, HI, false, BM>);
 }
 
 template <int BN, bool SPLIT3, bool HI>
-int launch_tc_mode(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
-                   cudaStream_t s) {
+int launch_tc_mode(int bm, const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K,
+                   const Launch& L, cudaStream_t s) {
+  if (bm == kTcBM64) {
+    if constexpr (SPLIT3)
+      return launch_tc<BN, k3xBK, TcShape64<BN>::k3xStages, true, HI, kTcBM64>(ma, mb, M, N, K, L, s);
+    else
+      return launch_tc<BN, 32, TcShape64<BN>::kTf32Stages, false, false, kTcBM64>(ma, mb, M, N, K, L, s);
+  }
   if constexpr (SPLIT3)
     return launch_tc<BN, k3xBK, TcShape<BN>::k3xStages, true, HI>(ma, mb, M, N, K, L, s);
   else
@@ -685,12 +721,12 @@ int launch_tc2_sk(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64
 }
 
 template <bool SPLIT3, bool HI>
-int dispatch_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K,
+int dispatch_tc_bn(int bm, int bn, const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K,
                    const Launch& L, cudaStream_t s) {
   switch (bn) {
-    case 64: return launch_tc_mode<64, SPLIT3, HI>(ma, mb, M, N, K, L, s);
-    case 128: return launch_tc_mode<128, SPLIT3, HI>(ma, mb, M, N, K, L, s);
-    default: return launch_tc_mode<256, SPLIT3, HI>(ma, mb, M, N, K, L, s);
+    case 64: return launch_tc_mode<64, SPLIT3, HI>(bm, ma, mb, M, N, K, L, s);
+    case 128: return launch_tc_mode<128, SPLIT3, HI>(bm, ma, mb, M, N, K, L, s);
+    default: return launch_tc_mode<256, SPLIT3, HI>(bm, ma, mb, M, N, K, L, s);
   }
 }
 
@@ -1031,7 +1067,7 @@ int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, vo
   } else {
     CUtensorMap ma, mb;
     const int bk = p.bk;
-    rc = encode_maps(A, B, M, N, K, lda, ldb, sa, na, sb, nbb, bk, L.layout, p.pair ? 128 : p.bn, &ma, &mb);
+    rc = encode_maps(A, B, M, N, K, lda, ldb, sa, na, sb, nbb, bk, L.layout, p.pair ? 128 : p.bn, &ma, &mb, p.bm);
     if (rc) return rc;
     if (p.sk) {
       Tc2StreamK sk{};
@@ -1049,11 +1085,11 @@ int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, vo
            : p.variant == TILEC_MM_3XMIXED ? launch_tc2<true, false, true>(ma, mb, M, N, K, L, s)
                                            : launch_tc2<true, true>(ma, mb, M, N, K, L, s);
     else if (p.variant == TILEC_MM_TF32)
-      rc = dispatch_tc_bn<false, false>(p.bn, ma, mb, M, N, K, L, s);
+      rc = dispatch_tc_bn<false, false>(p.bm, p.bn, ma, mb, M, N, K, L, s);
     else if (p.variant == TILEC_MM_3XTF32)
-      rc = dispatch_tc_bn<true, false>(p.bn, ma, mb, M, N, K, L, s);
+      rc = dispatch_tc_bn<true, false>(p.bm, p.bn, ma, mb, M, N, K, L, s);
     else
-      rc = dispatch_tc_bn<true, true>(p.bn, ma, mb, M, N, K, L, s);
+      rc = dispatch_tc_bn<true, true>(p.bm, p.bn, ma, mb, M, N, K, L, s);
   }
   if (rc) return rc;
   if (p.split > 1) {
@@ -1161,7 +1197,10 @@ int tilec_mm_plan(const float* A, const float* B, const float* C, int64_t M, int
   std::memset(out, 0, sizeof(*out));
   out->variant = p.variant;
   out->split_k = p.split;
-  out->flags = p.flags | (p.sk ? TILEC_MM_STREAM_K : 0);
+  const bool tensor = p.variant == TILEC_MM_TF32 || p.variant == TILEC_MM_3XTF32 ||
+                      p.variant == TILEC_MM_3XTF32_MASKED || p.variant == TILEC_MM_3XMIXED;
+  out->flags = p.flags | (p.sk ? TILEC_MM_STREAM_K : 0) |
+               (tensor && !p.pair ? (p.bm == kTcBM64 ? TILEC_MM_TILE_M64 : TILEC_MM_TILE_M128) : 0);
   out->activation = p.act;
   return TILEC_OK;
 }

@@ -126,7 +126,17 @@ def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k, flags=0):
     return out
 
 
-def _matrix_mul(x1, x2, variant=None, split_k=0, out=None, stream_k=False):
+def _tile_flags(tile_m):
+    if tile_m is None:
+        return 0
+    if tile_m == 64:
+        return _native.TILE_M64
+    if tile_m == 128:
+        return _native.TILE_M128
+    raise ValueError(f"tile_m must be None, 64 or 128, got {tile_m!r}")
+
+
+def _matrix_mul(x1, x2, variant=None, split_k=0, out=None, stream_k=False, tile_m=None):
     """matrix_mul with explicit kernel choice.
 
     variant: None (= $TILEC_MM_VARIANT or "auto"), "simt", "splitk", "tf32", "3xtf32",
@@ -135,7 +145,9 @@ def _matrix_mul(x1, x2, variant=None, split_k=0, out=None, stream_k=False):
     (0 = library choice; 1 = none, which also rules out stream-K).  stream_k: run the
     CTA-pair kernel in its stream-K form
     whenever it is the kernel and split_k <= 1 (the library picks it by itself where it
-    pays).  out: optional preallocated [M, N] float32 result (unit column stride).
+    pays).  tile_m: None (library choice), 64 or 128 rows per tile of the 1-CTA tensor-core
+    kernel (64 also rules out the CTA pair).  out: optional preallocated [M, N] float32
+    result (unit column stride).
     """
     M, K = x1.shape
     K2, N = x2.shape
@@ -157,7 +169,8 @@ def _matrix_mul(x1, x2, variant=None, split_k=0, out=None, stream_k=False):
         ldc = _check_out(out, M, N, x1.device)
     if M == 0 or N == 0:
         return out
-    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0) | (_native.STREAM_K if stream_k else 0)
+    flags = ((_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0) | (_native.STREAM_K if stream_k else 0)
+             | _tile_flags(tile_m))
     return _launch(a, lda, b, ldb, out, ldc, M, N, K, variant or _default_variant(), split_k, flags)
 
 
@@ -257,7 +270,8 @@ def _batched_operand(x):
     return x, max(c, 1), False, r * c, nb
 
 
-def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, split_k=0, stream_k=False):
+def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, split_k=0, stream_k=False,
+                  tile_m=None):
     """act(x1 @ x2 + bias), batched: the fused, batched form of matrix_mul.
 
     x1 [M, K] or [B, M, K]; x2 [K, N] or [B, K, N] (a 2-D operand is shared by every
@@ -266,8 +280,8 @@ def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, sp
     [M, N] or [B, M, N].  One library call (tilec_mm_f32_ex): the batch is a grid dimension
     of the kernels and the epilogue runs where C is stored.  Row views and column views
     (.t() / .transpose(-1, -2)) of each slice are read in place, as in matrix_mul.
-    variant / split_k / stream_k as in _matrix_mul (stream-K shares out the tiles of the
-    whole batch).
+    variant / split_k / stream_k / tile_m as in _matrix_mul (stream-K shares out the tiles
+    of the whole batch).
     """
     _check_operand(x1)
     _check_operand(x2)
@@ -301,7 +315,8 @@ def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, sp
     nbatch = 1 if nb is None else nb
     if nbatch > 1 and sc < (M - 1) * ldc + N:
         raise ValueError("matrix_mul_ex: the batches of out overlap")
-    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0) | (_native.STREAM_K if stream_k else 0)
+    flags = ((_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0) | (_native.STREAM_K if stream_k else 0)
+             | _tile_flags(tile_m))
     lib = _native.load()
     from . import select
     select.ensure_installed()
@@ -321,9 +336,10 @@ def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, sp
     return out
 
 
-def kernel_plan(x1, x2, variant=None, split_k=0, stream_k=False, detail=False):
+def kernel_plan(x1, x2, variant=None, split_k=0, stream_k=False, detail=False, tile_m=None):
     """The (variant name, split_k) that matrix_mul would launch for these operands; with
-    detail=True a dict that also says whether the pair kernel runs in its stream-K form."""
+    detail=True a dict that also says whether the pair kernel runs in its stream-K form and
+    the rows per tile of the 1-CTA tensor-core kernel (None for other kernels)."""
     M, K = x1.shape
     _, N = x2.shape
     a, lda, ta = _operand(x1)
@@ -331,7 +347,8 @@ def kernel_plan(x1, x2, variant=None, split_k=0, stream_k=False, detail=False):
     lib = _native.load()
     from . import select
     select.ensure_installed()
-    flags = (_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0) | (_native.STREAM_K if stream_k else 0)
+    flags = ((_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0) | (_native.STREAM_K if stream_k else 0)
+             | _tile_flags(tile_m))
     cfg = _native.make_cfg(variant or _default_variant(), split_k, flags)
     res = _native.MMConfig()
     with torch.cuda.device(x1.device):
@@ -340,7 +357,9 @@ def kernel_plan(x1, x2, variant=None, split_k=0, stream_k=False, detail=False):
     _native.check(rc, "tilec_mm_plan")
     name = _native.VARIANT_NAMES.get(res.variant, res.variant)
     if detail:
-        return {"variant": name, "split_k": res.split_k, "stream_k": bool(res.flags & _native.STREAM_K)}
+        tm = 64 if res.flags & _native.TILE_M64 else (128 if res.flags & _native.TILE_M128 else None)
+        return {"variant": name, "split_k": res.split_k, "stream_k": bool(res.flags & _native.STREAM_K),
+                "tile_m": tm}
     return name, res.split_k
 
 
@@ -488,5 +507,6 @@ def chunk_compute(d_x1, d_x2, variant=None, split_k=0):
     """compute(rows_of_x1, rows_of_out) for one row chunk of the product d_x1 @ d_x2 with
     the kernel and K split that the unchunked product uses (planned once on the full-size
     buffers), so a chunked product equals the unchunked one bit for bit."""
-    v, s = kernel_plan(d_x1, d_x2, variant=variant, split_k=split_k)
-    return lambda a, c: _matrix_mul(a, d_x2, variant=v, split_k=s, out=c)
+    info = kernel_plan(d_x1, d_x2, variant=variant, split_k=split_k, detail=True)
+    v, s, tm = info["variant"], info["split_k"], info["tile_m"]
+    return lambda a, c: _matrix_mul(a, d_x2, variant=v, split_k=s, out=c, tile_m=tm)
