@@ -286,20 +286,26 @@ def pick(M, K, N):
     return ext.kernel_plan(a, b)
 
 
-def run(shape, variant="auto", split=0, reps=3, seed=0, stream_k=False):
-    """`reps` launches of one product (for profilers); prints the plan that ran."""
+def run(shape, variant="auto", split=0, reps=3, seed=0, stream_k=False, batch=0, tile_m=None):
+    """`reps` launches of one product (for profilers); prints the plan that ran.  batch > 0:
+    one matrix_mul_ex call over `batch` products of the shape per launch."""
     import torch
     from . import ext
     m, k, n = shape
     g = torch.Generator(device="cuda").manual_seed(seed)
-    a = torch.randn(m, k, device="cuda", generator=g)
-    b = torch.randn(k, n, device="cuda", generator=g)
-    c = torch.empty(m, n, device="cuda")
+    lead = (batch,) if batch > 0 else ()
+    a = torch.randn(*lead, m, k, device="cuda", generator=g)
+    b = torch.randn(*lead, k, n, device="cuda", generator=g)
+    c = torch.empty(*lead, m, n, device="cuda")
     for _ in range(reps):
-        ext._matrix_mul(a, b, variant=variant, split_k=split, out=c, stream_k=stream_k)
+        if batch > 0:
+            ext.matrix_mul_ex(a, b, out=c, variant=variant, split_k=split, stream_k=stream_k, tile_m=tile_m)
+        else:
+            ext._matrix_mul(a, b, variant=variant, split_k=split, out=c, stream_k=stream_k, tile_m=tile_m)
     torch.cuda.synchronize()
-    plan = ext.kernel_plan(a, b, variant=variant, split_k=split, stream_k=stream_k, detail=True)
-    print(json.dumps({"shape": [m, k, n], "plan": plan, "reps": reps}))
+    a0, b0 = (a[0], b[0]) if batch > 0 else (a, b)
+    plan = ext.kernel_plan(a0, b0, variant=variant, split_k=split, stream_k=stream_k, detail=True, tile_m=tile_m)
+    print(json.dumps({"shape": [m, k, n], "batch": batch, "plan": plan, "reps": reps}))
 
 
 def main(argv=None):
@@ -318,6 +324,9 @@ def main(argv=None):
     pr.add_argument("--split", type=int, default=0)
     pr.add_argument("--reps", type=int, default=3)
     pr.add_argument("--stream-k", action="store_true", help="ask for the pair kernel's stream-K form")
+    pr.add_argument("--batch", type=int, default=0, help="run a batch of this many products per launch")
+    pr.add_argument("--tile-m", type=int, default=None, choices=[64, 128],
+                    help="rows per tile of the 1-CTA tensor-core kernel")
     args = p.parse_args(argv)
     if args.cmd == "bench":
         bench(args.shapes, args.csv, args.seed)
@@ -325,7 +334,7 @@ def main(argv=None):
         train(args.csv, args.out)
     else:
         run(tuple(int(x) for x in args.shape.split(",")), args.variant, args.split, args.reps,
-            stream_k=args.stream_k)
+            stream_k=args.stream_k, batch=args.batch, tile_m=args.tile_m)
 
 
 if __name__ == "__main__":
