@@ -317,12 +317,19 @@ __global__ void __launch_bounds__(kSimtThreads, 2)
 // Batched: blockIdx.y is the batch; its slabs are W + blockIdx.y*S*slab and its result
 // goes to C + blockIdx.y*stride_c.  bias / act: the fused epilogue, applied to the
 // finished sum.
-template <int P, int U>
-__global__ void __launch_bounds__(256, 2) splitk_reduce_kernel(const float* __restrict__ W, float* __restrict__ C,
+//
+// LB: blocks per SM the registers are bounded for.  LB = 4 (64 registers, U = 1 only)
+// leaves an SM room for the next product's GEMM CTA, which can then launch (programmatic
+// dependent launch), allocate TMEM and prefetch its first operand tiles into L2 while this
+// kernel still runs: on B200 1.7-1.8 us faster for 1024x8192x128 and 512x2048x256, but
+// 0.5-0.9 us slower for N = 64 products (fewer loads in flight per thread), which keep LB = 2.
+template <int P, int U, int LB = 2>
+__global__ void __launch_bounds__(256, LB) splitk_reduce_kernel(const float* __restrict__ W, float* __restrict__ C,
                                                             int64_t M, int64_t N, int64_t ldw, int64_t ldc,
                                                             int64_t slab, int S, int vec_out, int64_t stride_c,
                                                             const float* __restrict__ bias, int act) {
   static_assert(8 % U == 0, "U divides the load batch");
+  static_assert(LB == 2 || (LB == 4 && U == 1), "64-register bound only for one column group per thread");
   constexpr int G = 256 / P;
   __shared__ float4 part[P > 1 ? P - 1 : 1][P > 1 ? U * G : 1];
   pdl_wait();

@@ -888,7 +888,7 @@ int launch_reduce_p(int U, dim3 grid, const Reduce& r, int vec_out, cudaStream_t
   switch (U) {
     case 4: return go(splitk_reduce_kernel<P, 4>);
     case 2: return go(splitk_reduce_kernel<P, 2>);
-    default: return go(splitk_reduce_kernel<P, 1>);
+    default: return r.N > 64 ? go(splitk_reduce_kernel<P, 1, 4>) : go(splitk_reduce_kernel<P, 1>);
   }
 }
 
