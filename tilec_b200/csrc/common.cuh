@@ -189,18 +189,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// L2 prefetch of the tile a tma_load_3d with the same coordinates would copy: no shared-
-// memory destination and no completion to wait for.  Issued before pdl_wait() for a
-// kernel's first operand tiles, it overlaps their DRAM latency with the previous kernel's
-// tail; it is safe even when that kernel writes the operand, since L2 is the point of
-// coherence (a prefetched line that is written afterwards is simply updated there).
-__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int32_t x, int32_t y, int32_t z) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y), "r"(z)
-               : "memory");
-}
-
 // ---------------------------------------------------------------- epilogue
 // Element-wise epilogue applied where C is written: v + bias (when given), then the
 // activation (TILEC_MM_ACT_*: 0 none, 1 ReLU, 2 GELU with the exact erf form).

@@ -213,21 +213,6 @@ __global__ void __launch_bounds__(Tc2Cfg<BN, STAGES, SPLIT3, false, kTc2Bk<SPLIT
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    // This CTA's tiles of the first STAGES fills, into L2 while the previous kernel finishes.
-    const int npf = nkb < STAGES ? nkb : STAGES;
-    for (int kb = 0; kb < npf; ++kb) {
-      const int k0 = k_begin + kb * BK;
-      if (layout & kOpAMN) {
-        for (int j = 0; j < 128 / 32; ++j) tma_prefetch_l2_3d(&tmA, m0 + 32 * j, k0, a_batch);
-      } else {
-        tma_prefetch_l2_3d(&tmA, k0, m0, a_batch);
-      }
-      if (layout & kOpBK) {
-        tma_prefetch_l2_3d(&tmB, k0, nb0, b_batch);
-      } else {
-        for (int j = 0; j < Cfg::kBNHalf / 32; ++j) tma_prefetch_l2_3d(&tmB, nb0 + 32 * j, k0, b_batch);
-      }
-    }
   }
   __syncwarp();
   cluster_sync();  // both CTAs' barriers exist before anyone arrives remotely

@@ -224,21 +224,6 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3, BM>::kThreads, 1
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    // The tiles of the first STAGES fills, into L2 while the previous kernel finishes.
-    const int npf = nkb < STAGES ? nkb : STAGES;
-    for (int kb = 0; kb < npf; ++kb) {
-      const int k0 = k_begin + kb * BK;
-      if (layout & kOpAMN) {
-        for (int j = 0; j < BM / 32; ++j) tma_prefetch_l2_3d(&tmA, m0 + 32 * j, k0, a_batch);
-      } else {
-        tma_prefetch_l2_3d(&tmA, k0, m0, a_batch);
-      }
-      if (layout & kOpBK) {
-        tma_prefetch_l2_3d(&tmB, k0, n0, b_batch);
-      } else {
-        for (int j = 0; j < BN / 32; ++j) tma_prefetch_l2_3d(&tmB, n0 + 32 * j, k0, b_batch);
-      }
-    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -248,7 +233,7 @@ __global__ void __launch_bounds__(TcCfg<BN, BK, STAGES, SPLIT3, BM>::kThreads, 1
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // Barrier init, TMEM allocation, descriptor and L2 prefetches overlap the previous kernel.
+  // Barrier init, TMEM allocation and descriptor prefetch overlap the previous kernel.
   pdl_wait();
 
   if (warp == 0) {
