@@ -36,6 +36,7 @@ CASES = [
     ("3xtf32", (200, 1024, 256), 1, False),     # 1-CTA 3xTF32, BN 256, one slice
     ("3xtf32", (2048, 2048, 2048), 1, False),   # CTA pair, one pair per tile
     ("tf32", (2048, 2048, 2048), 1, False),     # CTA pair, TF32
+    ("tf32", (2304, 1024, 2304), 1, False),     # persistent TF32 pairs (81 tiles over the resident pairs)
     ("3xmixed", (2048, 2048, 2048), 1, False),  # CTA pair, mixed split
     ("3xtf32", (1024, 4096, 1024), 3, False),   # CTA pair, split-K
     ("3xtf32", (2304, 2048, 2304), 1, True),    # stream-K pairs with partial tiles

@@ -749,3 +749,47 @@ def test_non_finite_operands(variant):
     err = ((got[fin].double() - ref64).norm() / ref64.norm()).item()
     assert err <= TOL[variant], f"{variant}: finite outputs relFrob {err:.3e}"
     assert _status_clean()
+
+
+@pytest.mark.parametrize("shape,batch,ta,tb", [((2304, 1024, 2304), 0, False, False), ((4096, 512, 4096), 0, False, False),
+                                               ((2000, 700, 3000), 0, False, False), ((2304, 1024, 2304), 0, True, True),
+                                               ((1024, 256, 2048), 3, False, False)])
+def test_tf32_persistent_pairs(shape, batch, ta, tb):
+    """TF32 products with more 256 x 256 tiles than pairs fit at once run on the persistent
+    pair kernel (two TMEM accumulators per pair, a tile's epilogue overlapping the next
+    tile's MMAs).  Its per-tile MMA sequence is the 1-CTA kernel's, so every 128-row block
+    equals what the 1-CTA TF32 kernel gives for that slice, bit for bit; and it keeps the
+    TF32 gate, with operands read in place when transposed and with batches."""
+    m, k, n = shape
+    g = torch.Generator(device=DEV).manual_seed(m + n + 3 * batch)
+    lead = (batch,) if batch else ()
+    a = torch.randn(*lead, m, k, device=DEV, generator=g)
+    b = torch.randn(*lead, k, n, device=DEV, generator=g)
+    if ta:
+        a = a.transpose(-1, -2).contiguous().transpose(-1, -2)
+    if tb:
+        b = b.transpose(-1, -2).contiguous().transpose(-1, -2)
+    if batch:
+        got = ext.matrix_mul_ex(a, b, variant="tf32", split_k=1)
+    else:
+        got = ext._matrix_mul(a, b, variant="tf32", split_k=1)
+    for i in range(max(batch, 1)):
+        ai, bi, gi = (a[i], b[i], got[i]) if batch else (a, b, got)
+        for r0 in range(0, m, 512):
+            part = ext._matrix_mul(ai[r0:r0 + 128], bi, variant="tf32", split_k=1)
+            assert torch.equal(gi[r0:r0 + 128], part), (i, r0)
+    ref = (a.double() @ b.double())
+    assert ((got.double() - ref).norm() / ref.norm()).item() <= 5e-3
+    assert _status_clean()
+
+
+@pytest.mark.parametrize("act", (None, "relu", "gelu"))
+def test_tf32_persistent_pairs_fused_epilogue(act):
+    g = torch.Generator(device=DEV).manual_seed(11)
+    a = torch.randn(2304, 512, device=DEV, generator=g)
+    b = torch.randn(512, 2304, device=DEV, generator=g)
+    bias = torch.randn(2304, device=DEV, generator=g)
+    got = ext.matrix_mul_ex(a, b, bias=bias, activation=act, variant="tf32", split_k=1)
+    plain = ext._matrix_mul(a, b, variant="tf32", split_k=1) + bias
+    want = {None: plain, "relu": torch.relu(plain), "gelu": torch.nn.functional.gelu(plain)}[act]
+    assert torch.allclose(got, want, rtol=1e-6, atol=1e-5)

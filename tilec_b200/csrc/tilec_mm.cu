@@ -25,6 +25,7 @@
 #include "tc_gemm.cuh"
 #include "tc2_gemm.cuh"
 #include "tc2_sk.cuh"
+#include "tc2_tf32p.cuh"
 
 static_assert(TILEC_DEV_STATUS_TIMEOUT == tilec::TILEC_DEV_TIMEOUT && TILEC_DEV_STATUS_TMEM == tilec::TILEC_DEV_TMEM &&
                   TILEC_DEV_STATUS_BAD_LAUNCH == tilec::TILEC_DEV_BAD_LAUNCH,
@@ -45,6 +46,7 @@ struct DeviceInfo {
   int cc_minor = 0;
   int max_smem_optin = 0;
   int pair_slots = 0;  // CTA pairs of the stream-K pair kernel resident at once (0: stream-K off)
+  int tf32p_slots = 0; // CTA pairs of the persistent TF32 pair kernel resident at once (0: not used)
   cudaError_t init_err = cudaSuccess;
 };
 
@@ -156,12 +158,35 @@ cudaError_t init_device_attrs() {
   pair_attr(tc2_sk_kernel<256, kPair3xStages, true, true, true>, s3x);
   pair_attr(tc2_sk_kernel<256, kPairStages, false, false, false>, sTf);
   pair_attr(tc2_sk_kernel<256, kPairStages, false, false, true>, sTf);
+  pair_attr(tc2_tf32p_kernel<false>, Tc2PCfg::kSmemBytes);
+  pair_attr(tc2_tf32p_kernel<true>, Tc2PCfg::kSmemBytes);
   return e;
 }
 
 // CTA pairs of the stream-K kernel that fit on the device at once (clusters must sit within
 // one GPC, so this can be below SMs / 2).  A stream-K launch never asks for more: its pairs
 // wait on one another's partial tiles.  0 disables stream-K.
+// CTA pairs of the persistent TF32 pair kernel that fit on the device at once (its grid).
+int query_tf32p_slots() {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(2, 1, 1);
+  lc.blockDim = dim3(Tc2PCfg::kThreads);
+  lc.dynamicSmemBytes = Tc2PCfg::kSmemBytes;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  lc.attrs = &attr;
+  lc.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, tc2_tf32p_kernel<false>, &lc) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
 int query_pair_slots() {
   using Cfg = Tc2Cfg<256, kPair3xStages, true, true, 32>;
   cudaLaunchConfig_t lc = {};
@@ -201,6 +226,7 @@ int current_device(DeviceInfo** out) {
     if (e == cudaSuccess && d.cc_major != 10) e = cudaErrorNoKernelImageForDevice;
     if (e == cudaSuccess) e = init_device_attrs();
     if (e == cudaSuccess) d.pair_slots = query_pair_slots();
+    if (e == cudaSuccess) d.tf32p_slots = query_tf32p_slots();
     d.init_err = e;
     cudaGetLastError();
   });
@@ -255,6 +281,8 @@ struct Plan {
   bool tpose_a = false, tpose_b = false;  // SIMT variants: transposed operand -> row-major copy
   bool pair = false;  // 3XTF32 on a CTA pair (tc2_gemm_kernel, 256 x 256 tiles)
   bool sk = false;    // pair kernel in its stream-K form (split == 1)
+  bool persist = false;  // TF32 on the persistent pair kernel (split == 1, more tiles than pairs fit)
+  int persist_pairs = 0;
   int bk = 16;        // tensor variants: K per pipeline stage of the kernel that runs (TMA box depth)
   int sk_pairs = 0, sk_dp_tiles = 0, sk_tiles = 0, sk_tiles_per_batch = 0;
   size_t off_sk = 0;  // [sk_pairs partial tiles][sk_pairs x 16 ready flags]
@@ -469,6 +497,15 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
     p->bk = bk;
     if (p->pair && !mixed && K > 0 && requested_split <= 1 && (want_sk || (requested_split == 0 && p->split == 1))) {
       plan_stream_k(d, M, N, K, nb, bk, variant == TILEC_MM_TF32, cta_s, want_sk, p);
+    }
+    // TF32 tiles beyond one wave of pairs run on the persistent pair kernel: each pair walks
+    // its tiles with two TMEM accumulators, so a tile's epilogue overlaps the next tile's MMAs.
+    // Its per-tile MMA sequence is the one-pair-per-tile kernel's, so the results are the same.
+    const int64_t pair_tiles = cdiv(M, 256) * cdiv(N, 256) * nb;
+    if (p->pair && !p->sk && variant == TILEC_MM_TF32 && p->split == 1 && d.tf32p_slots > 0 &&
+        pair_tiles > d.tf32p_slots && pair_tiles < (int64_t(1) << 30)) {
+      p->persist = true;
+      p->persist_pairs = d.tf32p_slots;
     }
   } else {
     p->bn = N <= 64 ? 64 : 128;
@@ -718,6 +755,23 @@ int launch_tc2_sk(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64
   };
   return L.layout ? go(tc2_sk_kernel<256, kStages, SPLIT3, HI, true>)
                   : go(tc2_sk_kernel<256, kStages, SPLIT3, HI, false>);
+}
+
+// Persistent TF32 pair kernel: `pairs` pairs share out the 256 x 256 tiles of all batches.
+int launch_tc2p(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
+                int pairs, cudaStream_t s) {
+  const int mp_tiles = static_cast<int>(cdiv(M, 256));
+  const int n_tiles = static_cast<int>(cdiv(N, 256));
+  const int per_batch = mp_tiles * n_tiles;
+  const int total = per_batch * L.batch;
+  const int group_m = 8;
+  if (pairs > total) pairs = total;
+  auto go = [&](auto kern) {
+    return launch_k(kern, dim3(static_cast<unsigned>(2 * pairs)), dim3(Tc2PCfg::kThreads), Tc2PCfg::kSmemBytes, s, 2,
+                    ma, mb, L.out, static_cast<int>(M), static_cast<int>(N), L.ldo, static_cast<int>(K), mp_tiles,
+                    n_tiles, group_m, per_batch, total, L.vec_out, L.layout, L.out_batch, L.bias, L.act, L.shared);
+  };
+  return L.layout ? go(tc2_tf32p_kernel<true>) : go(tc2_tf32p_kernel<false>);
 }
 
 template <bool SPLIT3, bool HI>
@@ -1079,6 +1133,8 @@ int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, vo
       rc = p.variant == TILEC_MM_TF32     ? launch_tc2_sk<false, false>(ma, mb, M, N, K, L, sk, p.sk_pairs, s)
            : p.variant == TILEC_MM_3XTF32 ? launch_tc2_sk<true, false>(ma, mb, M, N, K, L, sk, p.sk_pairs, s)
                                           : launch_tc2_sk<true, true>(ma, mb, M, N, K, L, sk, p.sk_pairs, s);
+    } else if (p.persist) {
+      rc = launch_tc2p(ma, mb, M, N, K, L, p.persist_pairs, s);
     } else if (p.pair)
       rc = p.variant == TILEC_MM_TF32      ? launch_tc2<false, false>(ma, mb, M, N, K, L, s)
            : p.variant == TILEC_MM_3XTF32  ? launch_tc2<true, false>(ma, mb, M, N, K, L, s)
