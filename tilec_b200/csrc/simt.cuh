@@ -250,10 +250,18 @@ __global__ void __launch_bounds__(kSimtThreads, 2)
         const float4 b1 = *reinterpret_cast<const float4*>(bs + k * BN + 64);
         b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
       }
+      // Packed two-wide FMAs (sm_100 FFMA2): per component exactly fmaf, half the FMA
+      // instructions, so more issue slots go to the FMA pipe.
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < 8; ++i) {
+        const float2 ai = make_float2(a[i], a[i]);
 #pragma unroll
-        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        for (int j = 0; j < TN; j += 2) {
+          const float2 r = __ffma2_rn(ai, make_float2(b[j], b[j + 1]), make_float2(acc[i][j], acc[i][j + 1]));
+          acc[i][j] = r.x;
+          acc[i][j + 1] = r.y;
+        }
+      }
     }
   }
   cp_async_wait<0>();
