@@ -415,6 +415,58 @@ def test_transposed_views_forced_split_and_pair():
     assert ext.kernel_plan(y.t(), z.t(), variant="3xtf32")[0] == "3xtf32"
 
 
+NARROW_PAIR_SHAPES = [(1024, 4096, 300), (300, 520, 260), (777, 1000, 384), (513, 3001, 333)]
+
+
+@pytest.mark.parametrize("shape", NARROW_PAIR_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("variant", ("3xtf32", "tf32"))
+def test_pair_tiles_128_columns_wide(shape, variant):
+    """CTA pairs on 128-column tiles (M >= 256, 256 < N <= 384): one pair per tile, forced K
+    splits and the stream-K form all meet the variant's gate, repeat bit for bit, raw and
+    masked hi agree, and a TF32 pair equals the 1-CTA kernel row block by row block (same
+    K order per element; the 1-CTA kernel runs 256-column tiles here)."""
+    m, k, n = shape
+    g = torch.Generator(device=DEV).manual_seed(m + 3 * k + n)
+    a = torch.randn(m, k, device=DEV, generator=g)
+    b = torch.randn(k, n, device=DEV, generator=g)
+    ref = a.double() @ b.double()
+    for split, sk in ((1, False), (3, False), (0, True), (0, False)):
+        got = ext._matrix_mul(a, b, variant=variant, split_k=split, stream_k=sk)
+        again = ext._matrix_mul(a, b, variant=variant, split_k=split, stream_k=sk)
+        assert torch.equal(got, again), (split, sk)
+        assert ((got.double() - ref).norm() / ref.norm()).item() <= TOL[variant], (split, sk)
+        if variant == "3xtf32":
+            masked = ext._matrix_mul(a, b, variant="3xtf32_masked", split_k=split, stream_k=sk)
+            assert torch.equal(got, masked), (split, sk)
+        elif split == 1 and not sk:
+            for r0 in range(0, m, 128):
+                part = ext._matrix_mul(a[r0:r0 + 128], b, variant="tf32", split_k=1)
+                assert torch.equal(got[r0:r0 + 128], part), r0
+    if k % 4 == 0 and n % 4 == 0:
+        # Column views read in place equal the contiguous operands.
+        for split in (1, 3):
+            tv = ext._matrix_mul(a.t().contiguous().t(), b.t().contiguous().t(), variant=variant, split_k=split)
+            assert torch.equal(tv, ext._matrix_mul(a, b, variant=variant, split_k=split)), split
+    assert _status_clean()
+
+
+def test_pair_tiles_128_columns_wide_batched_and_misaligned():
+    """Batched 128-column pair tiles with an odd row stride (both operands packed) equal the
+    single products slice by slice."""
+    g = torch.Generator(device=DEV).manual_seed(17)
+    nb, m, k, n = 3, 600, 1001, 301
+    x1 = torch.randn(nb, m, k + 1, device=DEV, generator=g)[:, :, 1:]
+    x2 = torch.randn(nb, k, n, device=DEV, generator=g)
+    for variant in ("3xtf32", "tf32"):
+        for split in (1, 3):
+            got = ext.matrix_mul_ex(x1, x2, variant=variant, split_k=split)
+            for i in range(nb):
+                assert torch.equal(got[i], ext._matrix_mul(x1[i], x2[i], variant=variant, split_k=split)), i
+            ref = torch.matmul(x1.double(), x2.double())
+            assert ((got.double() - ref).norm() / ref.norm()).item() <= TOL[variant]
+    assert _status_clean()
+
+
 def _ref64(x1, x2, bias=None, act=None):
     r = torch.matmul(x1.double(), x2.double())
     if bias is not None:

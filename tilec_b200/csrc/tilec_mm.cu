@@ -158,6 +158,23 @@ cudaError_t init_device_attrs() {
   pair_attr(tc2_sk_kernel<256, kPair3xStages, true, true, true>, s3x);
   pair_attr(tc2_sk_kernel<256, kPairStages, false, false, false>, sTf);
   pair_attr(tc2_sk_kernel<256, kPairStages, false, false, true>, sTf);
+  // 256 x 128 pair tiles (N columns that pad badly to 256): 3XTF32, its masked form and TF32.
+  constexpr int k3x128 = Tc2Cfg<128, kPair3xStages, true, false, 32>::kSmemBytes;
+  constexpr int kTf128 = Tc2Cfg<128, kPairStages, false>::kSmemBytes;
+  constexpr int s3x128 = Tc2Cfg<128, kPair3xStages, true, true, 32>::kSmemBytes;
+  constexpr int sTf128 = Tc2Cfg<128, kPairStages, false, true, 32>::kSmemBytes;
+  pair_attr(tc2_gemm_kernel<128, kPair3xStages, true, false, false>, k3x128);
+  pair_attr(tc2_gemm_kernel<128, kPair3xStages, true, true, false>, k3x128);
+  pair_attr(tc2_gemm_kernel<128, kPair3xStages, true, false, true>, k3x128);
+  pair_attr(tc2_gemm_kernel<128, kPair3xStages, true, true, true>, k3x128);
+  pair_attr(tc2_gemm_kernel<128, kPairStages, false, false, false>, kTf128);
+  pair_attr(tc2_gemm_kernel<128, kPairStages, false, false, true>, kTf128);
+  pair_attr(tc2_sk_kernel<128, kPair3xStages, true, false, false>, s3x128);
+  pair_attr(tc2_sk_kernel<128, kPair3xStages, true, true, false>, s3x128);
+  pair_attr(tc2_sk_kernel<128, kPair3xStages, true, false, true>, s3x128);
+  pair_attr(tc2_sk_kernel<128, kPair3xStages, true, true, true>, s3x128);
+  pair_attr(tc2_sk_kernel<128, kPairStages, false, false, false>, sTf128);
+  pair_attr(tc2_sk_kernel<128, kPairStages, false, false, true>, sTf128);
   pair_attr(tc2_tf32p_kernel<false>, Tc2PCfg::kSmemBytes);
   pair_attr(tc2_tf32p_kernel<true>, Tc2PCfg::kSmemBytes);
   return e;
@@ -407,7 +424,7 @@ void plan_stream_k(const DeviceInfo& d, int64_t M, int64_t N, int64_t K, int64_t
                    double cta_s, bool forced, Plan* p) {
   const int64_t P = d.pair_slots;
   if (P <= 0) return;
-  const int64_t per_batch = cdiv(M, 256) * cdiv(N, 256);
+  const int64_t per_batch = cdiv(M, 256) * cdiv(N, p->bn);
   const int64_t T = per_batch * nb, nkb = cdiv(K, bk);
   if (T >= (int64_t(1) << 30)) return;
   if (!forced) {
@@ -467,6 +484,13 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
   if (tensor) {
     p->bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
     p->pair = p->bn == 256 && M >= kPairMinM && !(flags & TILEC_MM_TILE_M64);
+    // Pair tiles 128 columns wide for 256 < N <= 384, where 256-wide tiles pad N to 512
+    // columns of MMAs and 128-wide ones to 384.  A 128-column pair reads 4/3 of the shared
+    // memory per FLOP of a 256-column one, and on B200 ran each FLOP ~1.3x slower
+    // (8192 x 4096 x 1100: 420 against 307 us), so narrower tiles pay only where they cut
+    // the padding by a third (1024 x 4096 x 300 3xTF32: 28.4 against 30.8 us; TF32 19.5
+    // against 22.2 us).  N = 777 keeps 256 (56.7 against 47.9 us).  The mixed split keeps 256.
+    if (p->pair && variant != TILEC_MM_3XMIXED && N > 256 && N <= 384) p->bn = 128;
     if (!p->pair) {
       // 64-row tiles: asked for, or products of at most 64 rows (a 128-row tile would be
       // half empty).  Skinny products that split K keep 128-row tiles: 64-row tiles halve
@@ -486,7 +510,7 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
     const int64_t tiles = cdiv(M, p->bm) * cdiv(N, p->bn);
     // The CTA pair launches two CTAs per 256-row x 256-column tile; each computes 128 rows
     // and loads half of the B columns.
-    const int64_t ctas = (p->pair ? 2 * cdiv(M, 256) * cdiv(N, 256) : tiles) * nb;
+    const int64_t ctas = (p->pair ? 2 * cdiv(M, 256) * cdiv(N, p->bn) : tiles) * nb;
     const double cta_s = cta_seconds(p->bm, p->bn, p->pair ? p->bn / 2 : p->bn, K,
                                      variant == TILEC_MM_TF32 ? kRateTf32 : (mixed ? kRateMix : kRate3x), kBwPerSm);
     p->split = choose_split(ctas, d.sms, cta_s, double(M) * double(round_up(N, 4)) * 4.0 * double(nb),
@@ -502,7 +526,7 @@ int make_plan(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, Pl
     // its tiles with two TMEM accumulators, so a tile's epilogue overlaps the next tile's MMAs.
     // Its per-tile MMA sequence is the one-pair-per-tile kernel's, so the results are the same.
     const int64_t pair_tiles = cdiv(M, 256) * cdiv(N, 256) * nb;
-    if (p->pair && !p->sk && variant == TILEC_MM_TF32 && p->split == 1 && d.tf32p_slots > 0 &&
+    if (p->pair && p->bn == 256 && !p->sk && variant == TILEC_MM_TF32 && p->split == 1 && d.tf32p_slots > 0 &&
         pair_tiles > d.tf32p_slots && pair_tiles < (int64_t(1) << 30)) {
       p->persist = true;
       p->persist_pairs = d.tf32p_slots;
@@ -717,13 +741,13 @@ int launch_tc_mode(int bm, const CUtensorMap& ma, const CUtensorMap& mb, int64_t
     return launch_tc<BN, 32, TcShape<BN>::kTf32Stages, false, false>(ma, mb, M, N, K, L, s);
 }
 
-template <bool SPLIT3, bool HI, bool MIXED = false>
+template <int BN, bool SPLIT3, bool HI, bool MIXED = false>
 int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
                cudaStream_t s) {
   constexpr int kStages = SPLIT3 ? kPair3xStages : kPairStages;
-  using Cfg = Tc2Cfg<256, kStages, SPLIT3, false, kTc2Bk<SPLIT3, MIXED>>;
+  using Cfg = Tc2Cfg<BN, kStages, SPLIT3, false, kTc2Bk<SPLIT3, MIXED>>;
   const int mp_tiles = static_cast<int>(cdiv(M, 256));
-  const int n_tiles = static_cast<int>(cdiv(N, 256));
+  const int n_tiles = static_cast<int>(cdiv(N, BN));
   const int group_m = 8;
   const dim3 grid(static_cast<unsigned>(2 * int64_t(mp_tiles) * n_tiles), static_cast<unsigned>(L.batch),
                   static_cast<unsigned>(L.split));
@@ -732,29 +756,29 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t 
                     static_cast<int>(N), L.ldo, L.out_slab, static_cast<int>(K), static_cast<int>(L.k_chunk),
                     mp_tiles, n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias, L.act, L.shared);
   };
-  return L.layout ? go(tc2_gemm_kernel<256, kStages, SPLIT3, HI, true, MIXED>)
-                  : go(tc2_gemm_kernel<256, kStages, SPLIT3, HI, false, MIXED>);
+  return L.layout ? go(tc2_gemm_kernel<BN, kStages, SPLIT3, HI, true, MIXED>)
+                  : go(tc2_gemm_kernel<BN, kStages, SPLIT3, HI, false, MIXED>);
 }
 
 // Stream-K form: the flag reset (programmatic serialisation on both sides, so the GEMM's
 // set-up still overlaps the previous kernel) and a grid of `pairs` pairs.
-template <bool SPLIT3, bool HI>
+template <int BN, bool SPLIT3, bool HI>
 int launch_tc2_sk(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t N, int64_t K, const Launch& L,
                   const Tc2StreamK& sk, int pairs, cudaStream_t s) {
   int rc = launch_k(sk_flags_reset_kernel, dim3(1), dim3(256), 0, s, 1, sk.flags, pairs * kSkFlagsPerPair);
   if (rc) return rc;
   constexpr int kStages = SPLIT3 ? kPair3xStages : kPairStages;
-  using Cfg = Tc2Cfg<256, kStages, SPLIT3, true, 32>;
+  using Cfg = Tc2Cfg<BN, kStages, SPLIT3, true, 32>;
   const int mp_tiles = static_cast<int>(cdiv(M, 256));
-  const int n_tiles = static_cast<int>(cdiv(N, 256));
+  const int n_tiles = static_cast<int>(cdiv(N, BN));
   const int group_m = 8;
   auto go = [&](auto kern) {
     return launch_k(kern, dim3(static_cast<unsigned>(2 * pairs)), dim3(Cfg::kThreads), Cfg::kSmemBytes, s, 2, ma,
                     mb, L.out, static_cast<int>(M), static_cast<int>(N), L.ldo, static_cast<int>(K), mp_tiles,
                     n_tiles, group_m, L.vec_out, L.layout, L.out_batch, L.bias, L.act, L.shared, sk);
   };
-  return L.layout ? go(tc2_sk_kernel<256, kStages, SPLIT3, HI, true>)
-                  : go(tc2_sk_kernel<256, kStages, SPLIT3, HI, false>);
+  return L.layout ? go(tc2_sk_kernel<BN, kStages, SPLIT3, HI, true>)
+                  : go(tc2_sk_kernel<BN, kStages, SPLIT3, HI, false>);
 }
 
 // Persistent TF32 pair kernel: `pairs` pairs share out the 256 x 256 tiles of all batches.
@@ -1121,7 +1145,7 @@ int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, vo
   } else {
     CUtensorMap ma, mb;
     const int bk = p.bk;
-    rc = encode_maps(A, B, M, N, K, lda, ldb, sa, na, sb, nbb, bk, L.layout, p.pair ? 128 : p.bn, &ma, &mb, p.bm);
+    rc = encode_maps(A, B, M, N, K, lda, ldb, sa, na, sb, nbb, bk, L.layout, p.pair ? p.bn / 2 : p.bn, &ma, &mb, p.bm);
     if (rc) return rc;
     if (p.sk) {
       Tc2StreamK sk{};
@@ -1130,16 +1154,24 @@ int run_chunk(const DeviceInfo& d, const Problem& q, const tilec_mm_cfg* cfg, vo
       sk.dp_tiles = p.sk_dp_tiles;
       sk.tiles = p.sk_tiles;
       sk.tiles_per_batch = p.sk_tiles_per_batch;
-      rc = p.variant == TILEC_MM_TF32     ? launch_tc2_sk<false, false>(ma, mb, M, N, K, L, sk, p.sk_pairs, s)
-           : p.variant == TILEC_MM_3XTF32 ? launch_tc2_sk<true, false>(ma, mb, M, N, K, L, sk, p.sk_pairs, s)
-                                          : launch_tc2_sk<true, true>(ma, mb, M, N, K, L, sk, p.sk_pairs, s);
+      if (p.bn == 128)
+        rc = p.variant == TILEC_MM_TF32     ? launch_tc2_sk<128, false, false>(ma, mb, M, N, K, L, sk, p.sk_pairs, s)
+             : p.variant == TILEC_MM_3XTF32 ? launch_tc2_sk<128, true, false>(ma, mb, M, N, K, L, sk, p.sk_pairs, s)
+                                            : launch_tc2_sk<128, true, true>(ma, mb, M, N, K, L, sk, p.sk_pairs, s);
+      else
+        rc = p.variant == TILEC_MM_TF32     ? launch_tc2_sk<256, false, false>(ma, mb, M, N, K, L, sk, p.sk_pairs, s)
+             : p.variant == TILEC_MM_3XTF32 ? launch_tc2_sk<256, true, false>(ma, mb, M, N, K, L, sk, p.sk_pairs, s)
+                                            : launch_tc2_sk<256, true, true>(ma, mb, M, N, K, L, sk, p.sk_pairs, s);
     } else if (p.persist) {
       rc = launch_tc2p(ma, mb, M, N, K, L, p.persist_pairs, s);
     } else if (p.pair)
-      rc = p.variant == TILEC_MM_TF32      ? launch_tc2<false, false>(ma, mb, M, N, K, L, s)
-           : p.variant == TILEC_MM_3XTF32  ? launch_tc2<true, false>(ma, mb, M, N, K, L, s)
-           : p.variant == TILEC_MM_3XMIXED ? launch_tc2<true, false, true>(ma, mb, M, N, K, L, s)
-                                           : launch_tc2<true, true>(ma, mb, M, N, K, L, s);
+      rc = p.bn == 128 ? (p.variant == TILEC_MM_TF32     ? launch_tc2<128, false, false>(ma, mb, M, N, K, L, s)
+                          : p.variant == TILEC_MM_3XTF32 ? launch_tc2<128, true, false>(ma, mb, M, N, K, L, s)
+                                                         : launch_tc2<128, true, true>(ma, mb, M, N, K, L, s))
+           : p.variant == TILEC_MM_TF32      ? launch_tc2<256, false, false>(ma, mb, M, N, K, L, s)
+           : p.variant == TILEC_MM_3XTF32  ? launch_tc2<256, true, false>(ma, mb, M, N, K, L, s)
+           : p.variant == TILEC_MM_3XMIXED ? launch_tc2<256, true, false, true>(ma, mb, M, N, K, L, s)
+                                           : launch_tc2<256, true, true>(ma, mb, M, N, K, L, s);
     else if (p.variant == TILEC_MM_TF32)
       rc = dispatch_tc_bn<false, false>(p.bm, p.bn, ma, mb, M, N, K, L, s);
     else if (p.variant == TILEC_MM_3XTF32)
