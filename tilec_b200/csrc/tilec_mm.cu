@@ -93,8 +93,9 @@ constexpr int kTcBM64 = 64;
 
 
 
-// CTA-pair kernels (tc2_gemm_kernel, tc2_sk_kernel): 256 x 256 tiles, used for
-// M >= kPairMinM and N > 128 (B200: 245 vs 210 TFLOP/s for the 1-CTA kernel at 8192^3).
+// CTA-pair kernels (tc2_gemm_kernel, tc2_sk_kernel): 256 x 256 tiles (256 x 128 for
+// 256 < N <= 384), used for M >= kPairMinM and N > 128 (B200: 245 vs 210 TFLOP/s for the
+// 1-CTA kernel at 8192^3).
 // TF32: 6 stages of 32 KB (4 were measured slower).
 constexpr int kPairStages = 6;
 // 3XTF32 (both forms) and the mixed split: 3 stages of K = 32 (64 KB each), the same depth
