@@ -47,6 +47,8 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--variant", default="auto")
     p.add_argument("--panels", type=int, default=2)
+    p.add_argument("--taper", action="store_true",
+                   help="column panels growing twofold (first panel short) instead of equal widths")
     p.add_argument("--e2e-chunks", type=int, default=16)
     p.add_argument("--nccl-priority", default="high", choices=["high", "normal"],
                    help="priority of NCCL's streams (high: a broadcast's kernel is placed ahead of the GEMM's "
@@ -483,8 +485,9 @@ def main():
     out = torch.empty(rows, N5, device=dev)
     if args.variant != "auto":
         os.environ["TILEC_MM_VARIANT"] = args.variant
-    op = RowShardedMatmul(K5, N5, panels=args.panels, device=dev)
-    panel_w = op.bounds[0][1] - op.bounds[0][0]
+    op = RowShardedMatmul(K5, N5, panels=args.panels, device=dev, taper=args.taper)
+    panel_ws = [n1 - n0 for n0, n1 in op.bounds]
+    panel_w = panel_ws[0]
     variant, split = ext.kernel_plan(x1, x2 if world == 1 else torch.empty(K5, panel_w, device=dev))
 
     gemm_events = []
@@ -527,10 +530,11 @@ def main():
 
     ms_total = t_start.elapsed_time(t_end)
     gemm_ms = [s.elapsed_time(e) for s, e in gemm_events]
-    t = torch.tensor([ms_total, statistics.mean(gemm_ms)], device=dev, dtype=torch.float64)
+    t = torch.tensor([ms_total, sum(gemm_ms) / args.steps], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total, gemm_ms_max = t.tolist()
+    ms_total, gemm_ms_step = t.tolist()
+    gemm_ms_max = gemm_ms_step / len(op.bounds)  # mean per panel launch
     ms_step = ms_total / args.steps
     flops_step = 2.0 * M5 * N5 * K5
     value = flops_step * args.steps / (ms_total * 1e-3) / 1e12
@@ -542,12 +546,13 @@ def main():
     # under the same cap, so the fraction against it can exceed 1.
     peak, peak_note = variant_peak(variant, pk, sustained=False)
     peak_sus, _ = variant_peak(variant, pk, sustained=True)
-    flops_launch = 2.0 * rows * panel_w * K5
-    bytes_launch = 4.0 * (rows * K5 + K5 * panel_w + rows * panel_w)
+    # Per launch: the mean over this rank's panel GEMMs (one launch per panel per step).
+    flops_launch = 2.0 * rows * N5 * K5 / len(op.bounds)
+    bytes_launch = 4.0 * (rows * K5 + (K5 * N5 + rows * N5) / len(op.bounds))
     achieved = flops_launch / (gemm_ms_max * 1e-3) / 1e12
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tpath):
+    if os.path.exists(tpath) and len(set(panel_ws)) == 1:
         with open(tpath) as f:
             tr = json.load(f)
         key = f"{variant}:{rows}x{K5}x{panel_w}"
@@ -661,7 +666,8 @@ def main():
              if variant == "3xmixed" else ("tf32" if variant == "tf32" else "f32")),
             "data": "synthetic",
             "config": {"workload": f"config5 row-sharded GEMM [{M5},{K5}] @ [{K5},{N5}] fp32, x2 broadcast "
-                                   f"from rank 0 in {len(op.bounds)} column panel(s)",
+                                   f"from rank 0 in {len(op.bounds)} column panel(s)"
+                                   + (f" of widths {panel_ws}" if len(op.bounds) > 1 else ""),
                        "M": M5, "K": K5, "N": N5, "rows_per_rank": rows, "variant": variant, "split_k": split,
                        "parallelism": f"row-shard x{world}" + (f" + NCCL broadcast of x2 ({args.nccl_priority}-"
                                                                  "priority NCCL streams)" if world > 1 else ""),

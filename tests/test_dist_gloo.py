@@ -114,6 +114,16 @@ def test_panel_bounds():
     assert b == [(0, 384), (384, 768), (768, 1000)]
     assert all(n1 > n0 for n0, n1 in b)
     assert panel_bounds(0, 4) == []
+    # tapered: shares 1, 2, 4, ... of N, each rounded up to the alignment; contiguous cover
+    assert panel_bounds(8192, 3, taper=True) == [(0, 1280), (1280, 3584), (3584, 8192)]
+    assert panel_bounds(8192, 4, taper=True) == [(0, 768), (768, 1792), (1792, 3840), (3840, 8192)]
+    assert panel_bounds(8192, 1, taper=True) == [(0, 8192)]
+    assert panel_bounds(300, 4, taper=True) == [(0, 256), (256, 300)]
+    for n in (1, 255, 777, 1000, 4097, 8192):
+        for p in (2, 3, 5):
+            b = panel_bounds(n, p, taper=True)
+            assert b[0][0] == 0 and b[-1][1] == n and all(x[1] == y[0] for x, y in zip(b, b[1:]))
+            assert all(n1 > n0 for n0, n1 in b) and all((n1 - n0) % 256 == 0 for n0, n1 in b[:-1])
 
 
 def test_rowsharded_broadcast_and_gather_gloo():

@@ -23,7 +23,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q, M, K, N, panels):
+def _worker(rank, world, port, q, M, K, N, panels, taper=False):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         import torch.distributed as dist
@@ -36,7 +36,7 @@ def _worker(rank, world, port, q, M, K, N, panels):
         x1_full = torch.randn(M, K, device=dev, generator=g)   # same on every rank (same seed)
         x2_full = torch.randn(K, N, device=dev, generator=g) / K ** 0.5
         r0, r1 = shard_rows(M, world, rank)
-        op = RowShardedMatmul(K, N, panels=panels, device=dev)
+        op = RowShardedMatmul(K, N, panels=panels, device=dev, taper=taper)
         x2 = x2_full if rank == 0 else None
         c_full = op(x1_full[r0:r1].contiguous(), x2, gather=True, M=M)
         torch.cuda.synchronize()
@@ -75,13 +75,14 @@ def _worker(rank, world, port, q, M, K, N, panels):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("M,K,N,panels", [(8192, 2048, 4096, 2), (1001, 512, 777, 3), (65536 // 8, 8192, 8192, 2)])
-def test_rowsharded_two_gpus(M, K, N, panels):
+@pytest.mark.parametrize("M,K,N,panels,taper", [(8192, 2048, 4096, 2, False), (1001, 512, 777, 3, False),
+                                               (65536 // 8, 8192, 8192, 2, False), (8192, 2048, 8192, 3, True)])
+def test_rowsharded_two_gpus(M, K, N, panels, taper):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, M, K, N, panels)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, M, K, N, panels, taper)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}

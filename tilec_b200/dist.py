@@ -71,12 +71,25 @@ def shard_rows(M, world, rank):
     return start, start + base + (1 if rank < extra else 0)
 
 
-def panel_bounds(N, panels, align=256):
+def panel_bounds(N, panels, align=256, taper=False):
     """Split [0, N) into <= panels contiguous column ranges, widths multiples of `align`
-    except the last (tile-aligned panels keep the GEMM's N tiles whole)."""
+    except the last (tile-aligned panels keep the GEMM's N tiles whole).
+
+    taper: widths grow twofold from panel to panel (shares 1, 2, 4, ... of N), so the first
+    panel, whose broadcast no GEMM can hide, is short, and each later broadcast runs under
+    the GEMM of a panel half its width."""
     if N <= 0:
         return []
     panels = max(1, int(panels))
+    if taper and panels > 1:
+        total = (1 << panels) - 1
+        out, n0 = [], 0
+        for i in range(panels):
+            n1 = N if i == panels - 1 else min(N, -(-(N * ((1 << (i + 1)) - 1) // total) // align) * align)
+            if n1 > n0:
+                out.append((n0, n1))
+                n0 = n1
+        return out
     width = -(-N // panels)
     width = -(-width // align) * align
     out = []
@@ -121,14 +134,14 @@ class RowShardedMatmul:
     Buffers for x2's panels are allocated once and reused across calls.
     """
 
-    def __init__(self, K, N, panels=2, group=None, src=0, device=None):
+    def __init__(self, K, N, panels=2, group=None, src=0, device=None, taper=False):
         self.K, self.N = int(K), int(N)
         self.group = group
         self.src = src
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-        self.bounds = panel_bounds(self.N, panels if self.world > 1 else 1)
+        self.bounds = panel_bounds(self.N, panels if self.world > 1 else 1, taper=taper)
         self.bufs = [torch.empty(self.K, n1 - n0, dtype=torch.float32, device=self.device)
                      for (n0, n1) in self.bounds] if self.world > 1 else []
         self.gemm_launches_per_call = len(self.bounds)
