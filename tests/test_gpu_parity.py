@@ -122,6 +122,32 @@ def test_config4_sweep(shape):
         _sampled_check(x1, x2, got, TOL[v])
 
 
+@pytest.mark.parametrize("variant", ("auto", "tf32", "simt"))
+def test_operands_past_2_31_elements(variant):
+    """int64 indexing: an A and a C of more than 2^31 elements (the reference indexes in
+    int32, tilec/jit.py:37).  Rows on both sides of element 2^31 are checked against fp64."""
+    tol = TOL[variant]
+    g = torch.Generator(device=DEV).manual_seed(31)
+    # A: 263,000 x 8192 = 2.15e9 elements (row 262,144 starts at element 2^31).
+    a = torch.randn(263000, 8192, device=DEV, generator=g)
+    b = torch.randn(8192, 64, device=DEV, generator=g) / 8192 ** 0.5
+    c = ext._matrix_mul(a, b, variant=None if variant == "auto" else variant)
+    rows = torch.tensor([0, 262143, 262144, 262145, 262999], device=DEV)
+    ref = a[rows].double() @ b.double()
+    assert ((c[rows].double() - ref).norm() / ref.norm()).item() <= tol
+    del a, b, c
+    # C: 36,000 x 60,000 = 2.16e9 elements (row 35,792 starts past element 2^31).
+    a = torch.randn(36000, 64, device=DEV, generator=g)
+    b = torch.randn(64, 60000, device=DEV, generator=g) / 8
+    c = ext._matrix_mul(a, b, variant=None if variant == "auto" else variant)
+    rows = torch.tensor([0, 35791, 35792, 35999], device=DEV)
+    ref = a[rows].double() @ b.double()
+    assert ((c[rows].double() - ref).norm() / ref.norm()).item() <= tol
+    del a, b, c
+    torch.cuda.empty_cache()
+    assert _status_clean()
+
+
 def test_config5_single_gpu():
     m, k, n = 65536, 8192, 8192
     g = torch.Generator(device=DEV).manual_seed(5)
