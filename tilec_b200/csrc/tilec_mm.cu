@@ -353,11 +353,17 @@ void choose_auto(const DeviceInfo& d, const float* A, const float* B, int64_t M,
   *split = 0;
   const double flops = 2.0 * double(M) * double(N) * double(K) * double(batch);
   const bool aligned = tensor_path_ok(A, B, M, N, K, lda, ldb);
-  // Thresholds from a 64-shape B200 sweep (log-uniform over [1, 8192]^3): below about
-  // 1e7 FLOPs every variant sits at the launch floor; misaligned operands are packed
-  // first, which pays from about 3e7.  Smaller products go to the SIMT kernel, split
-  // over K when their tiles leave SMs idle (the split rule picks 1 when it would not pay).
-  if (tensor_dims_ok(M, N, K) && flops >= (aligned ? 1.0e7 : 3.0e7)) {
+  // Thresholds from B200 timings of small products, eager (back-to-back calls through the
+  // Python binding) and in CUDA graphs: from about 1e5 FLOPs the tcgen05 kernel, whose
+  // set-up overlaps the previous kernel (programmatic launch), beats the SIMT kernel
+  // (64^3: 8.0 / 4.3 us against 8.9 / 6.4; 100^3: 8.2 / 7.8 against 16.4 / 15.0; 32 x 2048
+  // x 32: 10.7 / 6.3 against 11.6 / 8.4).  Misaligned operands are packed first, one more
+  // launch, which pays from about 2e5 FLOPs when K >= 64 (5 x 306 x 169: 12.5 / 9.9
+  // against 14.3 / 12.2); with a smaller K the product is mostly the store of C and the
+  // SIMT kernel does it in one launch (2780 x 2 x 235: 8.8 against 11.3 us eager).  Smaller
+  // products (1 x 4096 x 1, 445 x 4 x 1, 2 x 283 x 13) go to the SIMT kernel, split over K
+  // when their tiles leave SMs idle (the split rule picks 1 when it would not pay).
+  if (tensor_dims_ok(M, N, K) && (aligned ? flops >= 1.0e5 : (flops >= 2.0e5 && K >= 64))) {
     *variant = TILEC_MM_3XTF32;
     return;
   }

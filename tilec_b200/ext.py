@@ -33,13 +33,36 @@ _ENV_VARIANT = "TILEC_MM_VARIANT"
 _ENV_CHECK = "TILEC_MM_CHECK"
 
 
+# Per-call host cost matters for small products, so the hot path reads the environment
+# through the bytes-keyed dict behind os.environ on POSIX (os.environ.get re-encodes the
+# key and decodes the value on every call: ~0.5 us against ~0.05 us) and takes the current
+# stream as a raw handle (torch.cuda.current_stream() builds a Stream object: ~2 us).
+_ENV_DATA = getattr(os.environ, "_data", None) if os.name == "posix" else None
+_ENV_VARIANT_B = _ENV_VARIANT.encode()
+_ENV_CHECK_B = _ENV_CHECK.encode()
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _default_variant():
+    if _ENV_DATA is not None:
+        v = _ENV_DATA.get(_ENV_VARIANT_B)
+        return "auto" if v is None else v.decode()
     return os.environ.get(_ENV_VARIANT, "auto")
 
 
 def _check_enabled():
     """TILEC_MM_CHECK=1: every call synchronises its stream and raises on a device fault."""
+    if _ENV_DATA is not None:
+        v = _ENV_DATA.get(_ENV_CHECK_B)
+        return v is not None and v not in (b"", b"0")
     return os.environ.get(_ENV_CHECK, "0") not in ("", "0")
+
+
+def _current_stream(index):
+    """Raw handle of the current stream of CUDA device `index`."""
+    if _raw_stream is not None:
+        return _raw_stream(index)
+    return torch.cuda.current_stream(index).cuda_stream
 
 
 def _check_operand(x):
@@ -55,24 +78,28 @@ def _operand(x):
     kernels read it in place (TILEC_MM_TRANS_A / _B).  The reference makes both
     contiguous (tilec/ext.py:59-60); anything else is still copied here."""
     r, c = x.shape
-    if (c <= 1 or x.stride(1) == 1) and (r <= 1 or x.stride(0) >= max(c, 1)):
-        return x, (x.stride(0) if r > 1 else max(c, 1)), False
-    if x.stride(0) == 1 and x.stride(1) >= r:
-        return x, x.stride(1), True
+    s0, s1 = x.stride()
+    if (c <= 1 or s1 == 1) and (r <= 1 or s0 >= max(c, 1)):
+        return x, (s0 if r > 1 else max(c, 1)), False
+    if s0 == 1 and s1 >= r:
+        return x, s1, True
     x = x.contiguous()
     return x, max(c, 1), False
 
 
 def _check_out(out, M, N, device):
+    """`device`: a torch.device or a CUDA device index."""
     if out.dtype != torch.float32:
         raise TypeError(f"matrix_mul: out must be float32, got {out.dtype}")
-    if out.device != device:
-        raise ValueError(f"matrix_mul: out is on {out.device}, inputs on {device}")
-    if tuple(out.shape) != (M, N):
+    index = device if isinstance(device, int) else device.index
+    if not out.is_cuda or out.get_device() != index:
+        raise ValueError(f"matrix_mul: out is on {out.device}, inputs on cuda:{index}")
+    if out.shape != (M, N):
         raise ValueError(f"matrix_mul: out has shape {tuple(out.shape)}, expected {(M, N)}")
-    if not ((N <= 1 or out.stride(1) == 1) and (M <= 1 or out.stride(0) >= max(N, 1))):
+    s0, s1 = out.stride()
+    if not ((N <= 1 or s1 == 1) and (M <= 1 or s0 >= max(N, 1))):
         raise ValueError("matrix_mul: out must have unit column stride and non-overlapping rows")
-    return out.stride(0) if M > 1 else max(N, 1)
+    return s0 if M > 1 else max(N, 1)
 
 
 _WS_BYTES = {}   # (shape, strides, 16-byte alignment of A/B/C, variant, split) -> workspace bytes
@@ -100,22 +127,21 @@ def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k, flags=0):
         _installed = True
     cfg = _native.make_cfg(variant, split_k, flags)
     pa, pb, pc = a.data_ptr(), b.data_ptr(), out.data_ptr()
-    dev = out.device
-    switch = torch.cuda.current_device() != dev.index
+    index = out.get_device()
     prev = torch.cuda.current_device()
+    switch = prev != index
     if switch:
-        torch.cuda.set_device(dev)
+        torch.cuda.set_device(index)
     try:
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        key = (M, N, K, lda, ldb, ldc, pa & 15 == 0, pb & 15 == 0, pc & 15 == 0, cfg.variant, cfg.split_k, flags,
-               dev.index)
+        stream = _current_stream(index)
+        key = (M, N, K, lda, ldb, ldc, (pa | pb << 4 | pc << 8) & 0xF0F0F, cfg.variant, cfg.split_k, flags, index)
         ws_bytes = _WS_BYTES.get(key)
         if ws_bytes is None:
             ws_bytes = lib.tilec_mm_workspace_bytes(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg))
             if len(_WS_BYTES) >= _WS_BYTES_MAX:  # a process that sees many shapes: start over
                 _WS_BYTES.clear()
             _WS_BYTES[key] = ws_bytes
-        ws_ptr = _workspace(dev, stream, ws_bytes).data_ptr() if ws_bytes else None
+        ws_ptr = _workspace(out.device, stream, ws_bytes).data_ptr() if ws_bytes else None
         rc = lib.tilec_mm_f32(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg), ws_ptr, ws_bytes, stream)
         _native.check(rc, "tilec_mm_f32")
         if _check_enabled():
@@ -155,10 +181,11 @@ def _matrix_mul(x1, x2, variant=None, split_k=0, out=None, stream_k=False, tile_
         raise ValueError(f"matrix_mul: shapes {tuple(x1.shape)} and {tuple(x2.shape)} don't match")
     _check_operand(x1)
     _check_operand(x2)
-    if x1.device.type != "cuda" or x2.device.type != "cuda":
+    if not (x1.is_cuda and x2.is_cuda):
         raise ValueError(f"matrix_mul: inputs must be CUDA tensors (got {x1.device} and {x2.device}); "
                          "tilec_b200 has no CPU path")
-    if x1.device != x2.device:
+    index = x1.get_device()
+    if x2.get_device() != index:
         raise ValueError(f"matrix_mul: inputs on different devices ({x1.device}, {x2.device})")
     a, lda, ta = _operand(x1)
     b, ldb, tb = _operand(x2)
@@ -166,11 +193,11 @@ def _matrix_mul(x1, x2, variant=None, split_k=0, out=None, stream_k=False, tile_
         out = x1.new_empty(M, N)
         ldc = max(N, 1)
     else:
-        ldc = _check_out(out, M, N, x1.device)
+        ldc = _check_out(out, M, N, index)
     if M == 0 or N == 0:
         return out
     flags = ((_native.TRANS_A if ta else 0) | (_native.TRANS_B if tb else 0) | (_native.STREAM_K if stream_k else 0)
-             | _tile_flags(tile_m))
+             | (_tile_flags(tile_m) if tile_m is not None else 0))
     return _launch(a, lda, b, ldb, out, ldc, M, N, K, variant or _default_variant(), split_k, flags)
 
 
@@ -324,7 +351,7 @@ def matrix_mul_ex(x1, x2, bias=None, activation=None, out=None, variant=None, sp
     pa, pb, pc = a.data_ptr(), b.data_ptr(), out.data_ptr()
     dev = out.device
     with torch.cuda.device(dev):
-        stream = torch.cuda.current_stream(dev).cuda_stream
+        stream = _current_stream(dev.index)
         ws_bytes = lib.tilec_mm_workspace_bytes_ex(pa, pb, pc, M, N, K, lda, ldb, ldc, nbatch, sa, sb, sc,
                                                    ctypes.byref(cfg))
         ws_ptr = _workspace(dev, stream, ws_bytes).data_ptr() if ws_bytes else None
