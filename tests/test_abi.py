@@ -112,3 +112,25 @@ def test_wait_limit_rejects_negative_before_device():
     assert lib.tilec_mm_set_wait_limit(-1, None) == 1  # TILEC_ERR_BAD_ARG
     assert _native.status_bits(0) == "clean"
     assert _native.status_bits(1) == "TIMEOUT" and _native.status_bits(5) == "TIMEOUT|BAD_LAUNCH"
+
+
+def test_fast_call_module_matches_ctypes():
+    """The CPython fast-call module (csrc/fastcall.c) builds, is installed with the loaded
+    library's entry points, and returns exactly what the ctypes calls return (argument
+    errors caught before any device work; a size query with no device)."""
+    build.build_fast()
+    lib = _native.load()
+    fast = _native.fast()
+    assert fast is not None, _native.fast_error()
+    cfg = _native.make_cfg("auto", 0, 0)
+    cases = [(0, 0, 0, -1, 4, 4, 4, 4, 4), (0, 0, 0, 4, 4, 4, 2, 4, 4), (16, 32, 48, 4, 4, 4, 4, 4, 4),
+             (16, 32, 48, 4, 4, 4, 4, 4, 2)]
+    for args in cases:
+        assert fast.mm(*args, cfg.variant, cfg.split_k, cfg.flags, None, 0, None) == \
+            lib.tilec_mm_f32(*args, ctypes.byref(cfg), None, 0, None), args
+        assert fast.ws_bytes(*args, cfg.variant, cfg.split_k, cfg.flags) == \
+            lib.tilec_mm_workspace_bytes(*args, ctypes.byref(cfg)), args
+    with pytest.raises(TypeError):
+        fast.mm(0, 0, 0)
+    with pytest.raises(ValueError):
+        fast.mm(*cases[0], 0, 0, 0, None, -1, None)

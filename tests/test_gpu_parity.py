@@ -770,6 +770,47 @@ def test_stream_k_batched_fused(act):
     assert _status_clean()
 
 
+def test_host_threads_on_separate_streams():
+    """The library is stream-ordered and reentrant: four host threads, each on a stream of
+    its own, call split-K, CTA-pair, packed (misaligned) and SIMT products at the same
+    time; every result equals the same product run alone, bit for bit, and each thread's
+    workspace (per stream) keeps its split-K slabs apart from the others'."""
+    import threading
+    g = torch.Generator(device=DEV).manual_seed(29)
+    cases = [((512, 4096, 64), "3xtf32"), ((2048, 1024, 2048), "3xtf32"), ((1000, 3001, 777), "auto"),
+             ((300, 700, 500), "splitk")]
+    ins = [(torch.randn(m, k, device=DEV, generator=g), torch.randn(k, n, device=DEV, generator=g), v)
+           for (m, k, n), v in cases]
+    alone = [ext._matrix_mul(a, b, variant=v) for a, b, v in ins]
+    torch.cuda.synchronize()
+    results = [[] for _ in ins]
+    errors = []
+
+    def work(i):
+        try:
+            a, b, v = ins[i]
+            s = torch.cuda.Stream(device=DEV)
+            with torch.cuda.stream(s):
+                for _ in range(8):
+                    results[i].append(ext._matrix_mul(a, b, variant=v))
+            s.synchronize()
+        except Exception as e:  # noqa: BLE001
+            errors.append(repr(e))
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(len(ins))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    torch.cuda.synchronize()
+    assert not errors, errors
+    for r, outs in zip(alone, results):
+        assert len(outs) == 8
+        for o in outs:
+            assert torch.equal(o, r)
+    assert _status_clean()
+
+
 def test_stream_k_concurrent_streams():
     """Two streams run stream-K products at the same time, so the pairs of one launch
     compete for SMs with the other's: a pair waits only on lower-numbered pairs, which the

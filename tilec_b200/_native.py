@@ -68,6 +68,8 @@ class TilecError(RuntimeError):
 
 
 _lib = None
+_fast = None     # the CPython fast-call module, once loaded and installed
+_fast_error = None
 _lock = threading.Lock()
 
 
@@ -119,8 +121,45 @@ def load():
         lib.tilec_mm_workspace_bytes_ex.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, i64, i64,
                                                     cfgp]
         lib.tilec_mm_workspace_bytes_ex.restype = sz
+        _load_fast(lib)
         _lib = lib
         return _lib
+
+
+def _load_fast(lib):
+    """Load _tilec_fast (csrc/fastcall.c; rebuilt first when stale and gcc exists) and give
+    it the addresses of this library's tilec_mm_f32 and tilec_mm_workspace_bytes.  When it
+    cannot be had, the binding makes the same calls through ctypes (`fast_error()` says
+    why); the kernels that run are the same either way."""
+    global _fast, _fast_error
+    try:
+        import importlib.util
+        if not _build.fast_up_to_date():
+            try:
+                _build.build_fast()
+            except Exception:  # noqa: BLE001  (no compiler here: use the module if one exists)
+                if not os.path.exists(_build.FAST):
+                    raise
+        spec = importlib.util.spec_from_file_location("_tilec_fast", _build.FAST)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        mod.install(ctypes.cast(lib.tilec_mm_f32, ctypes.c_void_p).value,
+                    ctypes.cast(lib.tilec_mm_workspace_bytes, ctypes.c_void_p).value)
+        _fast = mod
+    except Exception as e:  # noqa: BLE001
+        _fast, _fast_error = None, f"{type(e).__name__}: {e}"
+
+
+def fast():
+    """The fast-call module, or None when the binding uses ctypes for every call."""
+    if _lib is None:
+        load()
+    return _fast
+
+
+def fast_error():
+    """Why the fast-call module is not in use (None when it is)."""
+    return _fast_error
 
 
 def strerror(code):

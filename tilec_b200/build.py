@@ -2,12 +2,15 @@
 
 nvcc cross-compiles for sm_100a without a GPU, so this runs on CPU-only hosts too.
 The library is one translation unit (csrc/tilec_mm.cu) exporting the C ABI declared in
-include/tilec_mm.h.  Usage: ``python -m tilec_b200.build [--force]``.
+include/tilec_mm.h.  Beside it, gcc builds the small CPython module _tilec_fast
+(csrc/fastcall.c) through which the Python binding makes its per-call C ABI calls.
+Usage: ``python -m tilec_b200.build [--force]``.
 """
 import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
@@ -15,6 +18,8 @@ CSRC = os.path.join(PKG, "csrc")
 LIB_DIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(LIB_DIR, "libtilec_mm.so")
 HEADER = os.path.join(ROOT, "include", "tilec_mm.h")
+FAST_SRC = os.path.join(CSRC, "fastcall.c")
+FAST = os.path.join(LIB_DIR, "_tilec_fast" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -61,6 +66,31 @@ def build(force=False, verbose=False):
     return LIB
 
 
+def fast_up_to_date():
+    if not os.path.exists(FAST):
+        return False
+    t = os.path.getmtime(FAST)
+    return all(os.path.getmtime(s) <= t for s in (FAST_SRC, HEADER))
+
+
+def build_fast(force=False):
+    """Compile csrc/fastcall.c into _lib/_tilec_fast (skipped when fresh)."""
+    if not force and fast_up_to_date():
+        return FAST
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        raise RuntimeError("no C compiler: the CPython fast-call module cannot be built")
+    os.makedirs(LIB_DIR, exist_ok=True)
+    tmp = FAST + ".tmp"
+    cmd = [cc, "-O2", "-shared", "-fPIC", "-std=c11", "-Wall", "-Werror",
+           "-I", sysconfig.get_paths()["include"], "-o", tmp, FAST_SRC]
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, FAST)
+    return FAST
+
+
 if __name__ == "__main__":
     build(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    build_fast(force="--force" in sys.argv)
     print(LIB)
+    print(FAST)

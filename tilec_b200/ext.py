@@ -106,6 +106,7 @@ _WS_BYTES = {}   # (shape, strides, 16-byte alignment of A/B/C, variant, split) 
 _WS_BYTES_MAX = 4096
 _WS = {}         # (device index, stream handle) -> grow-only workspace tensor
 _installed = False
+_fast = None     # _native.fast(), fetched on the first launch
 
 
 def _workspace(dev, stream, nbytes):
@@ -119,11 +120,12 @@ def _workspace(dev, stream, nbytes):
 
 
 def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k, flags=0):
-    global _installed
+    global _installed, _fast
     lib = _native.load()
     if not _installed:
         from . import select  # installs the B200 selection table on first use
         select.ensure_installed()
+        _fast = _native.fast()
         _installed = True
     cfg = _native.make_cfg(variant, split_k, flags)
     pa, pb, pc = a.data_ptr(), b.data_ptr(), out.data_ptr()
@@ -142,7 +144,11 @@ def _launch(a, lda, b, ldb, out, ldc, M, N, K, variant, split_k, flags=0):
                 _WS_BYTES.clear()
             _WS_BYTES[key] = ws_bytes
         ws_ptr = _workspace(out.device, stream, ws_bytes).data_ptr() if ws_bytes else None
-        rc = lib.tilec_mm_f32(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg), ws_ptr, ws_bytes, stream)
+        if _fast is not None:  # the same C ABI call without ctypes' argument conversion
+            rc = _fast.mm(pa, pb, pc, M, N, K, lda, ldb, ldc, cfg.variant, cfg.split_k, cfg.flags, ws_ptr, ws_bytes,
+                          stream)
+        else:
+            rc = lib.tilec_mm_f32(pa, pb, pc, M, N, K, lda, ldb, ldc, ctypes.byref(cfg), ws_ptr, ws_bytes, stream)
         _native.check(rc, "tilec_mm_f32")
         if _check_enabled():
             check_device(stream)
