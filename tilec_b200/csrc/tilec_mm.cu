@@ -664,6 +664,19 @@ bool pdl_enabled() {
   return on;
 }
 
+// Raster band height (pair-rows) of the one-pair-per-tile kernel: 8 unless TILEC_MM_PAIR_BAND
+// (1..64, read once) says otherwise.  8 reads least from DRAM on B200 (16384x8192x8192: 4 /
+// 8 / 16 pair-rows read 5.84 / 4.65 / 5.32 GB, same speed within 1.2 %); the variable exists
+// to reproduce that measurement.
+int pair_band() {
+  static const int band = [] {
+    const char* e = std::getenv("TILEC_MM_PAIR_BAND");
+    const int v = e ? std::atoi(e) : 0;
+    return v >= 1 && v <= 64 ? v : 8;
+  }();
+  return band;
+}
+
 // Launches `kern`, with programmatic stream serialisation when `pdl` (every kernel here
 // calls pdl_wait() before touching global memory) and, when cluster_x > 1, a cluster of
 // cluster_x CTAs along x.
@@ -755,7 +768,7 @@ int launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, int64_t M, int64_t 
   using Cfg = Tc2Cfg<BN, kStages, SPLIT3, false, kTc2Bk<SPLIT3, MIXED>>;
   const int mp_tiles = static_cast<int>(cdiv(M, 256));
   const int n_tiles = static_cast<int>(cdiv(N, BN));
-  const int group_m = 8;
+  const int group_m = pair_band();
   const dim3 grid(static_cast<unsigned>(2 * int64_t(mp_tiles) * n_tiles), static_cast<unsigned>(L.batch),
                   static_cast<unsigned>(L.split));
   auto go = [&](auto kern) {

@@ -287,8 +287,9 @@ def pick(M, K, N):
 
 
 def run(shape, variant="auto", split=0, reps=3, seed=0, stream_k=False, batch=0, tile_m=None):
-    """`reps` launches of one product (for profilers); prints the plan that ran.  batch > 0:
-    one matrix_mul_ex call over `batch` products of the shape per launch."""
+    """One warm-up call, then `reps` back-to-back calls of one product timed with CUDA
+    events (for profilers and A/B runs); prints the plan that ran and the mean time per call.
+    batch > 0: one matrix_mul_ex call over `batch` products of the shape per launch."""
     import torch
     from . import ext
     m, k, n = shape
@@ -297,15 +298,26 @@ def run(shape, variant="auto", split=0, reps=3, seed=0, stream_k=False, batch=0,
     a = torch.randn(*lead, m, k, device="cuda", generator=g)
     b = torch.randn(*lead, k, n, device="cuda", generator=g)
     c = torch.empty(*lead, m, n, device="cuda")
-    for _ in range(reps):
+
+    def call():
         if batch > 0:
             ext.matrix_mul_ex(a, b, out=c, variant=variant, split_k=split, stream_k=stream_k, tile_m=tile_m)
         else:
             ext._matrix_mul(a, b, variant=variant, split_k=split, out=c, stream_k=stream_k, tile_m=tile_m)
+    call()
     torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        call()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / max(reps, 1)
     a0, b0 = (a[0], b[0]) if batch > 0 else (a, b)
     plan = ext.kernel_plan(a0, b0, variant=variant, split_k=split, stream_k=stream_k, detail=True, tile_m=tile_m)
-    print(json.dumps({"shape": [m, k, n], "batch": batch, "plan": plan, "reps": reps}))
+    flops = 2.0 * m * n * k * max(batch, 1)
+    print(json.dumps({"shape": [m, k, n], "batch": batch, "plan": plan, "reps": reps, "ms_per_call": round(ms, 4),
+                      "tflops": round(flops / ms / 1e9, 2)}))
 
 
 def main(argv=None):
