@@ -102,8 +102,12 @@ static PyObject* py_mm(PyObject* self, PyObject* const* args, Py_ssize_t nargs) 
     PyErr_SetString(PyExc_ValueError, "mm: negative workspace size");
     return NULL;
   }
-  const int rc = g_mm((const float*)p[0], (const float*)p[1], (float*)p[2], d[0], d[1], d[2], d[3], d[4], d[5],
-                     &cfg, ws, (size_t)ws_bytes, stream);
+  int rc;
+  /* The GIL is released around the launch, as ctypes does, so other host threads run. */
+  Py_BEGIN_ALLOW_THREADS
+  rc = g_mm((const float*)p[0], (const float*)p[1], (float*)p[2], d[0], d[1], d[2], d[3], d[4], d[5], &cfg, ws,
+            (size_t)ws_bytes, stream);
+  Py_END_ALLOW_THREADS
   return PyLong_FromLong(rc);
 }
 
