@@ -845,7 +845,8 @@ struct PackJob {
 // loads and stores throughout.  An aligned float4 never crosses a page, so reading one that
 // holds at least one element of the row cannot fault; the padding columns of the copy
 // (cols .. ldd) receive whatever the last chunk held and are never read by the GEMM.
-// Short rows share a block: a warp per row when cols <= 128.
+// Short rows share a block: a warp per row when cols <= 1024 (B200, 1000x3001x777 with both
+// operands packed: 47.9 -> 46.2 us, same box; taller rows are left at 256 threads per row).
 __global__ void __launch_bounds__(256) pack_rows_kernel(const PackJob j0, const PackJob j1) {
   pdl_wait();
   pdl_launch_dependents();
@@ -859,7 +860,7 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const PackJob j0, const 
   if (static_cast<int64_t>(blockIdx.y) >= (second ? j1.batches : j0.batches)) return;
   src += static_cast<int64_t>(blockIdx.y) * (second ? j1.sstride : j0.sstride);
   dst += static_cast<int64_t>(blockIdx.y) * rows * ldd;
-  const int64_t lanes = cols <= 128 ? 32 : blockDim.x;
+  const int64_t lanes = cols <= 1024 ? 32 : blockDim.x;
   const int64_t rows_per_block = blockDim.x / lanes;
   const int64_t sub = threadIdx.x / lanes, t = threadIdx.x % lanes;
   const int64_t chunks = (cols + 3) / 4;
@@ -949,7 +950,7 @@ PackJob pack_job(const float* src, int64_t lds, int64_t sstride, float* dst, int
   j.cols = cols;
   j.batches = batches;
   const int64_t cap = int64_t(d.sms) * 8 / batches + 1;
-  const int64_t per_block = cols <= 128 ? 8 : 1;  // rows per 256-thread block
+  const int64_t per_block = cols <= 1024 ? 8 : 1;  // rows per 256-thread block (warp per row up to 1024)
   j.blocks = cdiv(rows, per_block) < cap ? cdiv(rows, per_block) : cap;
   if (j.blocks < 1) j.blocks = 1;
   return j;
